@@ -1,0 +1,459 @@
+#!/usr/bin/env python
+"""Benchmark: slice+deslice coupling round, forward + backward, in Mpoints/s.
+
+A step is one coupling round over one batch of synthetic points: slice
+forward, token normalisation z_num / (s + 1e-5) (identity mix), deslice
+forward, and the backward of sum(out * r) (deslice backward, the mix's
+backward, slice backward). Workload: B=1, N=1,048,576
+points per GPU, H=8, D=DV=32, G=32, fp32, ieee dot level, per-head W (H, G, D)
+~ N(0, 1/D), b (H, G) ~ N(0, 0.02^2), tau ~ U[0.3, 1.0], x_mid, fx_mid, r
+~ N(0, 1), seeded. Inputs are larger than L2 (1 GiB each), so no L2 flush is
+needed between steps.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python -m torch.distributed.run --nproc-per-node N bench.py --gpus N ...
+
+One JSON line on rank 0. With N > 1 GPUs each rank holds its own N points
+(weak scaling); the per-rank slice partials and token gradients are summed
+across ranks in rank order (all-gather + ordered sum over NCCL) and the
+parameter gradients likewise, inside the timed step.
+
+``--impl reference`` times the reference's own CPU implementation of the
+round -- its eager op math, restated in ``oracle/eager_torch.py`` -- on the
+host cores, on a bounded sample of the workload (rank 0 only).
+"""
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "slice+deslice fwd+bwd Mpoints/s at N=1M,G=32 (1–8 GPU); % of HBM roofline"
+UNIT = "Mpoints/s"
+EPS = 1e-5
+
+CONFIGS = {
+    # configs[1] of the baseline: per-GPU shard of 2^20 points (weak scaling)
+    "cfg2": dict(B=1, N=1 << 20, H=8, D=32, DV=32, G=32, weight="hgd", tau="uniform",
+                 dtype=torch.float32, dot="ieee", split=False),
+    "cfg1": dict(B=1, N=16384, H=8, D=32, DV=32, G=32, weight="gd", tau="half",
+                 dtype=torch.float32, dot="ieee", split=False),
+    "cfg3": dict(B=2, N=262144, H=8, D=32, DV=64, G=1024, weight="bhgd", tau="half",
+                 dtype=torch.bfloat16, dot="bf16", split=False, bias=False),
+    # 2^24 points split over the ranks (strong scaling)
+    "cfg5": dict(B=1, N=1 << 24, H=8, D=32, DV=32, G=64, weight="hgd", tau="half",
+                 dtype=torch.float32, dot="ieee", split=True),
+}
+# algorithmic (B, N, H, width) tensors each op moves (bench_kernels.py:45)
+UNITS = {"slice_fwd": 2, "deslice_fwd": 2, "slice_bwd": 4, "deslice_bwd": 3}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="cfg2")
+    ap.add_argument("--n", type=int, default=None, help="override the point count")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--cpu-sample", type=int, default=131072,
+                    help="points per CPU-baseline step")
+    return ap.parse_args()
+
+
+# --------------------------------------------------------------------------- inputs
+
+def make_inputs(cfg, n, device, seed):
+    """Seeded synthetic leaves of one shard: x_mid, fx_mid, W, b, tau, r."""
+    gen = torch.Generator(device=device).manual_seed(seed)
+    B, H, D, DV, G = cfg["B"], cfg["H"], cfg["D"], cfg["DV"], cfg["G"]
+    dt = cfg["dtype"]
+    rn = lambda *s: torch.randn(*s, generator=gen, device=device)  # noqa: E731
+    x = rn(B, n, H, D).to(dt)
+    fx = rn(B, n, H, DV).to(dt)
+    r = rn(B, n, H, DV).to(dt)
+    if cfg["weight"] == "gd":
+        W, b = rn(G, D) / D ** 0.5, 0.02 * rn(G)
+    elif cfg["weight"] == "hgd":
+        W, b = rn(H, G, D) / D ** 0.5, 0.02 * rn(H, G)
+    else:  # tokens projected by a random linear map (parity_ops.Case), scaled to N(0, 1/D)
+        Ht = 64
+        Wk = rn(Ht, H * D) / (Ht * D) ** 0.5
+        W = (rn(B, G, Ht) @ Wk).view(B, G, H, D).permute(0, 2, 1, 3).contiguous()
+        b = None
+    if not cfg.get("bias", True):
+        b = None
+    if cfg["tau"] == "uniform":
+        tau = 0.3 + 0.7 * torch.rand(H, generator=gen, device=device)
+    else:
+        tau = torch.full((H,), 0.5, device=device)
+    W = W.to(dt) if dt != torch.float32 else W
+    return x, fx, W, b, tau, r
+
+
+# --------------------------------------------------------------------------- steps
+
+def coupling_step(K, x, fx, W, b, tau, r, group=None):
+    """Forward + backward of one round through the public API (autograd)."""
+    from flashslice_b200 import sharded
+    if group is None:
+        z, s = K.fused_slice(x, fx, W, b, tau)
+    else:
+        z, s = sharded.sharded_slice(x, fx, W, b, tau, group)
+    tok = z / (s + EPS)[..., None]
+    out = K.fused_deslice(x, W, b, tau, tok)
+    out.backward(r)
+    if group is not None:
+        sharded.reduce_grads([W, b, tau], group)
+    return out
+
+
+def zero_grads(*ts):
+    for t in ts:
+        if t is not None:
+            t.grad = None
+
+
+def op_timings(K, x, fx, W, b, tau, r, dot, reps=3):
+    """Per-op device time (ms) of one round, each op launched directly on the
+    current stream between CUDA events; median over reps."""
+    ops = torch.ops.flashslice
+    bb = b if b is not None else W.new_zeros(W.shape[-2])
+    Wd, bd, td = W.detach(), bb.detach(), tau.detach()
+    xd, fd = x.detach(), fx.detach()
+    times = {k: [] for k in UNITS}
+    for _ in range(reps):
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(7)]
+        ev[0].record()
+        z, s = ops.flash_slice(xd, fd, Wd, bd, td, dot)
+        ev[1].record()
+        den = (s + EPS)[..., None]
+        tok = z / den
+        ev[2].record()
+        ops.flash_deslice(xd, Wd, bd, td, tok, dot)
+        ev[3].record()
+        _, dtok, _, _, _ = ops.flash_deslice_bwd(xd, Wd, bd, td, tok, r, dot)
+        ev[4].record()
+        dz = dtok / den
+        ds = -(dtok * z).sum(-1) / (s + EPS) ** 2
+        ev[5].record()
+        ops.flash_slice_bwd(xd, fd, Wd, bd, td, dz, ds, dot)
+        ev[6].record()
+        torch.cuda.synchronize()
+        times["slice_fwd"].append(ev[0].elapsed_time(ev[1]))
+        times["deslice_fwd"].append(ev[2].elapsed_time(ev[3]))
+        times["deslice_bwd"].append(ev[3].elapsed_time(ev[4]))
+        times["slice_bwd"].append(ev[5].elapsed_time(ev[6]))
+    return {k: statistics.median(v) for k, v in times.items()}
+
+
+# --------------------------------------------------------------------------- clocks
+
+class ClockSampler:
+    """nvidia-smi samples (every 200 ms) over the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), "--query-gpu=" + self.FIELDS,
+                 "--format=csv,noheader,nounits", "-lms", "200", "-f", self.path],
+                stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, mx, reasons = [], [], set()
+        try:
+            with open(self.path) as f:
+                for line in f:
+                    parts = [p.strip() for p in line.split(",")]
+                    if len(parts) < 9:
+                        continue
+                    try:
+                        sm.append(float(parts[1]))
+                        mx.append(float(parts[2]))
+                    except ValueError:
+                        continue
+                    for name, val in zip(self.NAMES, parts[5:9]):
+                        if val.lower() == "active":
+                            reasons.add(name)
+        finally:
+            os.unlink(self.path)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx),
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# --------------------------------------------------------------------------- CPU legs
+
+def cpu_round_time(cfg, n, threads, reps, seed=0):
+    """Median seconds of one eager coupling round (the reference's op math on
+    the CPU, ``oracle/eager_torch.py``) over ``n`` points."""
+    from oracle import eager_torch as E
+    torch.set_num_threads(threads)
+    x, fx, W, b, tau, r = make_inputs(cfg, n, "cpu", seed)
+    x, fx = x.float(), fx.float()
+    W = W.float()
+    times = []
+    for i in range(reps + 1):
+        leaves = [t.detach().requires_grad_(True) if t is not None else None
+                  for t in (x, fx, W, b, tau)]
+        t0 = time.perf_counter()
+        E.coupling_round(*leaves, r.float(), eps=EPS)
+        if i:
+            times.append(time.perf_counter() - t0)
+    return statistics.median(times)
+
+
+def cpu_baseline(cfg, sample, reps=3):
+    threads = os.cpu_count() or 1
+    sec = cpu_round_time(cfg, sample, threads, reps)
+    return {"value": round(cfg["B"] * sample / sec / 1e6, 4), "unit": UNIT, "cores": threads,
+            "kind": "port",
+            "sample": "one eager coupling round (oracle/eager_torch.py, the reference's op math) "
+                      "over %d points of the same shape, median of %d" % (sample, reps)}
+
+
+def run_reference(args, cfg):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    sample = args.cpu_sample
+    from oracle import eager_torch as E
+    torch.set_num_threads(threads)
+    x, fx, W, b, tau, r = make_inputs(cfg, sample, "cpu", 0)
+    x, fx, W, r = x.float(), fx.float(), W.float(), r.float()
+
+    def step():
+        leaves = [t.detach().requires_grad_(True) if t is not None else None
+                  for t in (x, fx, W, b, tau)]
+        E.coupling_round(*leaves, r, eps=EPS)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    sec = (time.perf_counter() - t0) / args.steps
+    value = cfg["B"] * sample / sec / 1e6
+    line = {"metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(sec * 1e3, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "impl": "reference",
+            "config": {"workload": args.config + " (CPU sample)", "B": cfg["B"], "N": sample,
+                       "H": cfg["H"], "D": cfg["D"], "DV": cfg["DV"], "G": cfg["G"]},
+            "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": threads,
+                             "kind": "port",
+                             "sample": "eager coupling round over %d points per step" % sample},
+            "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------------- main
+
+def main():
+    args = parse()
+    cfg = dict(CONFIGS[args.config])
+    if args.n is not None:
+        cfg["N"] = args.n
+    if args.impl == "reference":
+        return run_reference(args, cfg)
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py: no CUDA device (the fused ops have no CPU implementation)")
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    group = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=device)
+        group = dist.group.WORLD
+    torch.backends.cuda.matmul.allow_tf32 = False
+
+    import flashslice_b200.kernels as K
+    from flashslice_b200.kernels import _native
+    lib = _native.load()
+    K.set_dot_mode(cfg["dot"])
+
+    if cfg["split"]:
+        from flashslice_b200.sharded import shard_range
+        lo, hi = shard_range(cfg["N"], rank, world)
+        n_local = hi - lo
+    else:
+        n_local = cfg["N"]
+    x, fx, W, b, tau, r = make_inputs(cfg, n_local, device, 1234 + rank)
+    # replicated parameters: identical on every rank
+    _, _, W, b, tau, _ = make_inputs(cfg, 1, device, 99)
+    leaves = [t.requires_grad_(True) for t in (x, fx, W, tau)]
+    if b is not None:
+        b.requires_grad_(True)
+
+    def step():
+        zero_grads(x, fx, W, b, tau)
+        coupling_step(K, x, fx, W, b, tau, r, group)
+
+    def barrier():
+        if group is not None:
+            import torch.distributed as dist
+            dist.barrier(group=group)
+
+    for _ in range(max(args.warmup, 1)):
+        step()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    launches0 = lib.fs_launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    launches = lib.fs_launch_count() - launches0
+    ms = e0.elapsed_time(e1) / args.steps
+    barrier()
+    clk = clocks.stop()
+    if group is not None:
+        import torch.distributed as dist
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+        ms = t.item()
+    points = cfg["B"] * (cfg["N"] if cfg["split"] else n_local * world)
+    value = points / (ms * 1e-3) / 1e6
+
+    # end to end: inputs from pinned host memory, parameter gradients back
+    e2e = None
+    if not args.no_e2e:
+        xh = x.detach().cpu().pin_memory()
+        fh = fx.detach().cpu().pin_memory()
+        res_bytes = sum(t.numel() * t.element_size() for t in (W, tau) + ((b,) if b is not None
+                                                                          else ()))
+        outs = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+                for t in (W, tau) + ((b,) if b is not None else ())]
+
+        def e2e_step():
+            with torch.no_grad():
+                x.copy_(xh, non_blocking=True)
+                fx.copy_(fh, non_blocking=True)
+            step()
+            for o, t in zip(outs, (W, tau) + ((b,) if b is not None else ())):
+                o.copy_(t.grad, non_blocking=True)
+
+        for _ in range(2):
+            e2e_step()
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record()
+        for _ in range(args.steps):
+            e2e_step()
+        f1.record()
+        torch.cuda.synchronize()
+        ems = f0.elapsed_time(f1) / args.steps
+        if group is not None:
+            import torch.distributed as dist
+            t = torch.tensor([ems], device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+            ems = t.item()
+        e2e = {"value": round(points / (ems * 1e-3) / 1e6, 3), "unit": UNIT,
+               "h2d_bytes_per_step": (xh.numel() * xh.element_size()
+                                      + fh.numel() * fh.element_size()),
+               "d2h_bytes_per_step": res_bytes,
+               "path": "fused_slice/fused_deslice + autograd, inputs copied from pinned host "
+                       "memory and parameter gradients read back every step"}
+
+    # per-op device times of the same round, for the roofline
+    dot = K.slice_ops._dot_mode(x)
+    opt = op_timings(K, x, fx, W, b, tau, r, dot)
+    elem = x.element_size()
+    unit_bytes = cfg["B"] * n_local * cfg["H"] * cfg["D"] * elem
+    top = max(opt, key=opt.get)
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except (OSError, ValueError):
+        pass
+    peak = peaks.get("hbm_gbs")
+    peak_src = "measured" if peak else "fallback"
+    peak = peak or 6650.0
+    algo = UNITS[top] * unit_bytes
+    achieved = algo / (opt[top] * 1e-3) / 1e9
+    round_bytes = sum(UNITS.values()) * unit_bytes
+    roofline = {"bound": "hbm", "kernel": top, "achieved": round(achieved, 1),
+                "peak": peak, "peak_source": peak_src, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "traffic": None,
+                "algorithmic_bytes_per_launch": algo,
+                "op_ms": {k: round(v, 4) for k, v in opt.items()},
+                "round_frac": round(round_bytes / (ms * 1e-3) / 1e9 / peak, 4)}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_baseline(cfg, min(args.cpu_sample, cfg["N"]))
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+                "higher_is_better": True, "scaling": "strong" if cfg["split"] else "weak",
+                "vs_baseline": None,
+                "dtype": "f32" if cfg["dtype"] == torch.float32 else "bf16",
+                "data": "synthetic (seeded torch.Generator on the device)",
+                "config": {"workload": args.config, "B": cfg["B"], "N_per_gpu": n_local,
+                           "H": cfg["H"], "D": cfg["D"], "DV": cfg["DV"], "G": cfg["G"],
+                           "weight": cfg["weight"], "dot": cfg["dot"],
+                           "parallelism": "point-shard x%d" % world,
+                           "l2": "inputs larger than L2 (%d MiB per point tensor), no flush"
+                                 % (unit_bytes >> 20)},
+                "e2e": e2e, "gpu_launches": int(launches), "roofline": roofline,
+                "cpu_baseline": cpu, "clocks": clk}
+        print(json.dumps(line), flush=True)
+    if group is not None:
+        import torch.distributed as dist
+        dist.barrier(group=group)
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

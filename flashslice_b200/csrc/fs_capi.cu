@@ -1,0 +1,387 @@
+// flashslice_b200 -- the C ABI (include/flashslice_b200.h): validation,
+// engine choice, workspace carving and launch order of each op.
+#include <cstdarg>
+#include <cstdio>
+#include <string>
+
+#include "flashslice_b200.h"
+#include "fs_launch.h"
+
+using namespace fs;
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return code;
+}
+
+#define FS_TRY(call)                                                              \
+  do {                                                                            \
+    const cudaError_t e_ = (call);                                                \
+    if (e_ != cudaSuccess)                                                        \
+      return fail(FS_ERR_CUDA, "%s failed: %s", #call, cudaGetErrorString(e_));   \
+  } while (0)
+
+int check_problem(const fs_problem* p) {
+  if (!p) return fail(FS_ERR_ARGUMENT, "problem is NULL");
+  if (p->B < 1 || p->H < 1 || p->N < 0 || p->G < 1)
+    return fail(FS_ERR_SHAPE, "bad extents B=%lld N=%lld H=%lld G=%lld", (long long)p->B,
+                (long long)p->N, (long long)p->H, (long long)p->G);
+  if (p->D < 1 || p->D > 256)
+    return fail(FS_ERR_UNSUPPORTED, "dim_head=%lld is outside the supported range [1, 256]",
+                (long long)p->D);
+  if (p->DV < 1 || p->DV > 256)
+    return fail(FS_ERR_UNSUPPORTED, "value width %lld is outside the supported range [1, 256]",
+                (long long)p->DV);
+  if (p->N > (int64_t)1 << 30 || p->B * p->H > 65535 || (p->G + GB - 1) / GB > 65535 ||
+      p->G > ((int64_t)1 << 24))
+    return fail(FS_ERR_SHAPE, "extents beyond the engine's index range");
+  if (p->act_dtype < 0 || p->act_dtype > 2) return fail(FS_ERR_ARGUMENT, "bad act_dtype");
+  if (p->dot < 0 || p->dot > 4) return fail(FS_ERR_ARGUMENT, "bad dot level %d", p->dot);
+  if (p->family != FS_FAMILY_SINGLE && p->family != FS_FAMILY_BLOCKED)
+    return fail(FS_ERR_ARGUMENT, "bad family %d", p->family);
+  if (p->stats_mode != 0 && p->stats_mode != 1)
+    return fail(FS_ERR_ARGUMENT, "bad stats_mode %d", p->stats_mode);
+  auto ext_ok = [](int32_t v, int64_t full) { return v == 1 || v == full; };
+  if (!ext_ok(p->w_batch, p->B) || !ext_ok(p->w_heads, p->H))
+    return fail(FS_ERR_SHAPE, "weight has (batch, heads) = (%d, %d), x_mid has (%lld, %lld)",
+                p->w_batch, p->w_heads, (long long)p->B, (long long)p->H);
+  if (!ext_ok(p->b_batch, p->B) || !ext_ok(p->b_heads, p->H))
+    return fail(FS_ERR_SHAPE, "bias has (batch, heads) = (%d, %d), x_mid has (%lld, %lld)",
+                p->b_batch, p->b_heads, (long long)p->B, (long long)p->H);
+  if (p->flags < 0 || p->flags > 3) return fail(FS_ERR_ARGUMENT, "bad flags %d", p->flags);
+  return FS_OK;
+}
+
+struct Setup {
+  bool fused;
+  int nt, ntiles, ngb, Pn, Pg, BH;
+  bool internal_stats;
+  size_t stats, delta, partA, partB, partS, partDt, total;
+};
+
+Setup setup(int op, const fs_problem& p) {
+  Setup s = {};
+  const int D = (int)p.D, DV = (int)p.DV, G = (int)p.G;
+  s.BH = (int)(p.B * p.H);
+  s.nt = (round4(D) <= 64 && round4(DV) <= 64) ? 128 : 32;
+  s.fused = p.family == FS_FAMILY_SINGLE && G <= GB && s.nt == 128;
+  s.ntiles = (int)((p.N + s.nt - 1) / s.nt);
+  s.ngb = (G + GB - 1) / GB;
+  auto clampP = [&](int64_t want) {
+    int64_t v = want < s.ntiles ? want : s.ntiles;
+    return (int)(v < 1 ? 1 : v);
+  };
+  s.Pn = clampP((kTargetCtas + s.BH - 1) / s.BH);
+  s.Pg = clampP((kTargetCtas + (int64_t)s.BH * s.ngb - 1) / ((int64_t)s.BH * s.ngb));
+  const bool has_in = p.flags & FS_FLAG_STATS_IN;
+  const bool has_out = p.flags & FS_FLAG_STATS_OUT;
+  size_t off = 0;
+  auto take = [&](int64_t floats) {
+    const size_t o = off;
+    off += ((size_t)floats * sizeof(float) + 255) & ~(size_t)255;
+    return o;
+  };
+  const int64_t BH = s.BH;
+  switch (op) {
+    case FS_OP_SLICE_FWD:
+      if (s.fused) {
+        s.partA = take(BH * s.Pn * G * DV);
+        s.partS = take(BH * s.Pn * G);
+      } else {
+        s.internal_stats = !has_in && !(p.family == FS_FAMILY_BLOCKED && has_out);
+        s.partA = take(BH * s.Pg * G * DV);
+        s.partS = take(BH * s.Pg * G);
+      }
+      break;
+    case FS_OP_DESLICE_FWD:
+      if (!s.fused) s.internal_stats = !has_in && !(p.family == FS_FAMILY_BLOCKED && has_out);
+      break;
+    case FS_OP_SLICE_BWD:
+    case FS_OP_DESLICE_BWD: {
+      const bool sl = op == FS_OP_SLICE_BWD;
+      if (s.fused) {
+        s.partA = take(BH * s.Pn * G * D);
+        if (!sl) s.partB = take(BH * s.Pn * G * DV);
+        s.partS = take(BH * s.Pn * G);
+        s.partDt = take(BH * s.Pn);
+      } else {
+        s.internal_stats = !has_in;
+        s.delta = take(BH * p.N);
+        s.partDt = take(BH * s.Pn);
+        s.partA = take(BH * s.Pg * G * D);
+        if (!sl) s.partB = take(BH * s.Pg * G * DV);
+        s.partS = take(BH * s.Pg * G);
+      }
+      break;
+    }
+    default:
+      break;
+  }
+  if (s.internal_stats) s.stats = take(BH * 2 * p.N);
+  s.total = off;
+  return s;
+}
+
+Params base_params(const fs_problem& p, const Setup& s, const float* W, const float* bias,
+                   const float* tau) {
+  Params q = {};
+  q.B = (int)p.B; q.N = (int)p.N; q.H = (int)p.H;
+  q.D = (int)p.D; q.DV = (int)p.DV; q.G = (int)p.G;
+  q.ntiles = s.ntiles;
+  q.W = W; q.bias = bias; q.tau = tau;
+  q.swb = p.w_batch > 1 ? (int64_t)p.w_heads * p.G * p.D : 0;
+  q.swh = p.w_heads > 1 ? p.G * p.D : 0;
+  q.sbb = p.b_batch > 1 ? (int64_t)p.b_heads * p.G : 0;
+  q.sbh = p.b_heads > 1 ? p.G : 0;
+  return q;
+}
+
+Pt pt(const fs_tensor4* t) {
+  Pt r;
+  r.data = t ? t->data : nullptr;
+  r.sb = t ? t->stride[0] : 0;
+  r.sn = t ? t->stride[1] : 0;
+  r.sh = t ? t->stride[2] : 0;
+  r.sw = t ? t->stride[3] : 0;
+  return r;
+}
+
+int check_ws(const Setup& s, void* ws, size_t bytes) {
+  if (s.total == 0) return FS_OK;
+  if (!ws) return fail(FS_ERR_WORKSPACE, "workspace of %zu bytes needed, got NULL", s.total);
+  if (bytes < s.total)
+    return fail(FS_ERR_WORKSPACE, "workspace of %zu bytes needed, got %zu", s.total, bytes);
+  if ((uintptr_t)ws % 256) return fail(FS_ERR_WORKSPACE, "workspace is not 256-byte aligned");
+  return FS_OK;
+}
+
+float* at(void* ws, size_t off) { return (float*)((char*)ws + off); }
+
+int need(const void* ptr, const char* what) {
+  if (!ptr) return fail(FS_ERR_ARGUMENT, "%s is NULL", what);
+  return FS_OK;
+}
+
+#define FS_CHECK(expr)           \
+  do {                           \
+    const int rc_ = (expr);      \
+    if (rc_ != FS_OK) return rc_; \
+  } while (0)
+
+int launch_kind(Kind k, const fs_problem& p, const Setup& s, Params q, int P, cudaStream_t st) {
+  q.P = P;
+  q.pl = make_plan(k, (int)p.D, (int)p.DV, s.nt);
+  FS_TRY(run_engine(k, p.act_dtype, s.nt, q, s.ngb, st));
+  return FS_OK;
+}
+
+int run_stats(const fs_problem& p, const Setup& s, const fs_tensor4* x, const float* W,
+              const float* bias, const float* tau, float* dst, cudaStream_t st) {
+  Params q = base_params(p, s, W, bias, tau);
+  q.x = pt(x);
+  q.stats_out = dst;
+  return launch_kind(p.stats_mode == 1 ? Kind::StatsTwoPass : Kind::StatsOnline, p, s, q, s.Pn,
+                     st);
+}
+
+}  // namespace
+
+extern "C" {
+
+int fs_version(void) { return FS_ABI_VERSION; }
+
+const char* fs_last_error(void) { return g_err.c_str(); }
+
+uint64_t fs_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+size_t fs_workspace_bytes(int op, const fs_problem* p) {
+  if (check_problem(p) != FS_OK) return 0;
+  return setup(op, *p).total;
+}
+
+int fs_compute_stats(const fs_problem* p, const fs_tensor4* x_mid, const float* weight,
+                     const float* bias, const float* tau, float* stats, void* stream) {
+  FS_CHECK(check_problem(p));
+  FS_CHECK(need(x_mid, "x_mid"));
+  FS_CHECK(need(weight, "weight"));
+  FS_CHECK(need(bias, "bias"));
+  FS_CHECK(need(tau, "tau"));
+  FS_CHECK(need(stats, "stats"));
+  const Setup s = setup(FS_OP_STATS, *p);
+  return run_stats(*p, s, x_mid, weight, bias, tau, stats, (cudaStream_t)stream);
+}
+
+int fs_slice_fwd(const fs_problem* p, const fs_tensor4* x_mid, const fs_tensor4* fx_mid,
+                 const float* weight, const float* bias, const float* tau, const float* stats_in,
+                 float* stats_out, float* z_num, float* s_out, void* workspace,
+                 size_t workspace_bytes, void* stream) {
+  FS_CHECK(check_problem(p));
+  FS_CHECK(need(x_mid, "x_mid"));
+  FS_CHECK(need(fx_mid, "fx_mid"));
+  FS_CHECK(need(weight, "weight"));
+  FS_CHECK(need(bias, "bias"));
+  FS_CHECK(need(tau, "tau"));
+  FS_CHECK(need(z_num, "z_num"));
+  FS_CHECK(need(s_out, "s"));
+  if (!!stats_in != !!(p->flags & FS_FLAG_STATS_IN) ||
+      !!stats_out != !!(p->flags & FS_FLAG_STATS_OUT))
+    return fail(FS_ERR_ARGUMENT, "stats pointers disagree with problem flags");
+  const Setup s = setup(FS_OP_SLICE_FWD, *p);
+  FS_CHECK(check_ws(s, workspace, workspace_bytes));
+  cudaStream_t st = (cudaStream_t)stream;
+  Params q = base_params(*p, s, weight, bias, tau);
+  q.x = pt(x_mid);
+  q.v = pt(fx_mid);
+  q.partA = at(workspace, s.partA);
+  q.partS = at(workspace, s.partS);
+  int P;
+  if (s.fused) {
+    P = s.Pn;
+    FS_CHECK(launch_kind(Kind::FusedSliceFwd, *p, s, q, P, st));
+  } else {
+    const float* stats = stats_in;
+    if (!stats) {
+      float* dst = s.internal_stats ? at(workspace, s.stats) : stats_out;
+      FS_CHECK(run_stats(*p, s, x_mid, weight, bias, tau, dst, st));
+      stats = dst;
+    }
+    q.stats_in = stats;
+    P = s.Pg;
+    FS_CHECK(launch_kind(Kind::SliceFwdG, *p, s, q, P, st));
+  }
+  const int BH = s.BH;
+  FS_TRY(run_reduce(q.partA, z_num, BH, 1, P, p->G * p->DV, BH, 1, st));
+  FS_TRY(run_reduce(q.partS, s_out, BH, 1, P, p->G, BH, 1, st));
+  return FS_OK;
+}
+
+int fs_deslice_fwd(const fs_problem* p, const fs_tensor4* x_mid, const float* weight,
+                   const float* bias, const float* tau, const float* tokens,
+                   const float* stats_in, float* stats_out, const fs_tensor4* out,
+                   void* workspace, size_t workspace_bytes, void* stream) {
+  FS_CHECK(check_problem(p));
+  FS_CHECK(need(x_mid, "x_mid"));
+  FS_CHECK(need(weight, "weight"));
+  FS_CHECK(need(bias, "bias"));
+  FS_CHECK(need(tau, "tau"));
+  FS_CHECK(need(tokens, "tokens"));
+  FS_CHECK(need(out, "out"));
+  if (!!stats_in != !!(p->flags & FS_FLAG_STATS_IN) ||
+      !!stats_out != !!(p->flags & FS_FLAG_STATS_OUT))
+    return fail(FS_ERR_ARGUMENT, "stats pointers disagree with problem flags");
+  const Setup s = setup(FS_OP_DESLICE_FWD, *p);
+  FS_CHECK(check_ws(s, workspace, workspace_bytes));
+  cudaStream_t st = (cudaStream_t)stream;
+  Params q = base_params(*p, s, weight, bias, tau);
+  q.x = pt(x_mid);
+  q.o1 = pt(out);
+  q.M = tokens;
+  if (s.fused) return launch_kind(Kind::FusedDesliceFwd, *p, s, q, s.Pn, st);
+  if (stats_in) {
+    q.stats_in = stats_in;
+    return launch_kind(Kind::DesliceFwdStats, *p, s, q, s.Pn, st);
+  }
+  float* dst = s.internal_stats ? at(workspace, s.stats) : stats_out;
+  if (p->stats_mode == 0) {
+    q.stats_out = dst;
+    return launch_kind(Kind::DesliceFwdOnline, *p, s, q, s.Pn, st);
+  }
+  FS_CHECK(run_stats(*p, s, x_mid, weight, bias, tau, dst, st));
+  q.stats_in = dst;
+  return launch_kind(Kind::DesliceFwdStats, *p, s, q, s.Pn, st);
+}
+
+static int bwd_common(bool slice, const fs_problem* p, const fs_tensor4* x_mid,
+                      const fs_tensor4* vals, const float* weight, const float* bias,
+                      const float* tau, const float* mat, const float* ds, const float* stats_in,
+                      const fs_tensor4* dx, const fs_tensor4* dfx, float* dtok, float* dW,
+                      float* db, float* dtau, void* workspace, size_t workspace_bytes,
+                      void* stream) {
+  FS_CHECK(check_problem(p));
+  FS_CHECK(need(x_mid, "x_mid"));
+  FS_CHECK(need(vals, slice ? "fx_mid" : "d_out"));
+  FS_CHECK(need(weight, "weight"));
+  FS_CHECK(need(bias, "bias"));
+  FS_CHECK(need(tau, "tau"));
+  FS_CHECK(need(mat, slice ? "dz_num" : "tokens"));
+  FS_CHECK(need(dx, "dx_mid"));
+  FS_CHECK(need(dW, "dW"));
+  FS_CHECK(need(db, "db"));
+  FS_CHECK(need(dtau, "dtau"));
+  if (slice) {
+    FS_CHECK(need(ds, "ds"));
+    FS_CHECK(need(dfx, "dfx_mid"));
+  } else {
+    FS_CHECK(need(dtok, "dtokens"));
+  }
+  if (!!stats_in != !!(p->flags & FS_FLAG_STATS_IN) || (p->flags & FS_FLAG_STATS_OUT))
+    return fail(FS_ERR_ARGUMENT, "stats pointers disagree with problem flags");
+  if (p->family == FS_FAMILY_BLOCKED && !stats_in)
+    return fail(FS_ERR_ARGUMENT, "the blocked backward needs the forward's statistics");
+  const Setup s = setup(slice ? FS_OP_SLICE_BWD : FS_OP_DESLICE_BWD, *p);
+  FS_CHECK(check_ws(s, workspace, workspace_bytes));
+  cudaStream_t st = (cudaStream_t)stream;
+  Params q = base_params(*p, s, weight, bias, tau);
+  q.x = pt(x_mid);
+  q.v = pt(vals);
+  q.o1 = pt(dx);
+  if (slice) q.o2 = pt(dfx);
+  q.M = mat;
+  q.ds = ds;
+  q.partA = at(workspace, s.partA);
+  if (!slice) q.partB = at(workspace, s.partB);
+  q.partS = at(workspace, s.partS);
+  q.partDt = at(workspace, s.partDt);
+  int Pw;
+  if (s.fused) {
+    Pw = s.Pn;
+    FS_CHECK(launch_kind(slice ? Kind::FusedSliceBwd : Kind::FusedDesliceBwd, *p, s, q, Pw, st));
+  } else {
+    const float* stats = stats_in;
+    if (!stats) {
+      float* dst = at(workspace, s.stats);
+      FS_CHECK(run_stats(*p, s, x_mid, weight, bias, tau, dst, st));
+      stats = dst;
+    }
+    q.stats_in = stats;
+    q.delta = at(workspace, s.delta);
+    FS_CHECK(launch_kind(slice ? Kind::SliceBwdN : Kind::DesliceBwdN, *p, s, q, s.Pn, st));
+    Pw = s.Pg;
+    FS_CHECK(launch_kind(slice ? Kind::SliceBwdG : Kind::DesliceBwdG, *p, s, q, Pw, st));
+  }
+  const int B = (int)p->B, H = (int)p->H, BH = s.BH;
+  FS_TRY(run_reduce(q.partA, dW, B, H, Pw, p->G * p->D, p->w_batch, p->w_heads, st));
+  FS_TRY(run_reduce(q.partS, db, B, H, Pw, p->G, p->b_batch, p->b_heads, st));
+  if (!slice) FS_TRY(run_reduce(q.partB, dtok, BH, 1, Pw, p->G * p->DV, BH, 1, st));
+  FS_TRY(run_reduce(q.partDt, dtau, B, H, s.Pn, 1, 1, H, st));
+  return FS_OK;
+}
+
+int fs_slice_bwd(const fs_problem* p, const fs_tensor4* x_mid, const fs_tensor4* fx_mid,
+                 const float* weight, const float* bias, const float* tau, const float* stats_in,
+                 const float* dz_num, const float* ds, const fs_tensor4* dx_mid,
+                 const fs_tensor4* dfx_mid, float* dW, float* db, float* dtau, void* workspace,
+                 size_t workspace_bytes, void* stream) {
+  return bwd_common(true, p, x_mid, fx_mid, weight, bias, tau, dz_num, ds, stats_in, dx_mid,
+                    dfx_mid, nullptr, dW, db, dtau, workspace, workspace_bytes, stream);
+}
+
+int fs_deslice_bwd(const fs_problem* p, const fs_tensor4* x_mid, const float* weight,
+                   const float* bias, const float* tau, const float* tokens,
+                   const float* stats_in, const fs_tensor4* d_out, const fs_tensor4* dx_mid,
+                   float* dtokens, float* dW, float* db, float* dtau, void* workspace,
+                   size_t workspace_bytes, void* stream) {
+  return bwd_common(false, p, x_mid, d_out, weight, bias, tau, tokens, nullptr, stats_in, dx_mid,
+                    nullptr, dtokens, dW, db, dtau, workspace, workspace_bytes, stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,94 @@
+"""Point-sharded slice/deslice coupling across the GPUs of one node.
+
+The slice is a sum over points, the deslice and both backward passes are
+per point given the token state, so the coupling shards over N with no
+exchange of point data: each rank slices its own contiguous range of points,
+the tiny per-rank partials (z_num, s) -- B*H*G*(DV+1) floats -- are summed
+across ranks, and the deslice runs locally on the replicated tokens. In the
+backward the per-rank token gradients are summed the same way (the slice's
+upstream gradient needs all of them), and the parameter gradients (dW, db,
+dtau) are summed once at the end (the point-sharded coupling the reference
+plans in ROADMAP.md "Point-sharded slice": an all-reduce of (z_num, s) in
+the forward and of dtokens in the backward).
+
+Every cross-rank sum is an all-gather of the per-rank partials into a
+(world, ...) buffer followed by a sum in rank order 0, 1, ..., so every rank
+computes bitwise the same result and the result is bitwise reproducible
+run to run for a fixed world size, whatever algorithm NCCL picks.
+"""
+
+import torch
+import torch.distributed as dist
+
+
+def shard_range(n, rank, world):
+    """Contiguous point range [start, stop) of ``rank``: N // world points
+    each, the remainder one point each to the last ranks."""
+    base, rem = divmod(n, world)
+    start = rank * base + max(0, rank - (world - rem))
+    return start, start + base + (1 if rank >= world - rem else 0)
+
+
+def ordered_sum(t, group=None):
+    """Sum of ``t`` over the ranks of ``group`` in rank order (no autograd)."""
+    world = dist.get_world_size(group)
+    if world == 1:
+        return t.clone()
+    t = t.contiguous()
+    buf = torch.empty((world,) + tuple(t.shape), dtype=t.dtype, device=t.device)
+    dist.all_gather_into_tensor(buf, t, group=group)
+    out = buf[0].clone()
+    for r in range(1, world):
+        out += buf[r]
+    return out
+
+
+class _RankSum(torch.autograd.Function):
+    """y = sum over ranks of x, replicated on every rank; the gradient of a
+    loss summed over ranks with respect to each rank's x is again the sum
+    over ranks of the gradients at y."""
+
+    @staticmethod
+    def forward(ctx, x, group):
+        ctx.group = group
+        return ordered_sum(x, group)
+
+    @staticmethod
+    def backward(ctx, g):
+        return ordered_sum(g, ctx.group), None
+
+
+def rank_sum(x, group=None):
+    return _RankSum.apply(x, group)
+
+
+def sharded_slice(x_mid, fx_mid, weight, bias, tau, group=None, slice_fn=None):
+    """``fused_slice`` of this rank's points, summed over the ranks: returns
+    the global z_num (B, H, G, DV) and s (B, H, G) on every rank.
+    ``slice_fn`` replaces ``fused_slice`` (tests run the host logic on CPU
+    ranks with the eager reference in its place)."""
+    if slice_fn is None:
+        from .kernels import fused_slice as slice_fn
+    z_num, s = slice_fn(x_mid, fx_mid, weight, bias, tau)
+    return rank_sum(z_num, group), rank_sum(s, group)
+
+
+def sharded_coupling(x_mid, fx_mid, weight, bias, tau, mix=None, eps=1e-5, group=None,
+                     slice_fn=None, deslice_fn=None):
+    """slice -> z_num / (s + eps) -> mix (None = identity) -> deslice over the
+    rank's points; the output rows are this rank's points."""
+    if deslice_fn is None:
+        from .kernels import fused_deslice as deslice_fn
+    z_num, s = sharded_slice(x_mid, fx_mid, weight, bias, tau, group, slice_fn)
+    tokens = z_num / (s + eps)[..., None]
+    if mix is not None:
+        tokens = mix(tokens)
+    return deslice_fn(x_mid, weight, bias, tau, tokens)
+
+
+def reduce_grads(params, group=None):
+    """Sum the gradients of replicated parameters over the ranks, in rank
+    order, in place (the data-parallel gradient of the sharded coupling)."""
+    for p in params:
+        if p is not None and p.grad is not None:
+            p.grad.copy_(ordered_sum(p.grad, group))

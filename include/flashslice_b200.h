@@ -1,0 +1,169 @@
+/*
+ * flashslice_b200 -- C ABI of the B200 (sm_100a) slice/deslice coupling.
+ *
+ * The reference (Shizheng-Wen/flashslice v0.3.0) exposes this path as Python
+ * functions that launch Triton kernels; each entry point below replaces one
+ * of its host launchers, with the same argument meaning:
+ *
+ *   fs_slice_fwd    <- _slice_impl            flashslice/kernels/slice_ops.py:804-819
+ *                      _slice_blk_impl        flashslice/kernels/blocked.py:1346-1368
+ *   fs_deslice_fwd  <- _deslice_impl          slice_ops.py:846-859
+ *                      _deslice_blk_impl      blocked.py:1406-1433
+ *   fs_slice_bwd    <- _slice_bwd_impl        slice_ops.py:822-843
+ *                      _slice_blk_bwd_impl    blocked.py:1371-1403
+ *   fs_deslice_bwd  <- _deslice_bwd_impl      slice_ops.py:862-885
+ *                      _deslice_blk_bwd_impl  blocked.py:1436-1469
+ *   fs_compute_stats<- compute_stats          blocked.py:1329-1343
+ *   fs_workspace_bytes: the partial-sum buffers the reference allocates with
+ *                      torch.empty inside each launcher (slice_ops.py:811-814).
+ *
+ * Conventions
+ *   - Shapes: x_mid (B, N, H, D); fx_mid, d_out, out (B, N, H, DV);
+ *     tokens, z_num, dz_num, dtokens (B, H, G, DV) fp32 contiguous;
+ *     s, ds (B, H, G) fp32 contiguous; tau, dtau (H,) fp32;
+ *     stats (B, H, 2, N) fp32 contiguous: [.., 0, n] row max m, [.., 1, n]
+ *     sum of exponentials l (blocked.py:293-346).
+ *   - The slice weight is fp32 contiguous of shape (w_batch, w_heads, G, D)
+ *     with w_batch in {1, B} and w_heads in {1, H}: (G, D), (H, G, D) and
+ *     (B, H, G, D) of the reference (slice_ops.py:503-526). The bias is
+ *     fp32 contiguous (b_batch, b_heads, G); a missing bias is zeros(G).
+ *     dW / db are returned in those same shapes, summed over the shared axes
+ *     (slice_ops.py:481-500).
+ *   - The point tensors (fs_tensor4) are read and written through arbitrary
+ *     element strides (b, n, h, width) in act_dtype.
+ *   - Every call enqueues on `stream` (a cudaStream_t) and returns at once.
+ *     Results are bitwise deterministic for a given shape: no atomics; every
+ *     reduction runs in a fixed order.
+ *   - Workspace: caller-allocated device memory of at least
+ *     fs_workspace_bytes(op, p) bytes, 256-byte aligned.
+ *   - Return value: FS_OK or an fs_status code; fs_last_error() describes the
+ *     last failure of the calling thread.
+ */
+#ifndef FLASHSLICE_B200_H
+#define FLASHSLICE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FS_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define FS_API __attribute__((visibility("default")))
+#else
+#define FS_API
+#endif
+
+typedef enum fs_dtype { FS_F32 = 0, FS_BF16 = 1, FS_F16 = 2 } fs_dtype;
+
+typedef enum fs_status {
+  FS_OK = 0,
+  FS_ERR_SHAPE = 1,       /* bad extents / layout (reference: ValueError)   */
+  FS_ERR_ARGUMENT = 2,    /* null pointer, bad enum, bad mode               */
+  FS_ERR_WORKSPACE = 3,   /* workspace too small or misaligned              */
+  FS_ERR_CUDA = 4,        /* a CUDA launch or runtime call failed           */
+  FS_ERR_TIMEOUT = 5,     /* a bounded device-side wait gave up             */
+  FS_ERR_UNSUPPORTED = 6  /* dims outside the supported range (D, DV > 256) */
+} fs_status;
+
+typedef enum fs_op {
+  FS_OP_SLICE_FWD = 0,
+  FS_OP_DESLICE_FWD = 1,
+  FS_OP_SLICE_BWD = 2,
+  FS_OP_DESLICE_BWD = 3,
+  FS_OP_STATS = 4
+} fs_op;
+
+/* Family: which reference kernel family's contract the call follows.
+ * FS_FAMILY_SINGLE forms the softmax whole per point and neither takes nor
+ * returns statistics (slice_ops.py); FS_FAMILY_BLOCKED works from the
+ * per-point statistics (m, l), takes them when given and returns them
+ * (blocked.py). */
+typedef enum fs_family { FS_FAMILY_SINGLE = 0, FS_FAMILY_BLOCKED = 1 } fs_family;
+
+typedef struct fs_problem {
+  int64_t B, N, H, D, DV, G;
+  int32_t act_dtype;   /* fs_dtype of the point tensors                        */
+  int32_t dot;         /* dot level 0 ieee .. 4 tf32x3 (slice_ops.py:336-360)  */
+  int32_t family;      /* fs_family                                            */
+  int32_t stats_mode;  /* 0 online, 1 two-pass (blocked.py:101-120)            */
+  int32_t w_batch, w_heads; /* weight leading extents: 1 or B, 1 or H          */
+  int32_t b_batch, b_heads; /* bias leading extents: 1 or B, 1 or H            */
+  int32_t flags;       /* FS_FLAG_* : which optional statistics buffers the
+                          call passes; part of the workspace size contract    */
+  int32_t reserved;    /* 0 */
+} fs_problem;
+
+#define FS_FLAG_STATS_IN 1  /* stats_in is given (non-NULL)   */
+#define FS_FLAG_STATS_OUT 2 /* stats_out is given (non-NULL)  */
+
+typedef struct fs_tensor4 {
+  void* data;
+  int64_t stride[4]; /* element strides along (b, n, h, width) */
+} fs_tensor4;
+
+/* Library ABI version (FS_ABI_VERSION). */
+FS_API int fs_version(void);
+
+/* Description of the last failure on the calling thread ("" if none). */
+FS_API const char* fs_last_error(void);
+
+/* Number of kernels this library has launched in this process (all
+ * devices and threads); a diagnostic for benchmarks, no reference
+ * counterpart. */
+FS_API uint64_t fs_launch_count(void);
+
+/* Bytes of workspace `op` needs for problem `p` (0 when it needs none). */
+FS_API size_t fs_workspace_bytes(int op, const fs_problem* p);
+
+/* Slice forward: z_num (B,H,G,DV), s (B,H,G). Blocked family: stats_in may
+ * be NULL (then the statistics are formed first) and stats_out, when not
+ * NULL, receives the statistics used (the reference's third output). */
+FS_API int fs_slice_fwd(const fs_problem* p, const fs_tensor4* x_mid,
+                 const fs_tensor4* fx_mid, const float* weight,
+                 const float* bias, const float* tau, const float* stats_in,
+                 float* stats_out, float* z_num, float* s, void* workspace,
+                 size_t workspace_bytes, void* stream);
+
+/* Deslice forward: out (B,N,H,DV) in act_dtype. Blocked family without
+ * stats_in: the online kernel forms out and the statistics in one pass
+ * (stats_mode 0) and writes them to stats_out. */
+FS_API int fs_deslice_fwd(const fs_problem* p, const fs_tensor4* x_mid,
+                   const float* weight, const float* bias, const float* tau,
+                   const float* tokens, const float* stats_in, float* stats_out,
+                   const fs_tensor4* out, void* workspace,
+                   size_t workspace_bytes, void* stream);
+
+/* Slice backward for upstream dz_num (B,H,G,DV) and ds (B,H,G):
+ * dx_mid, dfx_mid (act_dtype, strided), dW, db (parameter shapes), dtau (H).
+ * Blocked family: stats_in is required. */
+FS_API int fs_slice_bwd(const fs_problem* p, const fs_tensor4* x_mid,
+                 const fs_tensor4* fx_mid, const float* weight,
+                 const float* bias, const float* tau, const float* stats_in,
+                 const float* dz_num, const float* ds, const fs_tensor4* dx_mid,
+                 const fs_tensor4* dfx_mid, float* dW, float* db, float* dtau,
+                 void* workspace, size_t workspace_bytes, void* stream);
+
+/* Deslice backward for upstream d_out (B,N,H,DV): dx_mid, dtokens
+ * (B,H,G,DV), dW, db, dtau. Blocked family: stats_in is required. */
+FS_API int fs_deslice_bwd(const fs_problem* p, const fs_tensor4* x_mid,
+                   const float* weight, const float* bias, const float* tau,
+                   const float* tokens, const float* stats_in,
+                   const fs_tensor4* d_out, const fs_tensor4* dx_mid,
+                   float* dtokens, float* dW, float* db, float* dtau,
+                   void* workspace, size_t workspace_bytes, void* stream);
+
+/* Per-point softmax statistics (B,H,2,N) of the slice logits, in
+ * stats_mode's form (online or two-pass). */
+FS_API int fs_compute_stats(const fs_problem* p, const fs_tensor4* x_mid,
+                     const float* weight, const float* bias, const float* tau,
+                     float* stats, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FLASHSLICE_B200_H */

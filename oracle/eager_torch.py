@@ -64,3 +64,17 @@ def coupling_round(x, fx, w, b, tau, r, eps=1e-5, mix=None, r_z=None, r_s=None):
         if v is not None and v.grad is not None:
             res["grad:" + k] = v.grad.detach()
     return res
+
+
+def eager_orders(x, fx, w, b, tau, tm, tok, order):
+    """Both call orders of a tied coupling as ``parity_ops.eager`` forms them
+    (``parity_ops.py:69-79``): slice-first normalises the slice output,
+    applies ``tm`` and deslices it; deslice-first deslices the given tokens
+    and slices independently."""
+    sw = membership(x, w, b, tau)
+    z = torch.einsum("bhng,bnhd->bhgd", sw, fx)
+    s = sw.sum(2)
+    if order == "slice-first":
+        tok = (z / (s + 1e-5)[..., None]) @ tm
+    out = torch.einsum("bhgd,bhng->bnhd", tok.to(sw.dtype), sw)
+    return out, z, s

@@ -1,0 +1,145 @@
+"""Shared machinery of the GPU parity tests: seeded cases shaped as the
+reference's ``bench/parity_ops.py`` builds them (``Case``, ``:94-156``) and
+its gate (``run_case``, ``:159-208``), held to the tolerances of this
+build: within 1e-5 relative of the reference's fp32 eager implementation,
+or -- where the reference itself sits far from the float64 truth -- at
+least as close to the truth as the reference (1.25x its error + 1e-6); bf16
+within 2e-2 relative of the reference on the same bf16 inputs."""
+
+import numpy as np
+import torch
+
+from oracle import eager_torch as E
+
+FP32_TOL = 1e-5
+BF16_TOL = 2e-2
+
+
+def relerr(a, ref):
+    ref = ref.double()
+    n = ref.norm()
+    d = (a.double() - ref).norm()
+    return (d / n).item() if n > 0 else d.item()
+
+
+class Case:
+    """Leaves of one shape (``parity_ops.Case``): ``mode`` gd / hgd / bhgd
+    (weight = (t @ Wk) viewed (B, G, H, D), permuted: non-leaf and
+    non-contiguous)."""
+
+    def __init__(self, B, N, H, D, G, DV=None, mode="bhgd", bias=True, Ht=48, seed=7,
+                 device="cuda", strided=False):
+        self.B, self.N, self.H, self.D, self.G = B, N, H, D, G
+        self.DV = D if DV is None else DV
+        self.mode, self.bias, self.Ht, self.strided = mode, bias, Ht, strided
+        g = torch.Generator().manual_seed(seed)
+        r = lambda *s: torch.randn(*s, generator=g, dtype=torch.float64)  # noqa: E731
+        L = {"x": r(B, N, H, D), "fx": r(B, N, H, self.DV),
+             "tau": torch.full((H,), 0.7, dtype=torch.float64) + 0.1 * r(H),
+             "tok": r(B, H, G, self.DV)}
+        if mode == "gd":
+            L["w"] = r(G, D) / D ** 0.5
+            L["b"] = 0.1 * r(G)
+        elif mode == "hgd":
+            L["w"] = r(H, G, D) / D ** 0.5
+            L["b"] = 0.1 * r(H, G)
+        else:
+            L["t"] = r(B, G, Ht)
+            L["Wk"] = r(Ht, H * D) / (Ht * D) ** 0.25
+            if bias:
+                L["Wb"] = 0.1 * r(Ht, H)
+        self.leaves = {k: v.to(device) for k, v in L.items()}
+        self.tm = (r(self.DV, self.DV) / self.DV ** 0.5).to(device)
+        self.up = {"out": r(B, N, H, self.DV).to(device), "z": r(B, H, G, self.DV).to(device),
+                   "s": r(B, H, G).to(device)}
+
+    def build(self, L, amp):
+        x, fx, tau, tok = L["x"], L["fx"], L["tau"], L["tok"]
+        if self.strided:
+            # x_mid / fx_mid as permuted views of (B, H, N, D) tensors
+            x = x.permute(0, 2, 1, 3).contiguous().permute(0, 2, 1, 3)
+            fx = fx.permute(0, 2, 1, 3).contiguous().permute(0, 2, 1, 3)
+        if self.mode in ("gd", "hgd"):
+            w, b = L["w"], L.get("b")
+            if not self.bias:
+                b = None
+        else:
+            B, G, H, D = self.B, self.G, self.H, self.D
+            w = (L["t"] @ L["Wk"]).view(B, G, H, D).permute(0, 2, 1, 3)
+            b = (L["t"] @ L["Wb"]).permute(0, 2, 1) if self.bias else None
+        if amp:
+            x, fx, w = x.bfloat16(), fx.bfloat16(), w.bfloat16()
+            b = None if b is None else b.bfloat16()
+        return x, fx, w, b, tau, tok
+
+    def run(self, dtype, fused_ops, amp=False, order="slice-first"):
+        """Forward + backward of sum(out r_out) + sum(z r_z) + sum(s r_s);
+        ``fused_ops`` is the kernels module or None for the eager reference."""
+        L = {k: v.detach().to(dtype).requires_grad_(True) for k, v in self.leaves.items()}
+        x, fx, w, b, tau, tok = self.build(L, amp)
+        tm = self.tm.to(dtype)
+        if fused_ops is not None:
+            out, z, s = fused_coupling(fused_ops, x, fx, w, b, tau, tm, tok, order)
+        else:
+            f32 = (lambda t: None if t is None else (t.float() if amp else t))  # noqa: E731
+            out, z, s = E.eager_orders(f32(x), f32(fx), f32(w), f32(b), tau, tm, tok, order)
+        loss = ((out.float() * self.up["out"].float()).sum()
+                + (z.float() * self.up["z"].float()).sum()
+                + (s.float() * self.up["s"].float()).sum())
+        loss.backward()
+        res = {"out": out.detach(), "z_num": z.detach(), "s": s.detach()}
+        for k, v in L.items():
+            if v.grad is not None:
+                res["grad:" + k] = v.grad.detach()
+        return res
+
+
+def fused_coupling(K, x, fx, w, b, tau, tm, tok, order):
+    """The two call orders of a tied coupling through the fused ops
+    (``parity_ops.py:82-91``)."""
+    if order == "slice-first":
+        z, s, st = K.fused_slice(x, fx, w, b, tau, return_stats=True)
+        tok = (z / (s + 1e-5)[..., None]) @ tm.float()
+        out = K.fused_deslice(x, w, b, tau, tok, stats=st)
+    else:
+        out, st = K.fused_deslice(x, w, b, tau, tok.float(), return_stats=True)
+        z, s = K.fused_slice(x, fx, w, b, tau, stats=st)
+    return out, z, s
+
+
+def gate_case(case, K, kernel_mode="auto", dot="", order="slice-first", tau_gate=1.25):
+    """Run one case and return a list of (name, ok, detail) checks."""
+    K.set_kernel_mode(kernel_mode)
+    try:
+        ref = case.run(torch.float64, None, order=order)
+        amp = dot in ("bf16", "bf16v")
+        ea = case.run(torch.float32, None, amp=amp, order=order)
+        K.set_dot_mode(dot)
+        try:
+            fu = case.run(torch.float32, K, amp=amp, order=order)
+            fu2 = case.run(torch.float32, K, amp=amp, order=order)
+        finally:
+            K.set_dot_mode("")
+    finally:
+        K.set_kernel_mode("auto")
+    checks = []
+    for k in ref:
+        ee, ef, fe = relerr(ea[k], ref[k]), relerr(fu[k], ref[k]), relerr(fu[k], ea[k])
+        det = "eager-vs-fp64 %.3e fused-vs-fp64 %.3e fused-vs-eager %.3e" % (ee, ef, fe)
+        if ref[k].norm() == 0:
+            checks.append((k, fu[k].abs().max().item() <= 1e-6, "zero reference; " + det))
+            continue
+        if amp:
+            ok = fe <= BF16_TOL
+        else:
+            g = tau_gate if k == "grad:tau" else 1.25
+            ok = fe <= FP32_TOL or ef <= g * ee + 1e-6
+        checks.append((k, ok, det))
+    checks.append(("shapes", all(fu[k].shape == ref[k].shape for k in ref), ""))
+    checks.append(("determinism", all(torch.equal(fu[k], fu2[k]) for k in fu), ""))
+    return checks
+
+
+def assert_checks(checks):
+    bad = [(n, d) for n, ok, d in checks if not ok]
+    assert not bad, "failed checks: %s" % bad
