@@ -132,9 +132,19 @@ __device__ __forceinline__ void stage_rows(float* dst, int rs, int wt, const Pt&
                    ((uintptr_t)base % 16) == 0;
   if (vec) {
     const int q = w / VEC;
-    for (int i = threadIdx.x; i < NT * q; i += NT) {
-      const int r = i / q;
-      const int c = (i - r * q) * VEC;
+    // thread -> (row, chunk) once; rows advance by NT / q when q divides NT
+    const bool even = q <= NT && (NT % q) == 0;
+    const int step = even ? NT / q : 0;
+    const int c0 = even ? (threadIdx.x % q) * VEC : 0;
+    const int i_end = NT * q;
+    for (int i = threadIdx.x, r = even ? threadIdx.x / q : 0; i < i_end; i += NT) {
+      int c = c0;
+      if (even) {
+        if (i != (int)threadIdx.x) r += step;
+      } else {
+        r = i / q;
+        c = (i - r * q) * VEC;
+      }
       const int n = n0 + r;
       float f[VEC];
       if (n < N) {
@@ -174,9 +184,18 @@ __device__ __forceinline__ void store_rows(const float* src, int rs, const Pt& t
                    ((uintptr_t)base % 16) == 0;
   if (vec) {
     const int q = w / VEC;
-    for (int i = threadIdx.x; i < NT * q; i += NT) {
-      const int r = i / q;
-      const int c = (i - r * q) * VEC;
+    const bool even = q <= NT && (NT % q) == 0;
+    const int step = even ? NT / q : 0;
+    const int c0 = even ? (threadIdx.x % q) * VEC : 0;
+    const int i_end = NT * q;
+    for (int i = threadIdx.x, r = even ? threadIdx.x / q : 0; i < i_end; i += NT) {
+      int c = c0;
+      if (even) {
+        if (i != (int)threadIdx.x) r += step;
+      } else {
+        r = i / q;
+        c = (i - r * q) * VEC;
+      }
       const int n = n0 + r;
       if (n >= N) continue;
       float f[VEC];
@@ -245,6 +264,20 @@ __device__ __forceinline__ void block_logits(float (&lg)[GB], const float* xrow,
 }
 
 __device__ __forceinline__ float expd(float d) { return exp2f(d * kLog2e); }
+
+// Pairwise (tree) sum of a register array, in a fixed order: v[i] += v[i+s]
+// for s = N/2, N/4, ..., 1. The rounding error grows with log2(N) rather
+// than N, which the temperature gradient -- a row sum that cancels to zero
+// in exact arithmetic -- needs at large G. Destroys v.
+template <int N>
+__device__ __forceinline__ float tree_sum(float (&v)[N]) {
+#pragma unroll
+  for (int s = N / 2; s > 0; s >>= 1) {
+#pragma unroll
+    for (int i = 0; i < s; ++i) v[i] += v[i + s];
+  }
+  return v[0];
+}
 
 // row[c] = scale * row[c] + sum_g coef[g] * Ms[g][c]  over the padded width.
 __device__ __forceinline__ void row_axpy(float* row, const float (&coef)[GB], const float* Ms,

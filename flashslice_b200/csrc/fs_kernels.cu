@@ -35,12 +35,13 @@ __device__ __forceinline__ void row_softmax(const float (&lg)[GB], float (&w)[GB
   float m = lg[0];
 #pragma unroll
   for (int g = 1; g < GB; ++g) m = fmaxf(m, lg[g]);
-  float s = 0.f;
+  float tmp[GB];
 #pragma unroll
   for (int g = 0; g < GB; ++g) {
     w[g] = expd(lg[g] - m);
-    s += w[g];
+    tmp[g] = w[g];
   }
+  const float s = tree_sum(tmp);
   const float r = valid ? __frcp_rn(s) : 0.f;
 #pragma unroll
   for (int g = 0; g < GB; ++g) w[g] *= r;
@@ -50,17 +51,17 @@ __device__ __forceinline__ void row_softmax(const float (&lg)[GB], float (&w)[GB
 // sum_g dl * lg over the valid slots and leaves dl / tau in dw.
 __device__ __forceinline__ float row_jacobian(const float (&w)[GB], float (&dw)[GB],
                                               const float (&lg)[GB], float inv_tau, int G) {
-  float gs = 0.f;
+  float tmp[GB];
 #pragma unroll
-  for (int g = 0; g < GB; ++g) gs = fmaf(w[g], dw[g], gs);
-  float rdt = 0.f;
+  for (int g = 0; g < GB; ++g) tmp[g] = w[g] * dw[g];
+  const float gs = tree_sum(tmp);
 #pragma unroll
   for (int g = 0; g < GB; ++g) {
     const float dl = w[g] * (dw[g] - gs);
-    if (g < G) rdt = fmaf(dl, lg[g], rdt);
+    tmp[g] = g < G ? dl * lg[g] : 0.f;
     dw[g] = dl * inv_tau;
   }
-  return rdt;
+  return tree_sum(tmp);
 }
 
 template <int NT>
@@ -259,10 +260,9 @@ __global__ void __launch_bounds__(NT) k_blk_stats(Params p) {
         m = fmaxf(m, bm);
       } else {
         const float mn = fmaxf(m, bm);
-        float s = 0.f;
 #pragma unroll
-        for (int g = 0; g < GB; ++g) s += expd(lg[g] - mn);
-        l = l * expd(m - mn) + s;
+        for (int g = 0; g < GB; ++g) lg[g] = expd(lg[g] - mn);
+        l = l * expd(m - mn) + tree_sum(lg);
         m = mn;
       }
     }
@@ -274,10 +274,9 @@ __global__ void __launch_bounds__(NT) k_blk_stats(Params p) {
         __syncthreads();
         float lg[GB];
         block_logits(lg, xs + t * L.xrs, Ws, bs, L.dt, inv_tau, g0, G);
-        float s = 0.f;
 #pragma unroll
-        for (int g = 0; g < GB; ++g) s += expd(lg[g] - m);
-        l += s;
+        for (int g = 0; g < GB; ++g) lg[g] = expd(lg[g] - m);
+        l += tree_sum(lg);
       }
     }
     const int n = n0 + t;
@@ -319,13 +318,13 @@ __global__ void __launch_bounds__(NT) k_blk_deslice_fwd(Params p) {
         for (int g = 1; g < GB; ++g) bm = fmaxf(bm, lg[g]);
         const float mn = fmaxf(m, bm);
         const float alpha = expd(m - mn);
-        float s = 0.f;
+        float tmp[GB];
 #pragma unroll
         for (int g = 0; g < GB; ++g) {
           lg[g] = expd(lg[g] - mn);
-          s += lg[g];
+          tmp[g] = lg[g];
         }
-        l = l * alpha + s;
+        l = l * alpha + tree_sum(tmp);
         m = mn;
         row_axpy(os + t * L.ors, lg, Ms, L.dvt, L.dvt, alpha, first);
       } else {
@@ -426,8 +425,9 @@ __global__ void __launch_bounds__(NT) k_blk_bwd_n(Params p) {
 #pragma unroll
       for (int g = 0; g < GB; ++g) {
         if (SLICE) dw[g] += dss[g];
-        sdw = fmaf(lg[g], dw[g], sdw);
+        dw[g] *= lg[g];
       }
+      sdw += tree_sum(dw);
       if (SLICE) row_axpy(os + t * L.ors, lg, Ms, L.dvt, L.dvt, 1.f, first);
       first = false;
     }
@@ -451,9 +451,10 @@ __global__ void __launch_bounds__(NT) k_blk_bwd_n(Params p) {
         const float e = expd(lg[g] - m);
         const float dwg = SLICE ? dw[g] + dss[g] : dw[g];
         const float dl = (e * dwg - e * delta) * inv_l;
-        if (g0 + g < G) rdt = fmaf(dl, lg[g], rdt);
+        lg[g] = g0 + g < G ? dl * lg[g] : 0.f;
         dw[g] = dl;
       }
+      rdt += tree_sum(lg);
       row_axpy(ps + t * L.prs, dw, Ws, L.dt, L.dt, 1.f, first);
       first = false;
     }

@@ -184,7 +184,9 @@ def test_stats_modes_agree(K):
                   tau.double().cpu().numpy())
     got = st_two.double().cpu().numpy()
     assert np.max(np.abs(got[:, :, 0] - ref[:, :, 0])) < 1e-4
-    assert np.max(np.abs(got[:, :, 1] - ref[:, :, 1]) / ref[:, :, 1]) < 1e-5
+    # l is an fp32 sum of G = 1024 exponentials whose arguments carry the
+    # logits' own fp32 rounding: a few 1e-6 relative is the fp32 floor
+    assert np.max(np.abs(got[:, :, 1] - ref[:, :, 1]) / ref[:, :, 1]) < 2e-5
 
 
 def test_call_orders(K):
