@@ -115,7 +115,7 @@ Setup setup(int op, const fs_problem& p) {
         s.partDt = take(BH * s.Pn);
       } else {
         s.internal_stats = !has_in;
-        s.delta = take(BH * p.N);
+        s.delta = take(BH * 2 * p.N);
         s.partDt = take(BH * s.Pn);
         s.partA = take(BH * s.Pg * G * D);
         if (!sl) s.partB = take(BH * s.Pg * G * DV);

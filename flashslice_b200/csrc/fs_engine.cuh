@@ -52,7 +52,7 @@ struct Params {
   const float* ds;             // (B, H, G) fp32
   const float* stats_in;       // (B, H, 2, N)
   float* stats_out;
-  float* delta;                // (B, H, N) hand-off of the backward pair
+  float* delta;                // (B, H, 2, N): delta and row sum, point- to slot-owning
   float* partA;                // [bh][P][G][W] partials
   float* partB;
   float* partS;                // [bh][P][G]

@@ -405,10 +405,13 @@ __global__ void __launch_bounds__(NT) k_blk_bwd_n(Params p) {
     __syncthreads();
     stage_rows<T, NT>(xs, L.xrs, L.dt, p.x, b, h, n0, N, D);
     stage_rows<T, NT>(vs, L.vrs, L.dvt, p.v, b, h, n0, N, DV);
-    float m, l;
-    load_stats(p, bh, n, m, l);
-    const float inv_l = __frcp_rn(l);
-    float sdw = 0.f;
+    float m, l_saved;
+    load_stats(p, bh, n, m, l_saved);
+    // The row sum is formed here from the very exponentials the Jacobian
+    // uses, so that sum_g dl vanishes to one summation's rounding whatever
+    // rounding the saved l carries (the temperature gradient, sum dl*logit,
+    // turns any mismatch into a bias).
+    float sdw = 0.f, lrow = 0.f;
     bool first = true;
     for (int g0 = 0; g0 < G; g0 += GB) {
       __syncthreads();
@@ -417,10 +420,14 @@ __global__ void __launch_bounds__(NT) k_blk_bwd_n(Params p) {
       stage_block<NT>(Ms, L.dvt, mb, g0, G, DV);
       if (SLICE) stage_vec<NT>(dss, dsb, g0, G);
       __syncthreads();
-      float lg[GB], dw[GB];
+      float lg[GB], dw[GB], tmp[GB];
       block_logits(lg, xs + t * L.xrs, Ws, bs, L.dt, inv_tau, g0, G);
 #pragma unroll
-      for (int g = 0; g < GB; ++g) lg[g] = expd(lg[g] - m);
+      for (int g = 0; g < GB; ++g) {
+        lg[g] = expd(lg[g] - m);
+        tmp[g] = lg[g];
+      }
+      lrow += tree_sum(tmp);
       row_dots(dw, vs + t * L.vrs, Ms, L.dvt, L.dvt);
 #pragma unroll
       for (int g = 0; g < GB; ++g) {
@@ -431,8 +438,12 @@ __global__ void __launch_bounds__(NT) k_blk_bwd_n(Params p) {
       if (SLICE) row_axpy(os + t * L.ors, lg, Ms, L.dvt, L.dvt, 1.f, first);
       first = false;
     }
+    const float inv_l = __frcp_rn(lrow);
     const float delta = sdw * inv_l;
-    if (n < N) p.delta[(int64_t)bh * N + n] = delta;
+    if (n < N) {
+      p.delta[(int64_t)bh * 2 * N + n] = delta;
+      p.delta[(int64_t)bh * 2 * N + N + n] = lrow;
+    }
     if (SLICE) row_scale(os + t * L.ors, L.dvt, inv_l);
     float rdt = 0.f;
     first = true;
@@ -493,7 +504,9 @@ __global__ void __launch_bounds__(NT) k_blk_bwd_g(Params p) {
     stage_rows<T, NT>(vs, L.vrs, L.dvt, p.v, b, h, n0, N, DV);
     float m, l;
     load_stats(p, bh, n, m, l);
-    const float delta = n < N ? p.delta[(int64_t)bh * N + n] : 0.f;
+    // delta and the row sum the point-owning kernel formed (see k_blk_bwd_n)
+    const float delta = n < N ? p.delta[(int64_t)bh * 2 * N + n] : 0.f;
+    if (n < N) l = p.delta[(int64_t)bh * 2 * N + N + n];
     __syncthreads();
     float lg[GB], dw[GB];
     block_logits(lg, xs + t * L.xrs, Ws, bs, L.dt, inv_tau, g0, G);
