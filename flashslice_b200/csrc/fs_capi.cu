@@ -2,6 +2,7 @@
 // engine choice, workspace carving and launch order of each op.
 #include <cstdarg>
 #include <cstdio>
+#include <mutex>
 #include <string>
 
 #include "flashslice_b200.h"
@@ -195,7 +196,80 @@ int run_stats(const fs_problem& p, const Setup& s, const fs_tensor4* x, const fl
 
 }  // namespace
 
+// ---------------------------------------------------------------------------
+// Scratch for fs_slice_fwd_noalloc: a fixed device array, so that callers
+// that cannot allocate device memory can still run the slice forward. It is
+// created when the library is loaded on a device and lives until the process
+// exits; every call shares it.
+static __device__ __align__(256) float fs_noalloc_scratch[FS_NOALLOC_SCRATCH_BYTES / sizeof(float)];
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+float* g_noalloc_ptr[kMaxDevices] = {};
+
+// The device address of fs_noalloc_scratch on the current device. The name
+// of the array in host code is only a host-side stand-in, so the address is
+// asked of the runtime once per device (with that device current) and kept.
+int noalloc_scratch(float** out) {
+  int dev = 0;
+  FS_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices)
+    return fail(FS_ERR_UNSUPPORTED, "device ordinal %d beyond %d", dev, kMaxDevices);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* ptr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&ptr, fs_noalloc_scratch);
+    if (e != cudaSuccess || !ptr)
+      return fail(FS_ERR_CUDA, "cudaGetSymbolAddress(fs_noalloc_scratch) failed: %s",
+                  cudaGetErrorString(e));
+    g_noalloc_ptr[dev] = (float*)ptr;
+  }
+  *out = g_noalloc_ptr[dev];
+  return FS_OK;
+}
+
+}  // namespace
+
 extern "C" {
+
+int fs_slice_fwd_noalloc(const fs_problem* p, const fs_tensor4* x_mid, const fs_tensor4* fx_mid,
+                         const float* weight, const float* bias, const float* tau, float* z_num,
+                         float* s_out, void* stream) {
+  FS_CHECK(check_problem(p));
+  FS_CHECK(need(x_mid, "x_mid"));
+  FS_CHECK(need(fx_mid, "fx_mid"));
+  FS_CHECK(need(weight, "weight"));
+  FS_CHECK(need(bias, "bias"));
+  FS_CHECK(need(tau, "tau"));
+  FS_CHECK(need(z_num, "z_num"));
+  FS_CHECK(need(s_out, "s"));
+  if (p->flags != 0) return fail(FS_ERR_ARGUMENT, "fs_slice_fwd_noalloc takes no statistics");
+  const Setup s = setup(FS_OP_SLICE_FWD, *p);
+  if (!s.fused)
+    return fail(FS_ERR_UNSUPPORTED,
+                "fs_slice_fwd_noalloc serves the single-tile family with G <= 32 and "
+                "D, DV <= 64 only (G=%lld, D=%lld, DV=%lld)",
+                (long long)p->G, (long long)p->D, (long long)p->DV);
+  if (s.total > (size_t)FS_NOALLOC_SCRATCH_BYTES)
+    return fail(FS_ERR_UNSUPPORTED,
+                "fs_slice_fwd_noalloc: this problem needs %zu bytes of scratch, the static "
+                "scratch holds %zu; use fs_slice_fwd with a workspace",
+                s.total, (size_t)FS_NOALLOC_SCRATCH_BYTES);
+  float* base = nullptr;
+  FS_CHECK(noalloc_scratch(&base));
+  cudaStream_t st = (cudaStream_t)stream;
+  Params q = base_params(*p, s, weight, bias, tau);
+  q.x = pt(x_mid);
+  q.v = pt(fx_mid);
+  q.partA = at(base, s.partA);
+  q.partS = at(base, s.partS);
+  FS_CHECK(launch_kind(Kind::FusedSliceFwd, *p, s, q, s.Pn, st));
+  FS_TRY(run_reduce(q.partA, z_num, s.BH, 1, s.Pn, p->G * p->DV, s.BH, 1, st));
+  FS_TRY(run_reduce(q.partS, s_out, s.BH, 1, s.Pn, p->G, s.BH, 1, st));
+  return FS_OK;
+}
 
 int fs_version(void) { return FS_ABI_VERSION; }
 

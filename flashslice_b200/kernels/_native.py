@@ -58,6 +58,7 @@ SIGNATURES = {
     "fs_deslice_bwd": (ctypes.c_int, [_PP, _PT, _P, _P, _P, _P, _P, _PT, _PT, _P, _P, _P, _P,
                                       _P, ctypes.c_size_t, _P]),
     "fs_compute_stats": (ctypes.c_int, [_PP, _PT, _P, _P, _P, _P, _P]),
+    "fs_slice_fwd_noalloc": (ctypes.c_int, [_PP, _PT, _PT, _P, _P, _P, _P, _P, _P]),
 }
 
 _lib = None

@@ -156,6 +156,34 @@ FS_API int fs_deslice_bwd(const fs_problem* p, const fs_tensor4* x_mid,
                    float* dtokens, float* dW, float* db, float* dtau,
                    void* workspace, size_t workspace_bytes, void* stream);
 
+/* Slice forward without any device allocation by the caller or the library:
+ * the same results as fs_slice_fwd, with the per-CTA partial sums kept in a
+ * fixed scratch array inside this library instead of a caller workspace.
+ * No counterpart in the reference. For callers that cannot allocate device
+ * memory -- a host that owns and pre-plans all device memory (an engine
+ * plugin, an FFI caller with no device allocator at hand) or a code path
+ * where a cudaMalloc, which may synchronise the device, is not acceptable.
+ *
+ *  - Serves the single-tile family only: family FS_FAMILY_SINGLE, G <= 32,
+ *    D and DV <= 64, flags 0 (no statistics). Problems whose partial sums
+ *    need more than FS_NOALLOC_SCRATCH_BYTES are rejected with
+ *    FS_ERR_UNSUPPORTED; use fs_slice_fwd with a workspace for those.
+ *  - The scratch (FS_NOALLOC_SCRATCH_BYTES) is a static device array: every
+ *    GPU that loads this library holds it until the process exits.
+ *  - The first call on each device looks up the array's device address
+ *    (cudaGetSymbolAddress, with that device current); make that first call
+ *    before any stream capture. No call allocates or frees device memory.
+ *  - All calls share the one scratch array: calls that overlap on the GPU
+ *    (different streams, or different host threads on one device) race and
+ *    give wrong results. Serialise them. Every partial the kernel reads is
+ *    written by the same call first, so nothing needs clearing between calls.
+ */
+#define FS_NOALLOC_SCRATCH_BYTES (8u << 20)
+FS_API int fs_slice_fwd_noalloc(const fs_problem* p, const fs_tensor4* x_mid,
+                                const fs_tensor4* fx_mid, const float* weight,
+                                const float* bias, const float* tau, float* z_num,
+                                float* s, void* stream);
+
 /* Per-point softmax statistics (B,H,2,N) of the slice logits, in
  * stats_mode's form (online or two-pass). */
 FS_API int fs_compute_stats(const fs_problem* p, const fs_tensor4* x_mid,
