@@ -263,6 +263,7 @@ __device__ __forceinline__ void block_logits(float (&lg)[GB], const float* xrow,
     lg[g] = (g0 + g < G) ? (lg[g] + bs[g]) * inv_tau : -INFINITY;
 }
 
+// exp(d) for d = logit - max <= 0, as exp2 of d*log2(e).
 __device__ __forceinline__ float expd(float d) { return exp2f(d * kLog2e); }
 
 // Pairwise (tree) sum of a register array, in a fixed order: v[i] += v[i+s]

@@ -30,8 +30,9 @@ namespace fs {
   const float inv_tau = __frcp_rn(p.tau[h]);                              \
   (void)D; (void)DV; (void)Wb; (void)bb; (void)inv_tau; (void)G; (void)t;
 
-// whole-row softmax of one block (G <= 32): w = exp(lg - m) * (1 / sum)
-__device__ __forceinline__ void row_softmax(const float (&lg)[GB], float (&w)[GB], bool valid) {
+// whole-row softmax of one block (G <= 32): w = exp(lg - m) * (1 / sum);
+// returns the row max m
+__device__ __forceinline__ float row_softmax(const float (&lg)[GB], float (&w)[GB], bool valid) {
   float m = lg[0];
 #pragma unroll
   for (int g = 1; g < GB; ++g) m = fmaxf(m, lg[g]);
@@ -45,12 +46,17 @@ __device__ __forceinline__ void row_softmax(const float (&lg)[GB], float (&w)[GB
   const float r = valid ? __frcp_rn(s) : 0.f;
 #pragma unroll
   for (int g = 0; g < GB; ++g) w[g] *= r;
+  return m;
 }
 
 // dl = w * (dw - sum_g w dw) (the softmax Jacobian, pre-division); returns
-// sum_g dl * lg over the valid slots and leaves dl / tau in dw.
+// sum_g dl * (lg - m) over the valid slots and leaves dl / tau in dw.
+// sum_g dl vanishes exactly, so sum_g dl * lg = sum_g dl * (lg - m); centring
+// on the row max m keeps a common offset of the logits from multiplying the
+// rounding residue of sum_g dl into the temperature gradient.
 __device__ __forceinline__ float row_jacobian(const float (&w)[GB], float (&dw)[GB],
-                                              const float (&lg)[GB], float inv_tau, int G) {
+                                              const float (&lg)[GB], float m, float inv_tau,
+                                              int G) {
   float tmp[GB];
 #pragma unroll
   for (int g = 0; g < GB; ++g) tmp[g] = w[g] * dw[g];
@@ -58,7 +64,7 @@ __device__ __forceinline__ float row_jacobian(const float (&w)[GB], float (&dw)[
 #pragma unroll
   for (int g = 0; g < GB; ++g) {
     const float dl = w[g] * (dw[g] - gs);
-    tmp[g] = g < G ? dl * lg[g] : 0.f;
+    tmp[g] = g < G ? dl * (lg[g] - m) : 0.f;
     dw[g] = dl * inv_tau;
   }
   return tree_sum(tmp);
@@ -151,12 +157,12 @@ __global__ void __launch_bounds__(NT) k_fused_slice_bwd(Params p) {
     __syncthreads();
     float lg[GB], w[GB], dw[GB];
     block_logits(lg, xs + t * L.xrs, Ws, bs, L.dt, inv_tau, 0, G);
-    row_softmax(lg, w, n0 + t < N);
+    const float mrow = row_softmax(lg, w, n0 + t < N);
     // dw = fx . dz_num^T + ds  (slice_ops.py:695)
     row_dots(dw, vs + t * L.vrs, Ms, L.dvt, L.dvt);
 #pragma unroll
     for (int g = 0; g < GB; ++g) dw[g] += dss[g];
-    dt_acc += row_jacobian(w, dw, lg, inv_tau, G);
+    dt_acc += row_jacobian(w, dw, lg, mrow, inv_tau, G);
     // dfx = w @ dz_num, written over this point's fx row (slice_ops.py:690)
     row_axpy(vs + t * L.vrs, w, Ms, L.dvt, L.dvt, 1.f, true);
     row_put(us + t * L.ars, dw);
@@ -198,10 +204,10 @@ __global__ void __launch_bounds__(NT) k_fused_deslice_bwd(Params p) {
     __syncthreads();
     float lg[GB], w[GB], dw[GB];
     block_logits(lg, xs + t * L.xrs, Ws, bs, L.dt, inv_tau, 0, G);
-    row_softmax(lg, w, n0 + t < N);
+    const float mrow = row_softmax(lg, w, n0 + t < N);
     // dw = d_out . tokens^T  (slice_ops.py:760)
     row_dots(dw, vs + t * L.vrs, Ms, L.dvt, L.dvt);
-    dt_acc += row_jacobian(w, dw, lg, inv_tau, G);
+    dt_acc += row_jacobian(w, dw, lg, mrow, inv_tau, G);
     row_put(as + t * L.ars, w);
     row_put(us + t * L.ars, dw);
     __syncthreads();
@@ -462,7 +468,7 @@ __global__ void __launch_bounds__(NT) k_blk_bwd_n(Params p) {
         const float e = expd(lg[g] - m);
         const float dwg = SLICE ? dw[g] + dss[g] : dw[g];
         const float dl = (e * dwg - e * delta) * inv_l;
-        lg[g] = g0 + g < G ? dl * lg[g] : 0.f;
+        lg[g] = g0 + g < G ? dl * (lg[g] - m) : 0.f;  // centred, see row_jacobian
         dw[g] = dl;
       }
       rdt += tree_sum(lg);
