@@ -7,6 +7,7 @@
 
 #include "flashslice_b200.h"
 #include "fs_launch.h"
+#include "fs_tc_launch.h"
 
 using namespace fs;
 
@@ -59,7 +60,55 @@ int check_problem(const fs_problem* p) {
     return fail(FS_ERR_SHAPE, "bias has (batch, heads) = (%d, %d), x_mid has (%lld, %lld)",
                 p->b_batch, p->b_heads, (long long)p->B, (long long)p->H);
   if (p->flags < 0 || p->flags > 3) return fail(FS_ERR_ARGUMENT, "bad flags %d", p->flags);
+  if (p->engine != FS_ENGINE_AUTO && p->engine != FS_ENGINE_FMA)
+    return fail(FS_ERR_ARGUMENT, "bad engine %d", p->engine);
   return FS_OK;
+}
+
+// ---------------------------------------------------------------- tensor-core path
+// The tcgen05 kernels serve the single-tile family for fp32 point tensors
+// with D = DV = G = 32 whose rows TMA can address. Their CTA count per
+// (b, h) is a function of the shape only (148 SMs of a B200 as a constant),
+// so results stay bitwise reproducible.
+constexpr int kSmCount = 148;
+
+bool tc_tensor_ok(const fs_tensor4* t) {
+  if (!t || t->stride[3] != 1 || ((uintptr_t)t->data & 15)) return false;
+  for (int i = 0; i < 3; ++i)
+    if (t->stride[i] <= 0 || (t->stride[i] & 3)) return false;
+  return true;
+}
+
+bool tc_shape(const fs_problem& p) {
+  return p.engine == FS_ENGINE_AUTO && p.family == FS_FAMILY_SINGLE && p.act_dtype == FS_F32 &&
+         p.D == 32 && p.DV == 32 && p.G == 32 && p.N >= 1;
+}
+
+// Fill the tensor-core parameters; false when a tensor map cannot be made
+// (the FMA kernels then serve the call).
+bool tc_params(const fs_problem& p, tcx::TcKind k, const fs_tensor4* x, const fs_tensor4* v,
+               const float* W, const float* bias, const float* tau, tcx::TcParams& q) {
+  q = tcx::TcParams();
+  if (!tcx::make_point_map(&q.mx, x->data, p.B, p.N, p.H, x->stride)) return false;
+  if (v && !tcx::make_point_map(&q.mv, v->data, p.B, p.N, p.H, v->stride)) return false;
+  q.status = tcx::device_status();
+  if (!q.status) return false;
+  q.B = (int)p.B;
+  q.N = (int)p.N;
+  q.H = (int)p.H;
+  q.ntiles = (int)((p.N + 127) / 128);
+  const int64_t BH = p.B * p.H;
+  int64_t P = (tcx::tc_ctas_per_sm(k) * kSmCount + BH - 1) / BH;
+  if (P > q.ntiles) P = q.ntiles;
+  q.P = (int)(P < 1 ? 1 : P);
+  q.W = W;
+  q.bias = bias;
+  q.tau = tau;
+  q.swb = p.w_batch > 1 ? (int64_t)p.w_heads * p.G * p.D : 0;
+  q.swh = p.w_heads > 1 ? p.G * p.D : 0;
+  q.sbb = p.b_batch > 1 ? (int64_t)p.b_heads * p.G : 0;
+  q.sbh = p.b_heads > 1 ? p.G : 0;
+  return true;
 }
 
 struct Setup {
@@ -277,6 +326,21 @@ const char* fs_last_error(void) { return g_err.c_str(); }
 
 uint64_t fs_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
+uint64_t fs_tc_launch_count(void) { return tcx::g_tc_launches.load(std::memory_order_relaxed); }
+
+int fs_device_status(int reset) {
+  int* word = tcx::device_status();
+  if (!word) return -1;
+  if (cudaDeviceSynchronize() != cudaSuccess) return -2;
+  int v = 0;
+  if (cudaMemcpy(&v, word, sizeof v, cudaMemcpyDeviceToHost) != cudaSuccess) return -3;
+  if (reset) {
+    const int zero = 0;
+    if (cudaMemcpy(word, &zero, sizeof zero, cudaMemcpyHostToDevice) != cudaSuccess) return -4;
+  }
+  return v;
+}
+
 size_t fs_workspace_bytes(int op, const fs_problem* p) {
   if (check_problem(p) != FS_OK) return 0;
   return setup(op, *p).total;
@@ -318,7 +382,15 @@ int fs_slice_fwd(const fs_problem* p, const fs_tensor4* x_mid, const fs_tensor4*
   q.partA = at(workspace, s.partA);
   q.partS = at(workspace, s.partS);
   int P;
-  if (s.fused) {
+  tcx::TcParams tq;
+  if (s.fused && tc_shape(*p) && tc_tensor_ok(x_mid) && tc_tensor_ok(fx_mid) &&
+      tc_params(*p, tcx::TcKind::SliceFwd, x_mid, fx_mid, weight, bias, tau, tq)) {
+    // the partial buffers sized for the FMA kernels hold the (fewer) tensor-core CTAs'
+    tq.partA = q.partA;
+    tq.partS = q.partS;
+    P = tq.P;
+    FS_TRY(tcx::run_tc(tcx::TcKind::SliceFwd, tq, st));
+  } else if (s.fused) {
     P = s.Pn;
     FS_CHECK(launch_kind(Kind::FusedSliceFwd, *p, s, q, P, st));
   } else {
@@ -359,6 +431,15 @@ int fs_deslice_fwd(const fs_problem* p, const fs_tensor4* x_mid, const float* we
   q.x = pt(x_mid);
   q.o1 = pt(out);
   q.M = tokens;
+  tcx::TcParams tq;
+  if (s.fused && tc_shape(*p) && tc_tensor_ok(x_mid) && tc_tensor_ok(out) &&
+      tc_params(*p, tcx::TcKind::DesliceFwd, x_mid, nullptr, weight, bias, tau, tq)) {
+    tq.M = tokens;
+    tq.out = (float*)out->data;
+    for (int i = 0; i < 4; ++i) tq.so[i] = out->stride[i];
+    FS_TRY(tcx::run_tc(tcx::TcKind::DesliceFwd, tq, st));
+    return FS_OK;
+  }
   if (s.fused) return launch_kind(Kind::FusedDesliceFwd, *p, s, q, s.Pn, st);
   if (stats_in) {
     q.stats_in = stats_in;

@@ -1,0 +1,54 @@
+// flashslice_b200 -- host-side view of the tensor-core kernels
+// (fs_tc_kernels.cu): parameters, kinds, TMA tensor maps.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <atomic>
+
+namespace fs {
+namespace tcx {
+
+enum class TcKind { SliceFwd, DesliceFwd, SliceBwd, DesliceBwd };
+
+struct TcParams {
+  CUtensorMap mx;  // x_mid: (32, H, N, B) fp32 tiles of 128 points
+  CUtensorMap mv;  // fx_mid or d_out, same shape
+  int B, N, H, P, ntiles;
+  const float* W;
+  const float* bias;
+  const float* tau;
+  int64_t swb, swh, sbb, sbh;
+  const float* M;   // tokens or dz_num (B, H, 32, 32)
+  const float* ds;  // (B, H, 32)
+  float* out;       // deslice out / dx_mid (B, N, H, 32), element strides so
+  int64_t so[4];
+  float* out2;      // dfx_mid
+  int64_t so2[4];
+  float* partA;
+  float* partB;
+  float* partS;
+  float* partDt;
+  int* status;      // device word: set to a non-zero code when a bounded wait gives up
+};
+
+cudaError_t run_tc(TcKind k, const TcParams& p, cudaStream_t s);
+
+// tensor-core kernels launched (also counted in fs::g_launches)
+extern std::atomic<uint64_t> g_tc_launches;
+int tc_ctas_per_sm(TcKind k);
+
+// TMA map over a strided fp32 (B, N, H, 32) point tensor with 128-point
+// boxes and 128-byte swizzle. False when the layout is not TMA-addressable
+// (width stride != 1, unaligned base or strides) or the driver entry point is
+// missing.
+bool make_point_map(CUtensorMap* map, const void* data, int64_t B, int64_t N, int64_t H,
+                    const int64_t stride[4]);
+
+// Address of this library's device status word on the current device.
+int* device_status();
+
+}  // namespace tcx
+}  // namespace fs

@@ -34,7 +34,7 @@ class Problem(ctypes.Structure):
     _fields_ = [("B", _I64), ("N", _I64), ("H", _I64), ("D", _I64), ("DV", _I64), ("G", _I64),
                 ("act_dtype", _I32), ("dot", _I32), ("family", _I32), ("stats_mode", _I32),
                 ("w_batch", _I32), ("w_heads", _I32), ("b_batch", _I32), ("b_heads", _I32),
-                ("flags", _I32), ("reserved", _I32)]
+                ("flags", _I32), ("engine", _I32)]
 
 
 class Tensor4(ctypes.Structure):
@@ -59,7 +59,12 @@ SIGNATURES = {
                                       _P, ctypes.c_size_t, _P]),
     "fs_compute_stats": (ctypes.c_int, [_PP, _PT, _P, _P, _P, _P, _P]),
     "fs_slice_fwd_noalloc": (ctypes.c_int, [_PP, _PT, _PT, _P, _P, _P, _P, _P, _P]),
+    "fs_device_status": (ctypes.c_int, [ctypes.c_int]),
+    "fs_tc_launch_count": (ctypes.c_uint64, []),
 }
+
+ENGINE_AUTO, ENGINE_FMA = 0, 1
+ENGINES = {"auto": ENGINE_AUTO, "fma": ENGINE_FMA}
 
 _lib = None
 _lock = threading.Lock()

@@ -236,7 +236,7 @@ class _Call:
         Bw, Hw, Bb, Hb = self.ext
         self.prob = nat.Problem(B, N, H, D, dv, self.G, nat.DTYPE_CODE[pdtype], int(dot), family,
                                 1 if _state.stats_mode == "two-pass" else 0, Bw, Hw, Bb, Hb,
-                                flags, 0)
+                                flags, nat.ENGINES[_state.engine])
         self.device = x_mid.device
 
     def workspace(self, op):

@@ -94,8 +94,15 @@ typedef struct fs_problem {
   int32_t b_batch, b_heads; /* bias leading extents: 1 or B, 1 or H            */
   int32_t flags;       /* FS_FLAG_* : which optional statistics buffers the
                           call passes; part of the workspace size contract    */
-  int32_t reserved;    /* 0 */
+  int32_t engine;      /* FS_ENGINE_*: 0 lets the library choose */
 } fs_problem;
+
+/* Engine selection. FS_ENGINE_AUTO runs the tensor-core kernels where they
+ * serve the problem (single-tile family, fp32, D = DV = G = 32, TMA-friendly
+ * strides) and the exact-fp32 FMA kernels elsewhere; FS_ENGINE_FMA forces the
+ * FMA kernels (every product an fp32 FMA). Both meet the ieee contract. */
+#define FS_ENGINE_AUTO 0
+#define FS_ENGINE_FMA 1
 
 #define FS_FLAG_STATS_IN 1  /* stats_in is given (non-NULL)   */
 #define FS_FLAG_STATS_OUT 2 /* stats_out is given (non-NULL)  */
@@ -115,6 +122,16 @@ FS_API const char* fs_last_error(void);
  * devices and threads); a diagnostic for benchmarks, no reference
  * counterpart. */
 FS_API uint64_t fs_launch_count(void);
+
+/* Of those, the tensor-core (tcgen05) kernels. Diagnostic, no reference
+ * counterpart. */
+FS_API uint64_t fs_tc_launch_count(void);
+
+/* The current device's status word: 0, or the code of the first bounded
+ * device-side wait that gave up (1) or a misaligned shared window (2) since
+ * the last reset. Synchronises the device; clears the word when reset != 0.
+ * A diagnostic of this library, no reference counterpart. */
+FS_API int fs_device_status(int reset);
 
 /* Bytes of workspace `op` needs for problem `p` (0 when it needs none). */
 FS_API size_t fs_workspace_bytes(int op, const fs_problem* p);

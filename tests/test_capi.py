@@ -41,7 +41,7 @@ def test_struct_layout_matches_header():
 
 def prob(**kw):
     d = dict(B=1, N=1000, H=2, D=32, DV=32, G=32, act_dtype=0, dot=0, family=0, stats_mode=0,
-             w_batch=1, w_heads=1, b_batch=1, b_heads=1, flags=0, reserved=0)
+             w_batch=1, w_heads=1, b_batch=1, b_heads=1, flags=0, engine=0)
     d.update(kw)
     return nat.Problem(**d)
 

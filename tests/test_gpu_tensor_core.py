@@ -1,0 +1,92 @@
+"""The tensor-core (tcgen05) kernels against the exact-fp32 FMA kernels and
+the float64 truth, on the shapes they serve (fp32, D = DV = G = 32), with
+ragged point counts, strided inputs and every weight layout; plus proof that
+the tensor-core path actually ran and that no bounded device wait gave up."""
+
+import pytest
+import torch
+
+from parity import relerr
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def env(cuda_device):
+    torch.backends.cuda.matmul.allow_tf32 = False
+    import flashslice_b200.kernels as K
+    from flashslice_b200.kernels import _native as nat
+    from flashslice_b200.kernels import _state
+    lib = nat.load()
+    lib.fs_device_status(1)
+    return K, _state, lib
+
+
+def _inputs(N, mode, B=1, H=4, seed=3, strided=False):
+    g = torch.Generator().manual_seed(seed)
+    r = lambda *s: torch.randn(*s, generator=g, dtype=torch.float64)  # noqa: E731
+    x, fx = r(B, N, H, 32), r(B, N, H, 32)
+    if strided:
+        x = x.permute(0, 2, 1, 3).contiguous().permute(0, 2, 1, 3)
+    W = {"gd": r(32, 32), "hgd": r(H, 32, 32), "bhgd": r(B, H, 32, 32)}[mode] / 32 ** 0.5
+    b = {"gd": r(32), "hgd": r(H, 32), "bhgd": r(B, H, 32)}[mode] * 0.1
+    tau = 0.3 + 0.7 * torch.rand(H, generator=g, dtype=torch.float64)
+    tok = r(B, H, 32, 32)
+    return [t.cuda() for t in (x, fx, W, b, tau, tok)]
+
+
+def _run(K, st, engine, x, fx, W, b, tau, tok):
+    st.set_engine(engine)
+    try:
+        f = [t.float() for t in (x, fx, W, b, tau, tok)]  # .float() keeps x's strides
+        z, s = K.fused_slice(f[0], f[1], f[2], f[3], f[4])
+        out = K.fused_deslice(f[0], f[2], f[3], f[4], f[5])
+        torch.cuda.synchronize()
+        return z, s, out
+    finally:
+        st.set_engine("auto")
+
+
+@pytest.mark.parametrize("N", [1, 77, 128, 129, 4097, 100_003])
+@pytest.mark.parametrize("mode", ["gd", "hgd", "bhgd"])
+def test_forward_matches_exact_engine(env, N, mode):
+    K, st, lib = env
+    x, fx, W, b, tau, tok = _inputs(N, mode, B=2 if mode == "bhgd" else 1)
+    n0 = lib.fs_tc_launch_count()
+    tc = _run(K, st, "auto", x, fx, W, b, tau, tok)
+    assert lib.fs_tc_launch_count() - n0 == 2, "the tensor-core kernels did not run"
+    n1 = lib.fs_tc_launch_count()
+    ex = _run(K, st, "fma", x, fx, W, b, tau, tok)
+    assert lib.fs_tc_launch_count() == n1
+    from oracle import eager_torch as E
+    z64, s64 = E.slice_fwd(x, fx, W, b, tau)
+    o64 = E.deslice_fwd(x, W, b, tau, tok)
+    for name, a, e, ref in (("z_num", tc[0], ex[0], z64), ("s", tc[1], ex[1], s64),
+                            ("out", tc[2], ex[2], o64)):
+        et, ee = relerr(a, ref), relerr(e, ref)
+        # the tensor-core split products are at least as accurate as fp32 FMA
+        assert et <= max(2.0 * ee, 1e-6), (name, et, ee)
+        assert relerr(a, e) <= 1e-5, (name, relerr(a, e))
+    assert lib.fs_device_status(1) == 0
+
+
+def test_forward_strided_input(env):
+    K, st, lib = env
+    x, fx, W, b, tau, tok = _inputs(5000, "hgd", B=2, strided=True)
+    assert not x.is_contiguous()
+    n0 = lib.fs_tc_launch_count()
+    tc = _run(K, st, "auto", x, fx, W, b, tau, tok)
+    assert lib.fs_tc_launch_count() - n0 == 2
+    ex = _run(K, st, "fma", x, fx, W, b, tau, tok)
+    for a, e in zip(tc, ex):
+        assert relerr(a, e) <= 1e-5
+    assert lib.fs_device_status(1) == 0
+
+
+def test_forward_deterministic(env):
+    K, st, lib = env
+    x, fx, W, b, tau, tok = _inputs(300_000, "hgd", B=1, H=8)
+    a = _run(K, st, "auto", x, fx, W, b, tau, tok)
+    c = _run(K, st, "auto", x, fx, W, b, tau, tok)
+    for u, v in zip(a, c):
+        assert torch.equal(u, v)
