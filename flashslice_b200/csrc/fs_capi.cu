@@ -79,6 +79,29 @@ bool tc_tensor_ok(const fs_tensor4* t) {
   return true;
 }
 
+// FLASHSLICE_B200_DEBUG=1: report each op's engine choice on stderr
+bool debug_routes() {
+  static const int on = [] {
+    const char* v = getenv("FLASHSLICE_B200_DEBUG");
+    return v && v[0] == '1' ? 1 : 0;
+  }();
+  return on != 0;
+}
+
+void route_note(const char* op, const char* engine, const fs_problem& p, const fs_tensor4* a,
+                const fs_tensor4* b2) {
+  if (!debug_routes()) return;
+  fprintf(stderr, "[flashslice_b200] %s -> %s (B=%lld N=%lld H=%lld D=%lld DV=%lld G=%lld "
+          "dtype=%d family=%d engine=%d", op, engine, (long long)p.B, (long long)p.N,
+          (long long)p.H, (long long)p.D, (long long)p.DV, (long long)p.G, p.act_dtype, p.family,
+          p.engine);
+  for (const fs_tensor4* t : {a, b2})
+    if (t)
+      fprintf(stderr, " [%p %lld %lld %lld %lld]", t->data, (long long)t->stride[0],
+              (long long)t->stride[1], (long long)t->stride[2], (long long)t->stride[3]);
+  fprintf(stderr, ")\n");
+}
+
 bool tc_shape(const fs_problem& p) {
   return p.engine == FS_ENGINE_AUTO && p.family == FS_FAMILY_SINGLE && p.act_dtype == FS_F32 &&
          p.D == 32 && p.DV == 32 && p.G == 32 && p.N >= 1;
@@ -89,10 +112,19 @@ bool tc_shape(const fs_problem& p) {
 bool tc_params(const fs_problem& p, tcx::TcKind k, const fs_tensor4* x, const fs_tensor4* v,
                const float* W, const float* bias, const float* tau, tcx::TcParams& q) {
   q = tcx::TcParams();
-  if (!tcx::make_point_map(&q.mx, x->data, p.B, p.N, p.H, x->stride)) return false;
-  if (v && !tcx::make_point_map(&q.mv, v->data, p.B, p.N, p.H, v->stride)) return false;
+  if (!tcx::make_point_map(&q.mx, x->data, p.B, p.N, p.H, x->stride)) {
+    if (debug_routes()) fprintf(stderr, "[flashslice_b200] tensor map of x_mid refused\n");
+    return false;
+  }
+  if (v && !tcx::make_point_map(&q.mv, v->data, p.B, p.N, p.H, v->stride)) {
+    if (debug_routes()) fprintf(stderr, "[flashslice_b200] tensor map of the value tensor refused\n");
+    return false;
+  }
   q.status = tcx::device_status();
-  if (!q.status) return false;
+  if (!q.status) {
+    if (debug_routes()) fprintf(stderr, "[flashslice_b200] no device status word\n");
+    return false;
+  }
   q.B = (int)p.B;
   q.N = (int)p.N;
   q.H = (int)p.H;
@@ -389,9 +421,11 @@ int fs_slice_fwd(const fs_problem* p, const fs_tensor4* x_mid, const fs_tensor4*
     tq.partA = q.partA;
     tq.partS = q.partS;
     P = tq.P;
+    route_note("slice_fwd", "tensor-core", *p, x_mid, fx_mid);
     FS_TRY(tcx::run_tc(tcx::TcKind::SliceFwd, tq, st));
   } else if (s.fused) {
     P = s.Pn;
+    route_note("slice_fwd", "fma-fused", *p, x_mid, fx_mid);
     FS_CHECK(launch_kind(Kind::FusedSliceFwd, *p, s, q, P, st));
   } else {
     const float* stats = stats_in;
@@ -437,9 +471,11 @@ int fs_deslice_fwd(const fs_problem* p, const fs_tensor4* x_mid, const float* we
     tq.M = tokens;
     tq.out = (float*)out->data;
     for (int i = 0; i < 4; ++i) tq.so[i] = out->stride[i];
+    route_note("deslice_fwd", "tensor-core", *p, x_mid, out);
     FS_TRY(tcx::run_tc(tcx::TcKind::DesliceFwd, tq, st));
     return FS_OK;
   }
+  route_note("deslice_fwd", s.fused ? "fma-fused" : "fma-blocked", *p, x_mid, out);
   if (s.fused) return launch_kind(Kind::FusedDesliceFwd, *p, s, q, s.Pn, st);
   if (stats_in) {
     q.stats_in = stats_in;
@@ -496,9 +532,35 @@ static int bwd_common(bool slice, const fs_problem* p, const fs_tensor4* x_mid,
   if (!slice) q.partB = at(workspace, s.partB);
   q.partS = at(workspace, s.partS);
   q.partDt = at(workspace, s.partDt);
-  int Pw;
-  if (s.fused) {
+  int Pw, Pdt = s.Pn;
+  tcx::TcParams tq;
+  if (s.fused && tc_shape(*p) && tc_tensor_ok(x_mid) && tc_tensor_ok(vals) &&
+      tc_tensor_ok(dx) && (!slice || tc_tensor_ok(dfx)) &&
+      tc_params(*p, slice ? tcx::TcKind::SliceBwd : tcx::TcKind::DesliceBwd, x_mid, vals, weight,
+                bias, tau, tq)) {
+    // the partial buffers sized for the FMA kernels hold the (fewer) tensor-core CTAs'
+    tq.M = mat;
+    tq.ds = ds;
+    tq.out = (float*)dx->data;
+    for (int i = 0; i < 4; ++i) tq.so[i] = dx->stride[i];
+    if (slice) {
+      tq.out2 = (float*)dfx->data;
+      for (int i = 0; i < 4; ++i) tq.so2[i] = dfx->stride[i];
+    }
+    tq.partA = q.partA;
+    tq.partB = q.partB;
+    tq.partS = q.partS;
+    tq.partDt = q.partDt;
+    Pw = Pdt = tq.P;
+    route_note(slice ? "slice_bwd" : "deslice_bwd", "tensor-core", *p, x_mid, vals);
+    FS_TRY(tcx::run_tc(slice ? tcx::TcKind::SliceBwd : tcx::TcKind::DesliceBwd, tq, st));
+  } else if (s.fused) {
     Pw = s.Pn;
+    if (debug_routes())
+      fprintf(stderr, "[flashslice_b200] shape %d x %d vals %d dx %d dfx %d\n", (int)tc_shape(*p),
+              (int)tc_tensor_ok(x_mid), (int)tc_tensor_ok(vals), (int)tc_tensor_ok(dx),
+              (int)(!slice || tc_tensor_ok(dfx)));
+    route_note(slice ? "slice_bwd" : "deslice_bwd", "fma-fused", *p, x_mid, dx);
     FS_CHECK(launch_kind(slice ? Kind::FusedSliceBwd : Kind::FusedDesliceBwd, *p, s, q, Pw, st));
   } else {
     const float* stats = stats_in;
@@ -517,7 +579,7 @@ static int bwd_common(bool slice, const fs_problem* p, const fs_tensor4* x_mid,
   FS_TRY(run_reduce(q.partA, dW, B, H, Pw, p->G * p->D, p->w_batch, p->w_heads, st));
   FS_TRY(run_reduce(q.partS, db, B, H, Pw, p->G, p->b_batch, p->b_heads, st));
   if (!slice) FS_TRY(run_reduce(q.partB, dtok, BH, 1, Pw, p->G * p->DV, BH, 1, st));
-  FS_TRY(run_reduce(q.partDt, dtau, B, H, s.Pn, 1, 1, H, st));
+  FS_TRY(run_reduce(q.partDt, dtau, B, H, Pdt, 1, 1, H, st));
   return FS_OK;
 }
 

@@ -585,6 +585,10 @@ static cudaError_t launch(K kernel, dim3 grid, int nt, const Params& p, cudaStre
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)bytes);
   if (e != cudaSuccess) return e;
+  // the full shared carveout, so that as many CTAs as fit are resident
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                           cudaSharedmemCarveoutMaxShared);
+  if (e != cudaSuccess) return e;
   kernel<<<grid, nt, bytes, s>>>(p);
   g_launches.fetch_add(1, std::memory_order_relaxed);
   return cudaGetLastError();

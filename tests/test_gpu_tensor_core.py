@@ -90,3 +90,54 @@ def test_forward_deterministic(env):
     c = _run(K, st, "auto", x, fx, W, b, tau, tok)
     for u, v in zip(a, c):
         assert torch.equal(u, v)
+
+
+def _round(K, st, engine, leaves, r):
+    """slice -> normalise -> deslice, forward and backward of sum(out * r)."""
+    st.set_engine(engine)
+    try:
+        L = [t.detach().float().requires_grad_(True) for t in leaves]
+        x, fx, W, b, tau = L
+        z, s = K.fused_slice(x, fx, W, b, tau)
+        out = K.fused_deslice(x, W, b, tau, z / (s + 1e-5)[..., None])
+        out.backward(r.float())
+        torch.cuda.synchronize()
+        res = {"out": out.detach(), "z_num": z.detach(), "s": s.detach()}
+        for k, v in zip(("x", "fx", "W", "b", "tau"), L):
+            res["grad:" + k] = v.grad
+        return res
+    finally:
+        st.set_engine("auto")
+
+
+@pytest.mark.parametrize("N", [77, 4097, 100_003])
+@pytest.mark.parametrize("mode", ["gd", "hgd", "bhgd"])
+def test_round_matches_exact_engine(env, N, mode):
+    """Forward and backward of a coupling round on the tensor-core kernels
+    against the exact FMA kernels and the float64 eager reference."""
+    K, st, lib = env
+    x, fx, W, b, tau, _ = _inputs(N, mode, B=2 if mode == "bhgd" else 1)
+    r = torch.randn(x.shape, generator=torch.Generator().manual_seed(9),
+                    dtype=torch.float64).cuda()
+    n0 = lib.fs_tc_launch_count()
+    tc = _round(K, st, "auto", (x, fx, W, b, tau), r)
+    assert lib.fs_tc_launch_count() - n0 == 4, "the tensor-core kernels did not run"
+    ex = _round(K, st, "fma", (x, fx, W, b, tau), r)
+    from oracle import eager_torch as E
+    L = [t.detach().clone().requires_grad_(True) for t in (x, fx, W, b, tau)]
+    ref = E.coupling_round(*L, r)
+    for k in ref:
+        et, ee = relerr(tc[k], ref[k]), relerr(ex[k], ref[k])
+        assert relerr(tc[k], ex[k]) <= 1e-5 or et <= 1.25 * ee + 1e-6, (k, et, ee)
+    assert lib.fs_device_status(1) == 0
+
+
+def test_round_deterministic(env):
+    K, st, lib = env
+    x, fx, W, b, tau, _ = _inputs(200_000, "hgd", B=1, H=8)
+    r = torch.randn(x.shape, generator=torch.Generator().manual_seed(2),
+                    dtype=torch.float64).cuda()
+    a = _round(K, st, "auto", (x, fx, W, b, tau), r)
+    c = _round(K, st, "auto", (x, fx, W, b, tau), r)
+    for k in a:
+        assert torch.equal(a[k], c[k]), k
