@@ -3,19 +3,23 @@
 // accumulators), tcgen05.commit / ld, and the shared-memory and instruction
 // descriptors of the canonical no-swizzle operand layouts.
 //
-// Every wait is bounded: after kSpinLimit polls it records an error code in
-// the kernel's status word and returns false, so that a lost arrival ends
-// the kernel instead of hanging the GPU.
+// Every wait is bounded: after kWaitNs it records an error code in the
+// kernel's status word and returns false, so that a lost arrival ends the
+// kernel instead of hanging the GPU.
 #pragma once
 
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
 namespace fs {
 namespace tc {
 
-constexpr long kSpinLimit = 1L << 26;  // ~1 s of polling
+// A bounded wait gives up after this long (ns of %globaltimer); a poll of
+// mbarrier.try_wait suspends the thread for microseconds, so the count of
+// polls says little about the time waited.
+constexpr uint64_t kWaitNs = 2000000000ull;
 
 enum : int { kErrNone = 0, kErrTimeout = 1 };
 
@@ -52,11 +56,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
 // Wait for the phase with the given parity to complete; false (and *status
-// set) if it does not within kSpinLimit polls.
+// set) if it does not within kWaitNs.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status) {
-  for (long i = 0; i < kSpinLimit; ++i)
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 0; i < (1u << 30); ++i) {
     if (mbar_try_wait(bar, parity)) return true;
+    if (globaltimer_ns() - t0 > kWaitNs) break;
+  }
   if (status) atomicExch(status, kErrTimeout);
   return false;
 }

@@ -2,38 +2,57 @@
 // for the hot shape: fp32 point tensors, D = DV = G = 32.
 //
 // Every product is formed on the tensor cores from an exact three-way bf16
-// split of each fp32 operand, x = hi + mid + lo (8 + 8 + 8 significant bits):
-// all nine partial products are formed, each exact in the fp32 accumulator,
-// so the result differs from an exact-arithmetic dot only by the
-// accumulation's rounding. The parts are stacked so that one MMA forms
-// several partial products at once:
-//  * "wide" products (M = the 128 points of a tile): the small operand's
-//    parts are stacked along N ([B_hi | B_mid | B_lo], N = 96) and the three
-//    parts of the point operand are accumulated into them one after the
-//    other (lo, mid, hi: the tensor core truncates when it adds to its
-//    accumulator, so the small terms go first); the three column groups are
-//    added in registers.
-//  * "pool" products (sums over the tile's points, M = slots): the slot
-//    operand's parts are stacked along M ([A_lo; A_mid; A_hi; 0], M = 128)
-//    and the point operand's along N ([B_lo | B_mid | B_hi (| 1)], N = 96 or
-//    112 with a ones column for the plain sums s and db): one MMA per 16
-//    points; each warp reads one A part's 32 slots and adds its column
-//    groups, and the per-tile pool is drained into fp32 registers with
-//    round-to-nearest adds before the next tile.
+// split of each fp32 operand, x = hi + mid + lo (8 + 8 + 8 significant bits);
+// each partial product is exact in the fp32 accumulator, so the result
+// differs from an exact-arithmetic dot only by the accumulation's rounding.
+// The tensor core truncates when it adds to its accumulator, so small terms
+// go first everywhere.
 //
-// One CTA = one warpgroup (128 threads); thread t owns point row t of a
-// 128-point tile and TMEM lane t. Tiles arrive by TMA (128B swizzle) one tile
+// An MMA instruction (M = 128, K = 16) costs about 47 cycles whether N is 32
+// or 96 (measured on this part: N = 32 47, N = 96 48-57, N = 256 127), so the
+// schedules minimise instructions:
+//  * "wide" products (M = the 128 points of a tile, K = 32): with NW = 96 the
+//    small operand's parts are stacked along N ([B_lo | B_mid | B_hi]) and the
+//    point operand's parts lo, mid, hi accumulated one after the other (six
+//    MMAs, all nine partial products); the three column groups are added in
+//    registers. With NW = 32 (where TMEM is short) the six partial products
+//    above the fp32 rounding level (lo*lo, lo*mid and mid*lo are below 2^-26
+//    of the result) go into one 32-column accumulator (twelve MMAs). The
+//    point operand is read from TMEM, where each thread writes its own row: a
+//    tensor-core read of shared memory runs at about 128 bytes per clock.
+//  * "pool" products (sums over the tile's points, M = slots): the slot
+//    operand's parts are stacked along M ([A_lo; A_mid; A_hi; unused], M =
+//    128) and the point operand's along N ([B_lo | B_mid | B_hi], N = 96):
+//    one MMA per 16 points gives all nine part products; the threads of TMEM
+//    lanes 0-95 add the three column groups of their A part, and the per-tile
+//    pool is drained into fp32 registers with round-to-nearest adds before
+//    the next tile. Plain sums (s, db) are added up by the threads that own
+//    the rows.
+//
+// Threads: T threads share each of the 128 point rows of a tile (T = 2 or 4;
+// 128 * T threads per CTA). Warp w serves TMEM lanes 32 (w % 4) .. +31 and
+// the columns [C (w / 4), C (w / 4) + C) of every 32-column result, C = 32 /
+// T; row maxima and sums are combined across the T threads of a row through
+// shared memory. Row arithmetic uses the paired fp32 instructions (two
+// values per instruction). Tiles arrive by TMA (128B swizzle) one tile
 // ahead; one thread issues the MMAs and commits them to an mbarrier.
 //
 // Operand layouts (no swizzle, core matrices of 8 rows x 16 bytes):
-//  * per-point rows are written split into "stacked" buffers: for every group
-//    of 8 points, the lo, mid and hi parts of the 32 values (64 bytes each,
-//    4 core matrices) at +0, +512, +1024, and in 2048-byte groups a fourth
-//    block at +1536 that holds zeros (pool A) or a ones column (pool B). The
-//    same bytes serve as a K-major A operand (M = points, K = 32) and as an
-//    MN-major operand over points (K = points, M or N = 32 per part).
-//  * small operands (W, tokens, dz_num and their transposes, 32 x 32) are
-//    split into one K-major N = 96 buffer: rows 0-31 hi, 32-63 mid, 64-95 lo.
+//  * "stacked" buffers: for every group of 8 rows, the lo, mid and hi parts
+//    of the 32 values (64 bytes each, 4 core matrices) at +0, +512, +1024
+//    (group stride 1536). Point rows stored so serve as an N-stacked MN-major
+//    B operand over points and as an M-stacked MN-major A operand over points;
+//    the latter reads 512 bytes past each group (the next group's lo part, and
+//    a tail after the buffer) into TMEM lanes 96-127, which nothing reads. A
+//    small matrix stored so (rows r) is the N-stacked MN-major operand of its
+//    transpose.
+//  * a point operand in TMEM holds, in its thread's lane, the lo, mid and hi
+//    parts at columns +0, +16, +32 (two bf16 per column, even k low).
+//  * "small" operands (W, tokens, dz_num; 32 x 32, row-major M[r][c]) split
+//    into three K-major parts (rows r, k = c) at +0 (lo), +2048 (mid), +4096
+//    (hi): one N = 96 K-major operand ([B_lo | B_mid | B_hi]), or three
+//    N = 32 ones, and each part is also the MN-major operand of the transpose
+//    (K = r, N = c).
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cudaTypedefs.h>
@@ -51,23 +70,171 @@ namespace tcx {
 using namespace fs::tc;
 
 constexpr int kTile = 128;
-constexpr int kRS3 = 1536;    // stacked buffer, 8-row group stride, three parts
-constexpr int kRS4 = 2048;    // stacked buffer with a fourth (zero or ones) block
-constexpr uint32_t kIdWide = idesc_bf16(128, 96, 0, 0);    // M = points, N = 3 B parts
-constexpr uint32_t kIdPool = idesc_bf16(128, 96, 1, 1);    // M = 4 A parts, N = 3 B parts
-constexpr uint32_t kIdPool1 = idesc_bf16(128, 112, 1, 1);  // ... plus the ones column
+constexpr int kRS = 1536;               // stacked buffer: 8-row group stride
+constexpr int kSplit = 16 * kRS;        // one 128-point tile split (24 KB)
+constexpr int kTail = 512;              // read past an M-stacked operand (ignored)
+constexpr int kSmall = 3 * 2048;        // one 32 x 32 matrix, three parts
+constexpr int kSmallStk = 4 * kRS;      // one 32 x 32 matrix, stacked
+constexpr int kStage = kTile * 128;     // one fp32 TMA tile (16 KB)
+constexpr float kLn2 = 0.6931471805599453f;
+
+constexpr uint32_t kIdPool = idesc_bf16(128, 96, 1, 1);  // M = 4 A parts, N = 3 B parts
+
+// the six partial products of a 32-wide product, small first: (A part, B
+// part) with parts 0 = lo, 1 = mid, 2 = hi
+__host__ __device__ constexpr int part_a(int i) { return i == 0 ? 0 : i == 1 ? 2 : i < 4 ? 1 : 2; }
+__host__ __device__ constexpr int part_b(int i) {
+  return i == 0 ? 2 : i == 1 ? 0 : i == 2 ? 1 : i == 3 ? 2 : i == 4 ? 1 : 2;
+}
+
+// ------------------------------------------------------------ threads
+template <int T>
+struct Th {
+  static constexpr int NT = 128 * T;  // threads per CTA
+  static constexpr int C = 32 / T;    // columns per thread
+  int row, cs, q;
+  uint32_t lane_off;
+  __device__ __forceinline__ Th() {
+    const int w = threadIdx.x >> 5;
+    q = w & 3;
+    cs = w >> 2;
+    row = 32 * q + (threadIdx.x & 31);
+    lane_off = (uint32_t)(32 * q) << 16;
+  }
+};
+
+__device__ __forceinline__ void named_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// Combine one value per thread across the T threads of a row (fixed order).
+// `red` holds T * 128 floats and is not reused until a CTA-wide barrier.
+template <int T, bool MAX>
+__device__ __forceinline__ float row_combine(float v, float* red, const Th<T>& th) {
+  if constexpr (T == 1) {
+    return v;
+  } else {
+    red[th.cs * 128 + th.row] = v;
+    named_sync(1 + th.q, 32 * T);
+    float r[T];
+#pragma unroll
+    for (int c = 0; c < T; ++c) r[c] = red[c * 128 + th.row];
+    if constexpr (MAX) {
+      float m = r[0];
+#pragma unroll
+      for (int c = 1; c < T; ++c) m = fmaxf(m, r[c]);
+      return m;
+    } else {
+      return tree_sum(r);
+    }
+  }
+}
+
+// ------------------------------------------------------------ paired fp32
+__device__ __forceinline__ float2 f2(const float* v, int k) { return make_float2(v[2 * k], v[2 * k + 1]); }
+__device__ __forceinline__ void put2(float* v, int k, float2 x) {
+  v[2 * k] = x.x;
+  v[2 * k + 1] = x.y;
+}
+
+// sum of N values (N even) by pairs, fixed order
+template <int N>
+__device__ __forceinline__ float tree_sum2(const float (&v)[N]) {
+  float2 p[N / 2];
+#pragma unroll
+  for (int k = 0; k < N / 2; ++k) p[k] = f2(v, k);
+#pragma unroll
+  for (int s = N / 4; s > 0; s >>= 1) {
+#pragma unroll
+    for (int i = 0; i < s; ++i) p[i] = __fadd2_rn(p[i], p[i + s]);
+  }
+  return p[0].x + p[0].y;
+}
+
+// ------------------------------------------------------------ TMEM I/O
+template <int N>
+__device__ __forceinline__ void tld(uint32_t a, uint32_t (&r)[N]);
+template <>
+__device__ __forceinline__ void tld<8>(uint32_t a, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+                 "=r"(r[6]), "=r"(r[7])
+               : "r"(a));
+}
+template <>
+__device__ __forceinline__ void tld<16>(uint32_t a, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(a));
+}
+__device__ __forceinline__ void tld_wait() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+template <int N>
+__device__ __forceinline__ void tst(uint32_t a, const uint32_t (&r)[N]);
+template <>
+__device__ __forceinline__ void tst<4>(uint32_t a, const uint32_t (&r)[4]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a),
+               "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3])
+               : "memory");
+}
+template <>
+__device__ __forceinline__ void tst<8>(uint32_t a, const uint32_t (&r)[8]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(a),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+      : "memory");
+}
+__device__ __forceinline__ void tst_wait() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// This thread's C columns of a wide result at taddr (lane included): one
+// 32-column accumulator (NW = 32), or the sum of the three column groups of
+// an N-stacked one (NW = 96; groups x B_lo, x B_mid, x B_hi, added small
+// first).
+template <int NW, int C>
+__device__ __forceinline__ void ld_wide(uint32_t taddr, int cs, float (&v)[C]) {
+  if constexpr (NW == 32) {
+    uint32_t r[C];
+    tld<C>(taddr + cs * C, r);
+    tld_wait();
+#pragma unroll
+    for (int i = 0; i < C; ++i) v[i] = __uint_as_float(r[i]);
+  } else {
+    uint32_t a[C], b[C], c[C];
+    tld<C>(taddr + cs * C, a);
+    tld<C>(taddr + 32 + cs * C, b);
+    tld<C>(taddr + 64 + cs * C, c);
+    tld_wait();
+#pragma unroll
+    for (int k = 0; k < C / 2; ++k) {
+      const float2 s = __fadd2_rn(make_float2(__uint_as_float(a[2 * k]), __uint_as_float(a[2 * k + 1])),
+                                  make_float2(__uint_as_float(b[2 * k]), __uint_as_float(b[2 * k + 1])));
+      put2(v, k, __fadd2_rn(s, make_float2(__uint_as_float(c[2 * k]), __uint_as_float(c[2 * k + 1]))));
+    }
+  }
+}
 
 // ------------------------------------------------------------ row helpers
-// This thread's row of a 128 x 32 fp32 tile loaded by TMA with 128B swizzle.
-__device__ __forceinline__ void read_row(const uint8_t* tile, int t, float (&v)[32]) {
-  const uint8_t* row = tile + t * 128;
+// This thread's C columns of row `row` of a 128 x 32 fp32 tile loaded by TMA
+// with 128B swizzle (16-byte chunk j of row r sits at chunk j ^ (r % 8)).
+template <int C>
+__device__ __forceinline__ void read_cols(const uint8_t* tile, int row, int cs, float (&v)[C]) {
+  const uint8_t* r = tile + row * 128;
 #pragma unroll
-  for (int c = 0; c < 8; ++c) {
-    const float4 q = *(const float4*)(row + ((c ^ (t & 7)) << 4));
-    v[4 * c] = q.x;
-    v[4 * c + 1] = q.y;
-    v[4 * c + 2] = q.z;
-    v[4 * c + 3] = q.w;
+  for (int i = 0; i < C / 4; ++i) {
+    const int j = cs * (C / 4) + i;
+    const float4 f = *(const float4*)(r + ((j ^ (row & 7)) << 4));
+    v[4 * i] = f.x;
+    v[4 * i + 1] = f.y;
+    v[4 * i + 2] = f.z;
+    v[4 * i + 3] = f.w;
   }
 }
 
@@ -75,137 +242,166 @@ __device__ __forceinline__ uint32_t bf2_bits(__nv_bfloat162 v) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
-// Split row t's 32 values into bf16 lo / mid / hi and store them in a stacked
-// buffer with 8-row group stride rs.
-__device__ __forceinline__ void put_row_split(uint8_t* buf, int rs, int t, const float (&v)[32]) {
-  uint8_t* base = buf + (t >> 3) * rs + (t & 7) * 16;
+// (a, c) -> packed bf16 pairs of their hi, mid and lo parts (a in the low
+// half); the residuals are exact, so a = hi + mid + lo exactly
+__device__ __forceinline__ void split_pair(float2 v, uint32_t& hw, uint32_t& mw, uint32_t& lw) {
+  const float2 neg1 = make_float2(-1.f, -1.f);
+  const __nv_bfloat162 h2 = __float22bfloat162_rn(v);
+  const float2 r = __ffma2_rn(__bfloat1622float2(h2), neg1, v);
+  const __nv_bfloat162 m2 = __float22bfloat162_rn(r);
+  const float2 r2 = __ffma2_rn(__bfloat1622float2(m2), neg1, r);
+  hw = bf2_bits(h2);
+  mw = bf2_bits(m2);
+  lw = bf2_bits(__float22bfloat162_rn(r2));
+}
+
+// A row's C values split into packed bf16 pairs of their lo, mid and hi parts
+// (formed once, stored wherever the row serves as an operand).
+template <int C>
+struct Split {
+  uint32_t hw[C / 2], mw[C / 2], lw[C / 2];
+  __device__ __forceinline__ explicit Split(const float (&v)[C]) {
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    uint32_t hw[4], mw[4], lw[4];
+    for (int k = 0; k < C / 2; ++k) split_pair(f2(v, k), hw[k], mw[k], lw[k]);
+  }
+  // into a stacked buffer as row `row`, columns [C cs, C cs + C)
+  __device__ __forceinline__ void to_smem(uint8_t* buf, int row, int cs) const {
+    uint8_t* base = buf + (row >> 3) * kRS + (row & 7) * 16;
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const float a = v[8 * j + 2 * q], c = v[8 * j + 2 * q + 1];
-      const __nv_bfloat162 h2 = __floats2bfloat162_rn(a, c);
-      const float ra = a - __low2float(h2), rc = c - __high2float(h2);
-      const __nv_bfloat162 m2 = __floats2bfloat162_rn(ra, rc);
-      const __nv_bfloat162 l2 =
-          __floats2bfloat162_rn(ra - __low2float(m2), rc - __high2float(m2));
-      hw[q] = bf2_bits(h2);
-      mw[q] = bf2_bits(m2);
-      lw[q] = bf2_bits(l2);
+    for (int i = 0; i < C / 8; ++i) {
+      const int j = cs * (C / 8) + i;
+      *(uint4*)(base + 1024 + j * 128) =
+          make_uint4(hw[4 * i], hw[4 * i + 1], hw[4 * i + 2], hw[4 * i + 3]);
+      *(uint4*)(base + 512 + j * 128) =
+          make_uint4(mw[4 * i], mw[4 * i + 1], mw[4 * i + 2], mw[4 * i + 3]);
+      *(uint4*)(base + j * 128) = make_uint4(lw[4 * i], lw[4 * i + 1], lw[4 * i + 2], lw[4 * i + 3]);
     }
-    *(uint4*)(base + 1024 + j * 128) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-    *(uint4*)(base + 512 + j * 128) = make_uint4(mw[0], mw[1], mw[2], mw[3]);
-    *(uint4*)(base + j * 128) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
   }
-}
+  // into the TMEM point operand at taddr (lane included): parts lo, mid, hi
+  // at +0, +16, +32 columns. The caller waits (tst_wait) before the MMA is
+  // issued.
+  __device__ __forceinline__ void to_tmem(uint32_t taddr, int cs) const {
+    const uint32_t a = taddr + cs * (C / 2);
+    tst<C / 2>(a, lw);
+    tst<C / 2>(a + 16, mw);
+    tst<C / 2>(a + 32, hw);
+  }
+};
 
-// A 32 x 32 fp32 matrix M (row-major, row stride 32) split into the N = 96
-// K-major small operand at dst: operand row n + 32 * part (part 0 hi, 1 mid,
-// 2 lo), column k, is M[n][k], or M[k][n] when transposed.
-__device__ __forceinline__ void put_small_split(uint8_t* dst, const float* M, bool transposed) {
-  for (int i = threadIdx.x; i < 32 * 32; i += 128) {
-    const int n = i >> 5, k = i & 31;
-    const float v = transposed ? M[k * 32 + n] : M[n * 32 + k];
+// A 32 x 32 fp32 matrix M (row-major) split into the three-part small
+// operand at dst: part p (0 lo, 1 mid, 2 hi) at +2048 p, K-major with rows r
+// and k = c.
+template <int NT>
+__device__ __forceinline__ void put_small(uint8_t* dst, const float* M) {
+  for (int i = threadIdx.x; i < 32 * 32; i += NT) {
+    const int r = i >> 5, c = i & 31;
     __nv_bfloat16 h, m, l;
-    split3(v, h, m, l);
-    *(__nv_bfloat16*)(dst + kmajor_off(n, k, 32)) = h;
-    *(__nv_bfloat16*)(dst + kmajor_off(n + 32, k, 32)) = m;
-    *(__nv_bfloat16*)(dst + kmajor_off(n + 64, k, 32)) = l;
+    split3(M[i], h, m, l);
+    const uint32_t o = kmajor_off(r, c, 32);
+    *(__nv_bfloat16*)(dst + o) = l;
+    *(__nv_bfloat16*)(dst + 2048 + o) = m;
+    *(__nv_bfloat16*)(dst + 4096 + o) = h;
   }
 }
 
-// The fourth block of a 2048-stride stacked buffer: zeros (pool A), or the
-// ones column of a pool B (MN-group 12: column 96 = 1, 97-111 = 0).
-__device__ __forceinline__ void init_fourth_block(uint8_t* buf, bool ones) {
-  for (int i = threadIdx.x; i < 16 * 128; i += 128) {
-    const int grp = i >> 7, w = i & 127;  // 128 words of 4 bytes per 8-row group
-    uint32_t v = 0u;
-    if (ones && w < 32 && (w & 3) == 0) v = 0x3F80u;  // element 0 of each 16-byte row
-    *(uint32_t*)(buf + grp * kRS4 + 1536 + w * 4) = v;
+// The same matrix as a stacked buffer over its rows r (the N-stacked MN-major
+// operand of its transpose: K = r, N = part * 32 + c).
+template <int NT>
+__device__ __forceinline__ void put_small_stacked(uint8_t* dst, const float* M) {
+  for (int i = threadIdx.x; i < 32 * 32; i += NT) {
+    const int r = i >> 5, c = i & 31;
+    __nv_bfloat16 h, m, l;
+    split3(M[i], h, m, l);
+    const uint32_t o = (r >> 3) * kRS + (r & 7) * 16 + (c >> 3) * 128 + (c & 7) * 2;
+    *(__nv_bfloat16*)(dst + o) = l;
+    *(__nv_bfloat16*)(dst + 512 + o) = m;
+    *(__nv_bfloat16*)(dst + 1024 + o) = h;
   }
+}
+
+template <int C>
+__device__ __forceinline__ void store_cols(float* rowp, int cs, const float (&v)[C]) {
+#pragma unroll
+  for (int i = 0; i < C / 4; ++i)
+    *(float4*)(rowp + cs * C + 4 * i) =
+        make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
 }
 
 // ------------------------------------------------------------ MMA schedules
-// D (128 x 96) = sum over the point operand's parts (lo, mid, hi) of
-// A_part (points x 32) * [B_hi | B_mid | B_lo]^T; two K steps of 16 each.
-// ad / bd: descriptors of the A buffer (K-major, SBO = its group stride) and
-// of the small B buffer at their bases.
-__device__ __forceinline__ void mma_wide(uint32_t d, uint64_t ad, uint64_t bd) {
-#pragma unroll
-  for (int q = 0; q < 3; ++q)
-#pragma unroll
-    for (int ks = 0; ks < 2; ++ks)
-      mma_bf16(d, ad + ((q * 512 + ks * 256) >> 4), bd + ((ks * 256) >> 4), kIdWide, q | ks);
+// Descriptors: a stacked buffer as M-stacked / N-stacked MN-major operand;
+// a small operand in its K-major or (per part) MN-major view.
+__device__ __forceinline__ uint64_t desc_stacked(const void* p) {
+  return smem_desc(smem_u32(p), kRS, 128);
+}
+__device__ __forceinline__ uint64_t desc_smallK(const void* p) {
+  return smem_desc(smem_u32(p), 128, 512);
+}
+__device__ __forceinline__ uint64_t desc_smallM(const void* p) {
+  return smem_desc(smem_u32(p), 512, 128);
 }
 
-// D (128 x N) = pool over the tile's 128 points: A = [lo; mid; hi; 0] slot
-// parts (MN-major, M = 128), B = point parts (MN-major, N = 96 or 112);
-// eight K steps of 16 points.
-__device__ __forceinline__ void mma_pool(uint32_t d, uint64_t ad, uint64_t bd, int rsb,
-                                         uint32_t idesc) {
+// A from TMEM (K-major by construction): D[tmem] (+)= A[tmem] * B[smem]^T
+__device__ __forceinline__ void mma_ts(uint32_t d, uint32_t a, uint64_t b, uint32_t idesc,
+                                       bool accumulate) {
+  const uint32_t acc = accumulate ? 1u : 0u;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
+      "r"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+// Wide product D = A B^T, A = point rows in TMEM at `a` (K = 32), B = small
+// operand at bd:
+//  * NW = 32: twelve MMAs into one 32-column accumulator; bd is the three-part
+//    small operand, read K-major (B[n][k] = M[n][k]) or, MN, MN-major per
+//    part (B[n][k] = M[k][n]);
+//  * NW = 96: six MMAs into a 96-column N-stacked accumulator; bd is the
+//    three-part small operand read K-major (B[n][k] = M[n][k]) or, MN, the
+//    stacked copy of M (B[n][k] = M[k][n]).
+template <int NW, bool MN>
+__device__ __forceinline__ void wide_ts(uint32_t d, uint32_t a, uint64_t bd) {
+  if constexpr (NW == 32) {
+    constexpr uint32_t id = idesc_bf16(128, 32, 0, MN ? 1 : 0);
+#pragma unroll
+    for (int i = 0; i < 6; ++i)
+#pragma unroll
+      for (int ks = 0; ks < 2; ++ks)
+        mma_ts(d, a + part_a(i) * 16 + ks * 8,
+               bd + ((part_b(i) * 2048 + ks * (MN ? 1024 : 256)) >> 4), id, (i | ks) != 0);
+  } else {
+    constexpr uint32_t id = idesc_bf16(128, 96, 0, MN ? 1 : 0);
+#pragma unroll
+    for (int pa = 0; pa < 3; ++pa)
+#pragma unroll
+      for (int ks = 0; ks < 2; ++ks)
+        mma_ts(d, a + pa * 16 + ks * 8, bd + ((ks * (MN ? 2 * kRS : 256)) >> 4), id,
+               (pa | ks) != 0);
+  }
+}
+
+// D (128 x 96) = pool over the tile's points: A = M-stacked slot parts, B =
+// N-stacked point parts; eight K steps of 16 points.
+__device__ __forceinline__ void mma_pool(uint32_t d, uint64_t ad, uint64_t bd) {
 #pragma unroll
   for (int ks = 0; ks < 8; ++ks)
-    mma_bf16(d, ad + ((ks * 2 * kRS4) >> 4), bd + ((ks * 2 * rsb) >> 4), idesc, ks > 0);
+    mma_bf16(d, ad + ((ks * 2 * kRS) >> 4), bd + ((ks * 2 * kRS) >> 4), kIdPool, ks > 0);
 }
 
-// TMEM loads without their wait (issue several, then tmem_wait once)
-__device__ __forceinline__ void tmem_ld32_nw(uint32_t taddr, uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
-      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
-        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
-        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-}
-__device__ __forceinline__ void tmem_ld1_nw(uint32_t taddr, uint32_t& r) {
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r) : "r"(taddr));
-}
-__device__ __forceinline__ void tmem_wait() {
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+// Add this thread's columns of its pool row (column groups lo, mid, hi of the
+// B parts, small first) into acc. Lanes 0-95 only (A parts lo, mid, hi).
+template <int C>
+__device__ __forceinline__ void drain_pool(uint32_t taddr, int cs, float (&acc)[C]) {
+  float v[C];
+  ld_wide<96, C>(taddr, cs, v);
+#pragma unroll
+  for (int k = 0; k < C / 2; ++k) put2(acc, k, __fadd2_rn(f2(acc, k), f2(v, k)));
 }
 
-// The three column groups of a 96-wide result row, added small first:
-// (group 2 + group 1) + group 0, with the groups in [B_hi | B_mid | B_lo]
-// order for wide products.
-__device__ __forceinline__ void ld_wide(uint32_t taddr, float (&v)[32]) {
-  uint32_t a[32], b[32];
-  tmem_ld32_nw(taddr + 64, a);
-  tmem_ld32_nw(taddr + 32, b);
-  tmem_wait();
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(a[i]) + __uint_as_float(b[i]);
-  tmem_ld32_nw(taddr, a);
-  tmem_wait();
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] += __uint_as_float(a[i]);
-}
-
-// Add this lane's pool row (column groups [B_lo | B_mid | B_hi], lo first)
-// into acc; with ones, also column 96 into acc1.
-__device__ __forceinline__ void ld_pool(uint32_t taddr, float (&acc)[32], bool ones,
-                                        float* acc1) {
-  uint32_t a[32], b[32];
-  tmem_ld32_nw(taddr, a);
-  tmem_ld32_nw(taddr + 32, b);
-  tmem_wait();
-  float v[32];
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(a[i]) + __uint_as_float(b[i]);
-  tmem_ld32_nw(taddr + 64, a);
-  uint32_t s = 0u;
-  if (ones) tmem_ld1_nw(taddr + 96, s);
-  tmem_wait();
-#pragma unroll
-  for (int i = 0; i < 32; ++i) acc[i] += v[i] + __uint_as_float(a[i]);
-  if (ones) *acc1 += __uint_as_float(s);
-}
-
-// all threads' shared writes visible to the tensor core, TMEM reads done
+// ------------------------------------------------------------ sync
+// all threads' shared (and TMEM) writes visible to the tensor core, TMEM
+// reads done
 __device__ __forceinline__ void to_async_barrier() {
   fence_async_shared();
   tc_fence_before();
@@ -219,52 +415,73 @@ __device__ __forceinline__ void wait_mma(uint64_t* bar, uint32_t& phase, int* st
   tc_fence_after();
 }
 
-// logits -> softmax weights in place (rows past N get zero weights); keeps
-// logit - rowmax in lgc when given
-__device__ __forceinline__ void softmax_row(float (&lg)[32], const float* bias, float inv_tau,
-                                            bool valid, float* lgc) {
+// ------------------------------------------------------------ row math
+// Per-head row constants in shared memory: the logit scale in log2 units
+// (log2(e) / tau) and the bias on that scale.
+struct RowConst {
+  float scale;
+  const float* bias2;  // 32 floats: bias * log2(e) / tau
+};
+
+template <int NT>
+__device__ __forceinline__ RowConst row_const(float* bias_s, const float* bias, float tau) {
+  const float inv_tau = __frcp_rn(tau);
+  const float scale = inv_tau * kLog2e;
+  if (threadIdx.x < 32) bias_s[threadIdx.x] = bias[threadIdx.x] * scale;
+  return RowConst{scale, bias_s};
+}
+
+// raw logits (x W^T) -> softmax weights in place (rows past N get zero
+// weights); keeps the centred logit in log2 units, (logit - rowmax) log2(e),
+// in lgc when given
+template <int T, int C>
+__device__ __forceinline__ void softmax_cols(float (&lg)[C], const RowConst& rc, bool valid,
+                                             float* lgc, float* red0, float* red1,
+                                             const Th<T>& th) {
+  const float2 sc = make_float2(rc.scale, rc.scale);
+  const float2* b2 = (const float2*)(rc.bias2 + th.cs * C);
   float m = -INFINITY;
 #pragma unroll
-  for (int g = 0; g < 32; ++g) {
-    lg[g] = (lg[g] + bias[g]) * inv_tau;
-    m = fmaxf(m, lg[g]);
+  for (int k = 0; k < C / 2; ++k) {
+    const float2 v = __ffma2_rn(f2(lg, k), sc, b2[k]);
+    put2(lg, k, v);
+    m = fmaxf(m, fmaxf(v.x, v.y));
   }
-  float tmp[32];
+  m = row_combine<T, true>(m, red0, th);
+  const float2 nm = make_float2(-m, -m);
 #pragma unroll
-  for (int g = 0; g < 32; ++g) {
-    const float c = lg[g] - m;
-    if (lgc) lgc[g] = c;
-    lg[g] = exp2f(c * kLog2e);
-    tmp[g] = lg[g];
+  for (int k = 0; k < C / 2; ++k) {
+    const float2 d = __fadd2_rn(f2(lg, k), nm);
+    if (lgc) put2(lgc, k, d);
+    put2(lg, k, make_float2(exp2f(d.x), exp2f(d.y)));
   }
-  const float r = valid ? __frcp_rn(tree_sum(tmp)) : 0.f;
+  const float s = row_combine<T, false>(tree_sum2(lg), red1, th);
+  const float r = valid ? __frcp_rn(s) : 0.f;
+  const float2 r2 = make_float2(r, r);
 #pragma unroll
-  for (int g = 0; g < 32; ++g) lg[g] *= r;
+  for (int k = 0; k < C / 2; ++k) put2(lg, k, __fmul2_rn(f2(lg, k), r2));
 }
 
-// softmax Jacobian of one row: dl = w (dw - sum w dw); returns
-// sum_g dl (logit - m) (centred: sum_g dl = 0 exactly, so this is
-// sum_g dl * logit, without a common offset multiplying the rounding residue
-// of sum_g dl) and leaves dl / tau in dw
-__device__ __forceinline__ float jacobian_row(const float (&w)[32], float (&dw)[32],
-                                              const float (&lgc)[32], float inv_tau) {
-  float tmp[32];
+// softmax Jacobian of one row: dl = w (dw - sum w dw); returns this thread's
+// part of sum_g dl lgc (centred: sum_g dl = 0 exactly, so this is sum_g dl *
+// logit without a common offset multiplying the rounding residue of sum_g
+// dl; in log2 units) and leaves dl / tau in dw
+template <int T, int C>
+__device__ __forceinline__ float jacobian_cols(const float (&w)[C], float (&dw)[C],
+                                               const float (&lgc)[C], float inv_tau, float* red,
+                                               const Th<T>& th) {
+  float tmp[C];
 #pragma unroll
-  for (int g = 0; g < 32; ++g) tmp[g] = w[g] * dw[g];
-  const float gs = tree_sum(tmp);
+  for (int k = 0; k < C / 2; ++k) put2(tmp, k, __fmul2_rn(f2(w, k), f2(dw, k)));
+  const float gs = row_combine<T, false>(tree_sum2(tmp), red, th);
+  const float2 ng = make_float2(-gs, -gs), it = make_float2(inv_tau, inv_tau);
 #pragma unroll
-  for (int g = 0; g < 32; ++g) {
-    const float dl = w[g] * (dw[g] - gs);
-    tmp[g] = dl * lgc[g];
-    dw[g] = dl * inv_tau;
+  for (int k = 0; k < C / 2; ++k) {
+    const float2 dl = __fmul2_rn(f2(w, k), __fadd2_rn(f2(dw, k), ng));
+    put2(tmp, k, __fmul2_rn(dl, f2(lgc, k)));
+    put2(dw, k, __fmul2_rn(dl, it));
   }
-  return tree_sum(tmp);
-}
-
-__device__ __forceinline__ void store_row(float* base, const float (&v)[32]) {
-#pragma unroll
-  for (int c = 0; c < 8; ++c)
-    *(float4*)(base + 4 * c) = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+  return tree_sum2(tmp);
 }
 
 // The TMA 128B-swizzle destinations need 1024-byte alignment. The dynamic
@@ -276,34 +493,62 @@ __device__ __forceinline__ uint8_t* align_smem(uint8_t* raw) {
   return raw + (((a + 1023u) & ~1023u) - a);
 }
 
-// Pool partials: warp w (A part lo, mid, hi for w = 0, 1, 2) holds slot
-// `lane`'s sums; add the parts small first through xch and write the 32 x n
-// partial (n = 32, or 1 for a scalar per slot).
-__device__ __forceinline__ void pool_write(float* xch, const float* acc, int n, float* part) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+// Pool partials: threads of lanes 0-95 (A part lo, mid, hi = lane quarter)
+// hold slot `lane`'s sums over their C columns; add the parts small first
+// through xch (96 x 33 floats) and write the 32 x 32 partial.
+template <int T>
+__device__ __forceinline__ void pool_write(float* xch, const float* acc, float* part,
+                                           const Th<T>& th) {
+  constexpr int C = Th<T>::C;
   __syncthreads();
-  if (warp < 3)
-    for (int i = 0; i < n; ++i) xch[(warp * 32 + lane) * 33 + i] = acc[i];
+  const int lane = threadIdx.x & 31;
+  if (th.q < 3) {
+#pragma unroll
+    for (int i = 0; i < C; ++i) xch[(th.q * 32 + lane) * 33 + th.cs * C + i] = acc[i];
+  }
   __syncthreads();
-  if (warp == 0)
-    for (int i = 0; i < n; ++i)
-      part[lane * n + i] =
-          (xch[lane * 33 + i] + xch[(32 + lane) * 33 + i]) + xch[(64 + lane) * 33 + i];
+  for (int i = threadIdx.x; i < 32 * 32; i += Th<T>::NT) {
+    const int g = i >> 5, c = i & 31;
+    part[i] = (xch[g * 33 + c] + xch[(32 + g) * 33 + c]) + xch[(64 + g) * 33 + c];
+  }
 }
 
-__device__ __forceinline__ float cta_sum128(float v, float* red) {
+// Plain sums over the CTA's points (s, db): thread (row, cs) holds its rows'
+// sums of columns [C cs, C cs + C); add them over the 128 rows in a fixed
+// order through xch (128 x 33 floats) and write the 32 sums.
+template <int T>
+__device__ __forceinline__ void rowsum_write(float* xch, const float* acc, float* part,
+                                             const Th<T>& th) {
+  constexpr int C = Th<T>::C;
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < C; ++i) xch[th.row * 33 + th.cs * C + i] = acc[i];
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float s[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      s[k] = 0.f;
+      for (int r = k; r < 128; r += 8) s[k] += xch[r * 33 + threadIdx.x];
+    }
+    part[threadIdx.x] = tree_sum(s);
+  }
+}
+
+template <int NT>
+__device__ __forceinline__ float cta_sum_nt(float v, float* red) {
   __syncthreads();
   red[threadIdx.x] = v;
   __syncthreads();
 #pragma unroll
-  for (int s = 64; s > 0; s >>= 1) {
+  for (int s = NT / 2; s > 0; s >>= 1) {
     if ((int)threadIdx.x < s) red[threadIdx.x] += red[threadIdx.x + s];
     __syncthreads();
   }
   return red[0];
 }
 
-// Kernel prologue shared by all four kernels: TMEM, barriers, bias.
+// ------------------------------------------------------------ prologue
 struct Ctl {
   uint64_t* bar_tma;
   uint64_t* bar_mma;
@@ -346,10 +591,10 @@ __device__ __forceinline__ void epilogue(Ctl& c) {
   if ((threadIdx.x >> 5) == 0) tmem_dealloc(c.tmem, NCOLS);
 }
 
-// issue the TMA loads of one tile (one or two point tensors) on bar_tma
+// issue the TMA loads of one tile (one or two point tensors) on bar
 __device__ __forceinline__ void tma_tile(const TcParams& p, uint8_t* st0, uint8_t* st1, int h,
                                          int tile, int b, uint64_t* bar) {
-  mbar_arrive_expect_tx(bar, st1 ? 2 * 16384 : 16384);
+  mbar_arrive_expect_tx(bar, st1 ? 2 * kStage : kStage);
   tma_load_4d(st0, &p.mx, 0, h, tile * kTile, b, bar);
   if (st1) tma_load_4d(st1, &p.mv, 0, h, tile * kTile, b, bar);
 }
@@ -357,7 +602,7 @@ __device__ __forceinline__ void tma_tile(const TcParams& p, uint8_t* st0, uint8_
 // Prefetch the tile after `tile` into the staging buffers. Called by one
 // thread after a barrier that every thread reached only after its reads of
 // the staging rows were consumed (their values stored into the split
-// buffers) and after a proxy fence: a barrier alone does not order
+// buffers or TMEM) and after a proxy fence: a barrier alone does not order
 // generic-proxy shared loads still in flight before the TMA's async-proxy
 // writes, and with two CTAs per SM such loads were seen returning the next
 // tile's bytes.
@@ -366,348 +611,384 @@ __device__ __forceinline__ void prefetch(const TcParams& p, uint8_t* st0, uint8_
   if (tile + p.P < p.ntiles) tma_tile(p, st0, st1, h, tile + p.P, b, bar);
 }
 
-// ------------------------------------------------------------ slice forward
-// smem: [stage x 16K][stage fx 16K][X split / w pool-A 32K][FX pool-B 32K]
-//       [W small 6K][bias 128B][barriers]
-constexpr int kSfStageX = 0, kSfStageF = 16384, kSfX = 32768, kSfF = 65536, kSfWs = 98304,
-              kSfBias = 104448, kSfBar = 104576, kSfBytes = 104576 + 64;
+// Per-kernel threads per point row and co-resident CTAs per SM (shared
+// memory, TMEM and registers sized for it).
+constexpr int kTSliceFwd = 2, kTDesliceFwd = 4, kTSliceBwd = 2, kTDesliceBwd = 4;
+constexpr int kCtasSliceFwd = 2, kCtasDesliceFwd = 2, kCtasSliceBwd = 2, kCtasDesliceBwd = 1;
 
-__global__ void __launch_bounds__(128, 1) k_tc_slice_fwd(const __grid_constant__ TcParams p) {
+// ------------------------------------------------------------ slice forward
+// smem: [stage x][stage fx][WS split: w][F split: fx][W][bias][red][bars]
+// TMEM (256 columns): logits (N-stacked) at 0, z pool at 96, the x point
+// operand at 192. TMEM a thread writes at the start of a tile is disjoint
+// from every column read at the end of the previous one: a warp that is done
+// with a tile may write while another warp of the same lanes still reads.
+constexpr int kSfStageX = 0, kSfStageF = kStage, kSfWS = 2 * kStage,
+              kSfF = kSfWS + kSplit + kTail, kSfWs = kSfF + kSplit, kSfBias = kSfWs + kSmall,
+              kSfRed = kSfBias + 128, kSfBar = kSfRed + 2 * kTSliceFwd * 512,
+              kSfBytes = kSfBar + 64;
+
+__global__ void __launch_bounds__(128 * kTSliceFwd, kCtasSliceFwd)
+    k_tc_slice_fwd(const __grid_constant__ TcParams p) {
+  constexpr int T = kTSliceFwd, NT = Th<T>::NT, C = Th<T>::C;
   extern __shared__ __align__(16) uint8_t sm_raw[];
   uint8_t* sm = align_smem(sm_raw);
-  const int t = threadIdx.x, warp = t >> 5;
+  const Th<T> th;
   const int bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
   Ctl c = prologue_begin<256>(sm, kSfBar);
-  float* bias_s = (float*)(sm + kSfBias);
-  put_small_split(sm + kSfWs, p.W + (int64_t)b * p.swb + (int64_t)h * p.swh, false);
-  if (t < 32) bias_s[t] = p.bias[(int64_t)b * p.sbb + (int64_t)h * p.sbh + t];
-  init_fourth_block(sm + kSfX, false);  // w pool A: zeros
-  init_fourth_block(sm + kSfF, true);   // fx pool B: ones column (s)
-  const float inv_tau = __frcp_rn(p.tau[h]);
+  float* red0 = (float*)(sm + kSfRed);
+  float* red1 = red0 + T * 128;
+  put_small<NT>(sm + kSfWs, p.W + (int64_t)b * p.swb + (int64_t)h * p.swh);
+  const RowConst rc = row_const<NT>((float*)(sm + kSfBias),
+                                    p.bias + (int64_t)b * p.sbb + (int64_t)h * p.sbh, p.tau[h]);
   prologue_end(c);
-  const uint32_t tL = c.tmem, tP = c.tmem + 128, lane_off = (uint32_t)(warp * 32) << 16;
-  const uint64_t dX = smem_desc(smem_u32(sm + kSfX), 128, kRS4);      // K-major A
-  const uint64_t dWs = smem_desc(smem_u32(sm + kSfWs), 128, 512);     // small B
-  const uint64_t dWp = smem_desc(smem_u32(sm + kSfX), kRS4, 128);     // pool A (w)
-  const uint64_t dFp = smem_desc(smem_u32(sm + kSfF), kRS4, 128);     // pool B (fx)
-  float accz[32], accs = 0.f;
+  const uint32_t tL = c.tmem, tP = c.tmem + 96, tX = c.tmem + 192;
+  const uint64_t dWs = desc_smallK(sm + kSfWs);
+  const uint64_t dWp = desc_stacked(sm + kSfWS), dFp = desc_stacked(sm + kSfF);
+  float accz[C], accs[C];
 #pragma unroll
-  for (int i = 0; i < 32; ++i) accz[i] = 0.f;
+  for (int i = 0; i < C; ++i) accz[i] = accs[i] = 0.f;
   int tile = blockIdx.x;
-  if (t == 0 && tile < p.ntiles) tma_tile(p, sm + kSfStageX, sm + kSfStageF, h, tile, b, c.bar_tma);
+  if (threadIdx.x == 0 && tile < p.ntiles)
+    tma_tile(p, sm + kSfStageX, sm + kSfStageF, h, tile, b, c.bar_tma);
   for (; tile < p.ntiles; tile += p.P) {
     const int n0 = tile * kTile;
     mbar_wait(c.bar_tma, c.ph_tma, p.status);
     c.ph_tma ^= 1;
     {
-      float x[32], f[32];
-      read_row(sm + kSfStageX, t, x);
-      read_row(sm + kSfStageF, t, f);
-      put_row_split(sm + kSfX, kRS4, t, x);
-      put_row_split(sm + kSfF, kRS4, t, f);
+      float x[C], f[C];
+      read_cols<C>(sm + kSfStageX, th.row, th.cs, x);
+      read_cols<C>(sm + kSfStageF, th.row, th.cs, f);
+      Split<C>(x).to_tmem(tX + th.lane_off, th.cs);
+      Split<C>(f).to_smem(sm + kSfF, th.row, th.cs);
+      tst_wait();
     }
     to_async_barrier();
-    if (t == 0) {
+    if (threadIdx.x == 0) {
       prefetch(p, sm + kSfStageX, sm + kSfStageF, h, tile, b, c.bar_tma);
-      mma_wide(tL, dX, dWs);
+      wide_ts<96, false>(tL, tX, dWs);  // logits = x W^T
       mma_commit(c.bar_mma);
     }
     wait_mma(c.bar_mma, c.ph_mma, p.status);
     {
-      float lg[32];
-      ld_wide(tL + lane_off, lg);
-      softmax_row(lg, bias_s, inv_tau, n0 + t < p.N, nullptr);
-      put_row_split(sm + kSfX, kRS4, t, lg);  // w, over the consumed X split
+      float lg[C];
+      ld_wide<96, C>(tL + th.lane_off, th.cs, lg);
+      softmax_cols<T, C>(lg, rc, n0 + th.row < p.N, nullptr, red0, red1, th);
+      Split<C>(lg).to_smem(sm + kSfWS, th.row, th.cs);
+#pragma unroll
+      for (int k = 0; k < C / 2; ++k) put2(accs, k, __fadd2_rn(f2(accs, k), f2(lg, k)));
     }
     to_async_barrier();
-    if (t == 0) {
-      mma_pool(tP, dWp, dFp, kRS4, kIdPool1);
+    if (threadIdx.x == 0) {
+      mma_pool(tP, dWp, dFp);  // z += w^T fx
       mma_commit(c.bar_mma);
     }
     wait_mma(c.bar_mma, c.ph_mma, p.status);
-    if (warp < 3) ld_pool(tP + lane_off, accz, true, &accs);
+    if (th.q < 3) drain_pool<C>(tP + th.lane_off, th.cs, accz);
   }
   const int64_t slot = (int64_t)bh * p.P + blockIdx.x;
   float* xch = (float*)(sm + kSfF);
   tc_fence_before();
-  pool_write(xch, accz, 32, p.partA + slot * 32 * 32);
-  pool_write(xch, &accs, 1, p.partS + slot * 32);
+  pool_write<T>(xch, accz, p.partA + slot * 32 * 32, th);
+  rowsum_write<T>(xch, accs, p.partS + slot * 32, th);
   epilogue<256>(c);
 }
 
 // ------------------------------------------------------------ deslice forward
-// smem: [stage x 16K][X split / w split 24K][W small 6K][tok^T small 6K][bias][barriers]
-constexpr int kDfStageX = 0, kDfX = 16384, kDfWs = 40960, kDfTs = 47104, kDfBias = 53248,
-              kDfBar = 53376, kDfBytes = 53376 + 64;
+// smem: [stage x][W][tokens (stacked)][bias][red][bars]
+// TMEM (256 columns): logits -> out (N-stacked) at 0, the point operand (x,
+// then w) at 96.
+constexpr int kDfStageX = 0, kDfWs = kStage, kDfTs = kDfWs + kSmall,
+              kDfBias = kDfTs + kSmallStk, kDfRed = kDfBias + 128,
+              kDfBar = kDfRed + 2 * kTDesliceFwd * 512, kDfBytes = kDfBar + 64;
 
-__global__ void __launch_bounds__(128, 1) k_tc_deslice_fwd(const __grid_constant__ TcParams p) {
+__global__ void __launch_bounds__(128 * kTDesliceFwd, kCtasDesliceFwd)
+    k_tc_deslice_fwd(const __grid_constant__ TcParams p) {
+  constexpr int T = kTDesliceFwd, NT = Th<T>::NT, C = Th<T>::C;
   extern __shared__ __align__(16) uint8_t sm_raw[];
   uint8_t* sm = align_smem(sm_raw);
-  const int t = threadIdx.x, warp = t >> 5;
+  const Th<T> th;
   const int bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
-  Ctl c = prologue_begin<128>(sm, kDfBar);
-  float* bias_s = (float*)(sm + kDfBias);
-  put_small_split(sm + kDfWs, p.W + (int64_t)b * p.swb + (int64_t)h * p.swh, false);
-  put_small_split(sm + kDfTs, p.M + (int64_t)bh * 32 * 32, true);
-  if (t < 32) bias_s[t] = p.bias[(int64_t)b * p.sbb + (int64_t)h * p.sbh + t];
-  const float inv_tau = __frcp_rn(p.tau[h]);
+  Ctl c = prologue_begin<256>(sm, kDfBar);
+  float* red0 = (float*)(sm + kDfRed);
+  float* red1 = red0 + T * 128;
+  put_small<NT>(sm + kDfWs, p.W + (int64_t)b * p.swb + (int64_t)h * p.swh);
+  put_small_stacked<NT>(sm + kDfTs, p.M + (int64_t)bh * 32 * 32);
+  const RowConst rc = row_const<NT>((float*)(sm + kDfBias),
+                                    p.bias + (int64_t)b * p.sbb + (int64_t)h * p.sbh, p.tau[h]);
   prologue_end(c);
-  const uint32_t tL = c.tmem, lane_off = (uint32_t)(warp * 32) << 16;
-  const uint64_t dX = smem_desc(smem_u32(sm + kDfX), 128, kRS3);
-  const uint64_t dWs = smem_desc(smem_u32(sm + kDfWs), 128, 512);
-  const uint64_t dTs = smem_desc(smem_u32(sm + kDfTs), 128, 512);
+  const uint32_t tL = c.tmem, tA = c.tmem + 96;
+  const uint64_t dWs = desc_smallK(sm + kDfWs), dTs = desc_stacked(sm + kDfTs);
   int tile = blockIdx.x;
-  if (t == 0 && tile < p.ntiles) tma_tile(p, sm + kDfStageX, nullptr, h, tile, b, c.bar_tma);
+  if (threadIdx.x == 0 && tile < p.ntiles)
+    tma_tile(p, sm + kDfStageX, nullptr, h, tile, b, c.bar_tma);
   for (; tile < p.ntiles; tile += p.P) {
     const int n0 = tile * kTile;
     mbar_wait(c.bar_tma, c.ph_tma, p.status);
     c.ph_tma ^= 1;
     {
-      float x[32];
-      read_row(sm + kDfStageX, t, x);
-      put_row_split(sm + kDfX, kRS3, t, x);
+      float x[C];
+      read_cols<C>(sm + kDfStageX, th.row, th.cs, x);
+      Split<C>(x).to_tmem(tA + th.lane_off, th.cs);
+      tst_wait();
     }
     to_async_barrier();
-    if (t == 0) {
+    if (threadIdx.x == 0) {
       prefetch(p, sm + kDfStageX, nullptr, h, tile, b, c.bar_tma);
-      mma_wide(tL, dX, dWs);
+      wide_ts<96, false>(tL, tA, dWs);  // logits = x W^T
       mma_commit(c.bar_mma);
     }
     wait_mma(c.bar_mma, c.ph_mma, p.status);
     {
-      float lg[32];
-      ld_wide(tL + lane_off, lg);
-      softmax_row(lg, bias_s, inv_tau, true, nullptr);
-      put_row_split(sm + kDfX, kRS3, t, lg);
+      float lg[C];
+      ld_wide<96, C>(tL + th.lane_off, th.cs, lg);
+      softmax_cols<T, C>(lg, rc, true, nullptr, red0, red1, th);
+      Split<C>(lg).to_tmem(tA + th.lane_off, th.cs);  // w, over the consumed x
+      tst_wait();
     }
     to_async_barrier();
-    if (t == 0) {
-      mma_wide(tL, dX, dTs);  // out = w tokens, over the consumed logits
+    if (threadIdx.x == 0) {
+      wide_ts<96, true>(tL, tA, dTs);  // out = w tokens, over the consumed logits
       mma_commit(c.bar_mma);
     }
     wait_mma(c.bar_mma, c.ph_mma, p.status);
-    float o[32];
-    ld_wide(tL + lane_off, o);
-    if (n0 + t < p.N)
-      store_row(p.out + (int64_t)b * p.so[0] + (int64_t)(n0 + t) * p.so[1] + (int64_t)h * p.so[2],
-                o);
+    float o[C];
+    ld_wide<96, C>(tL + th.lane_off, th.cs, o);
+    if (n0 + th.row < p.N)
+      store_cols<C>(p.out + (int64_t)b * p.so[0] + (int64_t)(n0 + th.row) * p.so[1] +
+                        (int64_t)h * p.so[2],
+                    th.cs, o);
   }
-  epilogue<128>(c);
+  epilogue<256>(c);
+}
+
+// ------------------------------------------------------------ slice backward
+// smem: [stage x][stage fx][X split][UP split: dl/tau][W][dz_num][bias][ds][red][bars]
+// TMEM (256 columns): logits (N-stacked) at 0, dw at 96, point operands x at
+// 160 and fx at 208; then dfx at 0, dx at 32, the dW pool at 64 and point
+// operands w at 160 and dl/tau at 208. The operands written at the start of
+// a tile are disjoint from the columns read at the end of the previous one.
+constexpr int kSbStageX = 0, kSbStageF = kStage, kSbX = 2 * kStage, kSbUp = kSbX + kSplit,
+              kSbWs = kSbUp + kSplit + kTail, kSbZs = kSbWs + kSmall, kSbBias = kSbZs + kSmall,
+              kSbDs = kSbBias + 128, kSbRed = kSbDs + 128,
+              kSbBar = kSbRed + 3 * kTSliceBwd * 512, kSbBytes = kSbBar + 64;
+
+__global__ void __launch_bounds__(128 * kTSliceBwd, kCtasSliceBwd)
+    k_tc_slice_bwd(const __grid_constant__ TcParams p) {
+  constexpr int T = kTSliceBwd, NT = Th<T>::NT, C = Th<T>::C;
+  extern __shared__ __align__(16) uint8_t sm_raw[];
+  uint8_t* sm = align_smem(sm_raw);
+  const Th<T> th;
+  const int bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
+  Ctl c = prologue_begin<256>(sm, kSbBar);
+  float* ds_s = (float*)(sm + kSbDs);
+  float* red0 = (float*)(sm + kSbRed);
+  float* red1 = red0 + T * 128;
+  float* red2 = red1 + T * 128;
+  put_small<NT>(sm + kSbWs, p.W + (int64_t)b * p.swb + (int64_t)h * p.swh);
+  put_small<NT>(sm + kSbZs, p.M + (int64_t)bh * 32 * 32);
+  const RowConst rc = row_const<NT>((float*)(sm + kSbBias),
+                                    p.bias + (int64_t)b * p.sbb + (int64_t)h * p.sbh, p.tau[h]);
+  if (threadIdx.x < 32) ds_s[threadIdx.x] = p.ds[(int64_t)bh * 32 + threadIdx.x];
+  const float inv_tau = __frcp_rn(p.tau[h]);
+  prologue_end(c);
+  const uint32_t tL = c.tmem, tDw = c.tmem + 96, tX = c.tmem + 160, tF = c.tmem + 208;
+  const uint32_t tDfx = c.tmem, tDx = c.tmem + 32, tP = c.tmem + 64, tW = c.tmem + 160,
+                 tU = c.tmem + 208;
+  const uint64_t dXb = desc_stacked(sm + kSbX), dUp = desc_stacked(sm + kSbUp);
+  const uint64_t dWk = desc_smallK(sm + kSbWs), dWm = desc_smallM(sm + kSbWs);
+  const uint64_t dZk = desc_smallK(sm + kSbZs), dZm = desc_smallM(sm + kSbZs);
+  float accw[C], accb[C], dt_acc = 0.f;
+#pragma unroll
+  for (int i = 0; i < C; ++i) accw[i] = accb[i] = 0.f;
+  int tile = blockIdx.x;
+  if (threadIdx.x == 0 && tile < p.ntiles)
+    tma_tile(p, sm + kSbStageX, sm + kSbStageF, h, tile, b, c.bar_tma);
+  for (; tile < p.ntiles; tile += p.P) {
+    const int n0 = tile * kTile;
+    const bool valid = n0 + th.row < p.N;
+    mbar_wait(c.bar_tma, c.ph_tma, p.status);
+    c.ph_tma ^= 1;
+    {
+      float x[C], f[C];
+      read_cols<C>(sm + kSbStageX, th.row, th.cs, x);
+      read_cols<C>(sm + kSbStageF, th.row, th.cs, f);
+      const Split<C> xs(x);
+      xs.to_smem(sm + kSbX, th.row, th.cs);
+      xs.to_tmem(tX + th.lane_off, th.cs);
+      Split<C>(f).to_tmem(tF + th.lane_off, th.cs);
+      tst_wait();
+    }
+    to_async_barrier();
+    if (threadIdx.x == 0) {
+      prefetch(p, sm + kSbStageX, sm + kSbStageF, h, tile, b, c.bar_tma);
+      wide_ts<96, false>(tL, tX, dWk);   // logits = x W^T
+      wide_ts<32, false>(tDw, tF, dZk);  // dw = fx dz_num^T
+      mma_commit(c.bar_mma);
+    }
+    wait_mma(c.bar_mma, c.ph_mma, p.status);
+    {
+      float w[C], lgc[C], dw[C];
+      ld_wide<96, C>(tL + th.lane_off, th.cs, w);
+      softmax_cols<T, C>(w, rc, valid, lgc, red0, red1, th);
+      ld_wide<32, C>(tDw + th.lane_off, th.cs, dw);
+      const float2* ds2 = (const float2*)(ds_s + th.cs * C);
+#pragma unroll
+      for (int k = 0; k < C / 2; ++k) put2(dw, k, __fadd2_rn(f2(dw, k), ds2[k]));
+      const float rdt = jacobian_cols<T, C>(w, dw, lgc, inv_tau, red2, th);
+      if (valid) dt_acc += rdt;
+      Split<C>(w).to_tmem(tW + th.lane_off, th.cs);
+      const Split<C> us(dw);  // dl / tau
+      us.to_tmem(tU + th.lane_off, th.cs);
+      us.to_smem(sm + kSbUp, th.row, th.cs);
+#pragma unroll
+      for (int k = 0; k < C / 2; ++k) put2(accb, k, __fadd2_rn(f2(accb, k), f2(dw, k)));
+      tst_wait();
+    }
+    to_async_barrier();
+    if (threadIdx.x == 0) {
+      wide_ts<32, true>(tDfx, tW, dZm);  // dfx = w dz_num
+      wide_ts<32, true>(tDx, tU, dWm);   // dx = (dl/tau) W
+      mma_pool(tP, dUp, dXb);            // dW += (dl/tau)^T x
+      mma_commit(c.bar_mma);
+    }
+    wait_mma(c.bar_mma, c.ph_mma, p.status);
+    {
+      float v[C];
+      ld_wide<32, C>(tDfx + th.lane_off, th.cs, v);
+      if (valid)
+        store_cols<C>(p.out2 + (int64_t)b * p.so2[0] + (int64_t)(n0 + th.row) * p.so2[1] +
+                          (int64_t)h * p.so2[2],
+                      th.cs, v);
+      ld_wide<32, C>(tDx + th.lane_off, th.cs, v);
+      if (valid)
+        store_cols<C>(p.out + (int64_t)b * p.so[0] + (int64_t)(n0 + th.row) * p.so[1] +
+                          (int64_t)h * p.so[2],
+                      th.cs, v);
+    }
+    if (th.q < 3) drain_pool<C>(tP + th.lane_off, th.cs, accw);
+  }
+  const int64_t slot = (int64_t)bh * p.P + blockIdx.x;
+  float* xch = (float*)(sm + kSbX);
+  tc_fence_before();
+  pool_write<T>(xch, accw, p.partA + slot * 32 * 32, th);
+  rowsum_write<T>(xch, accb, p.partS + slot * 32, th);
+  const float tot = cta_sum_nt<NT>(dt_acc, (float*)(sm + kSbUp));
+  if (threadIdx.x == 0) p.partDt[slot] = -inv_tau * kLn2 * tot;
+  epilogue<256>(c);
 }
 
 // ------------------------------------------------------------ deslice backward
-// smem: [stage x 16K][stage dout 16K][X 32K (RS4, ones)][DO 24K (RS3)]
-// [WP 32K (RS4, zeros)][UP 32K (RS4, zeros)][W 6K][tok 6K][W^T 6K][bias][red][bars]
-constexpr int kDbStageX = 0, kDbStageO = 16384, kDbX = 32768, kDbO = 65536, kDbWp = 90112,
-              kDbUp = 122880, kDbWs = 155648, kDbTs = 161792, kDbWt = 167936,
-              kDbBias = 174080, kDbRed = 174208, kDbBar = 174720, kDbBytes = 174720 + 64;
+// smem: [stage x][stage dout][X split][O split: dout][WP split: w][UP split: dl/tau]
+//       [W][W stacked][tokens][bias][red][bars]
+// TMEM (512 columns): logits -> dx (N-stacked) at 0, dw at 96, the dtokens
+// pool at 192 and the dW pool at 288, point operands x -> dl/tau at 384 and
+// dout at 432.
+constexpr int kDbStageX = 0, kDbStageO = kStage, kDbX = 2 * kStage, kDbO = kDbX + kSplit,
+              kDbWp = kDbO + kSplit, kDbUp = kDbWp + kSplit + kTail,
+              kDbWs = kDbUp + kSplit + kTail, kDbWst = kDbWs + kSmall,
+              kDbTs = kDbWst + kSmallStk, kDbBias = kDbTs + kSmall, kDbRed = kDbBias + 128,
+              kDbBar = kDbRed + 3 * kTDesliceBwd * 512, kDbBytes = kDbBar + 64;
 
-__global__ void __launch_bounds__(128, 1) k_tc_deslice_bwd(const __grid_constant__ TcParams p) {
+__global__ void __launch_bounds__(128 * kTDesliceBwd, kCtasDesliceBwd)
+    k_tc_deslice_bwd(const __grid_constant__ TcParams p) {
+  constexpr int T = kTDesliceBwd, NT = Th<T>::NT, C = Th<T>::C;
   extern __shared__ __align__(16) uint8_t sm_raw[];
   uint8_t* sm = align_smem(sm_raw);
-  const int t = threadIdx.x, warp = t >> 5;
+  const Th<T> th;
   const int bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
   Ctl c = prologue_begin<512>(sm, kDbBar);
-  float* bias_s = (float*)(sm + kDbBias);
+  float* red0 = (float*)(sm + kDbRed);
+  float* red1 = red0 + T * 128;
+  float* red2 = red1 + T * 128;
   const float* Wb = p.W + (int64_t)b * p.swb + (int64_t)h * p.swh;
-  put_small_split(sm + kDbWs, Wb, false);                             // logits: W
-  put_small_split(sm + kDbTs, p.M + (int64_t)bh * 32 * 32, false);    // dw: tok
-  put_small_split(sm + kDbWt, Wb, true);                              // dx: W^T
-  if (t < 32) bias_s[t] = p.bias[(int64_t)b * p.sbb + (int64_t)h * p.sbh + t];
-  init_fourth_block(sm + kDbX, true);
-  init_fourth_block(sm + kDbWp, false);
-  init_fourth_block(sm + kDbUp, false);
+  put_small<NT>(sm + kDbWs, Wb);
+  put_small_stacked<NT>(sm + kDbWst, Wb);
+  put_small<NT>(sm + kDbTs, p.M + (int64_t)bh * 32 * 32);
+  const RowConst rc = row_const<NT>((float*)(sm + kDbBias),
+                                    p.bias + (int64_t)b * p.sbb + (int64_t)h * p.sbh, p.tau[h]);
   const float inv_tau = __frcp_rn(p.tau[h]);
   prologue_end(c);
-  // TMEM: logits / dx at 0, dw / dtok-pool at 128, dW-pool at 256
-  const uint32_t tA = c.tmem, tB = c.tmem + 128, tC = c.tmem + 256;
-  const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
-  const uint64_t dXa = smem_desc(smem_u32(sm + kDbX), 128, kRS4);
-  const uint64_t dOa = smem_desc(smem_u32(sm + kDbO), 128, kRS3);
-  const uint64_t dUa = smem_desc(smem_u32(sm + kDbUp), 128, kRS4);
-  const uint64_t dWs = smem_desc(smem_u32(sm + kDbWs), 128, 512);
-  const uint64_t dTs = smem_desc(smem_u32(sm + kDbTs), 128, 512);
-  const uint64_t dWt = smem_desc(smem_u32(sm + kDbWt), 128, 512);
-  const uint64_t dWpP = smem_desc(smem_u32(sm + kDbWp), kRS4, 128);
-  const uint64_t dUpP = smem_desc(smem_u32(sm + kDbUp), kRS4, 128);
-  const uint64_t dOb = smem_desc(smem_u32(sm + kDbO), kRS3, 128);
-  const uint64_t dXb = smem_desc(smem_u32(sm + kDbX), kRS4, 128);
-  float acct[32], accw[32], accb = 0.f, dt_acc = 0.f;
+  const uint32_t tL = c.tmem, tDw = c.tmem + 96, tP1 = c.tmem + 192, tP2 = c.tmem + 288,
+                 tX = c.tmem + 384, tO = c.tmem + 432;
+  const uint64_t dXb = desc_stacked(sm + kDbX), dOb = desc_stacked(sm + kDbO),
+                 dWp = desc_stacked(sm + kDbWp), dUp = desc_stacked(sm + kDbUp);
+  const uint64_t dWk = desc_smallK(sm + kDbWs), dWst = desc_stacked(sm + kDbWst),
+                 dTk = desc_smallK(sm + kDbTs);
+  float acct[C], accw[C], accb[C], dt_acc = 0.f;
 #pragma unroll
-  for (int i = 0; i < 32; ++i) acct[i] = accw[i] = 0.f;
+  for (int i = 0; i < C; ++i) acct[i] = accw[i] = accb[i] = 0.f;
   int tile = blockIdx.x;
-  if (t == 0 && tile < p.ntiles) tma_tile(p, sm + kDbStageX, sm + kDbStageO, h, tile, b, c.bar_tma);
+  if (threadIdx.x == 0 && tile < p.ntiles)
+    tma_tile(p, sm + kDbStageX, sm + kDbStageO, h, tile, b, c.bar_tma);
   for (; tile < p.ntiles; tile += p.P) {
     const int n0 = tile * kTile;
-    const bool valid = n0 + t < p.N;
+    const bool valid = n0 + th.row < p.N;
     mbar_wait(c.bar_tma, c.ph_tma, p.status);
     c.ph_tma ^= 1;
     {
-      float x[32], o[32];
-      read_row(sm + kDbStageX, t, x);
-      read_row(sm + kDbStageO, t, o);
-      put_row_split(sm + kDbX, kRS4, t, x);
-      put_row_split(sm + kDbO, kRS3, t, o);
+      float x[C], o[C];
+      read_cols<C>(sm + kDbStageX, th.row, th.cs, x);
+      read_cols<C>(sm + kDbStageO, th.row, th.cs, o);
+      const Split<C> xs(x);
+      xs.to_smem(sm + kDbX, th.row, th.cs);
+      xs.to_tmem(tX + th.lane_off, th.cs);
+      const Split<C> os(o);
+      os.to_smem(sm + kDbO, th.row, th.cs);
+      os.to_tmem(tO + th.lane_off, th.cs);
+      tst_wait();
     }
     to_async_barrier();
-    if (t == 0) {
+    if (threadIdx.x == 0) {
       prefetch(p, sm + kDbStageX, sm + kDbStageO, h, tile, b, c.bar_tma);
-      mma_wide(tA, dXa, dWs);  // logits = x W^T
-      mma_wide(tB, dOa, dTs);  // dw = d_out tok^T
+      wide_ts<96, false>(tL, tX, dWk);   // logits = x W^T
+      wide_ts<96, false>(tDw, tO, dTk);  // dw = d_out tok^T
       mma_commit(c.bar_mma);
     }
     wait_mma(c.bar_mma, c.ph_mma, p.status);
     {
-      float w[32], lgc[32], dw[32];
-      ld_wide(tA + lane_off, w);
-      softmax_row(w, bias_s, inv_tau, valid, lgc);
-      ld_wide(tB + lane_off, dw);
-      const float rdt = jacobian_row(w, dw, lgc, inv_tau);
+      float w[C], lgc[C], dw[C];
+      ld_wide<96, C>(tL + th.lane_off, th.cs, w);
+      softmax_cols<T, C>(w, rc, valid, lgc, red0, red1, th);
+      ld_wide<96, C>(tDw + th.lane_off, th.cs, dw);
+      const float rdt = jacobian_cols<T, C>(w, dw, lgc, inv_tau, red2, th);
       if (valid) dt_acc += rdt;
-      put_row_split(sm + kDbWp, kRS4, t, w);
-      put_row_split(sm + kDbUp, kRS4, t, dw);  // dl / tau
+      Split<C>(w).to_smem(sm + kDbWp, th.row, th.cs);
+      const Split<C> us(dw);  // dl / tau
+      us.to_smem(sm + kDbUp, th.row, th.cs);
+      us.to_tmem(tX + th.lane_off, th.cs);  // over the consumed x
+#pragma unroll
+      for (int k = 0; k < C / 2; ++k) put2(accb, k, __fadd2_rn(f2(accb, k), f2(dw, k)));
+      tst_wait();
     }
     to_async_barrier();
-    if (t == 0) {
-      mma_wide(tA, dUa, dWt);                      // dx = (dl/tau) W
-      mma_pool(tB, dWpP, dOb, kRS3, kIdPool);      // dtokens += w^T d_out
-      mma_pool(tC, dUpP, dXb, kRS4, kIdPool1);     // dW += (dl/tau)^T x, db
+    if (threadIdx.x == 0) {
+      wide_ts<96, true>(tL, tX, dWst);  // dx = (dl/tau) W
+      mma_pool(tP1, dWp, dOb);          // dtokens += w^T d_out
+      mma_pool(tP2, dUp, dXb);          // dW += (dl/tau)^T x
       mma_commit(c.bar_mma);
     }
     wait_mma(c.bar_mma, c.ph_mma, p.status);
     {
-      float v[32];
-      ld_wide(tA + lane_off, v);
+      float v[C];
+      ld_wide<96, C>(tL + th.lane_off, th.cs, v);
       if (valid)
-        store_row(p.out + (int64_t)b * p.so[0] + (int64_t)(n0 + t) * p.so[1] +
-                      (int64_t)h * p.so[2],
-                  v);
+        store_cols<C>(p.out + (int64_t)b * p.so[0] + (int64_t)(n0 + th.row) * p.so[1] +
+                          (int64_t)h * p.so[2],
+                      th.cs, v);
     }
-    if (warp < 3) {
-      ld_pool(tB + lane_off, acct, false, nullptr);
-      ld_pool(tC + lane_off, accw, true, &accb);
+    if (th.q < 3) {
+      drain_pool<C>(tP1 + th.lane_off, th.cs, acct);
+      drain_pool<C>(tP2 + th.lane_off, th.cs, accw);
     }
   }
   const int64_t slot = (int64_t)bh * p.P + blockIdx.x;
   float* xch = (float*)(sm + kDbX);
   tc_fence_before();
-  pool_write(xch, acct, 32, p.partB + slot * 32 * 32);
-  pool_write(xch, accw, 32, p.partA + slot * 32 * 32);
-  pool_write(xch, &accb, 1, p.partS + slot * 32);
-  const float tot = cta_sum128(dt_acc, (float*)(sm + kDbRed));
-  if (t == 0) p.partDt[slot] = -inv_tau * tot;
-  epilogue<512>(c);
-}
-
-// ------------------------------------------------------------ slice backward
-// smem: [stage x 16K][stage fx 16K][X 32K (RS4, ones)][F / w 24K (RS3)]
-// [UP 32K (RS4, zeros)][W 6K][dzn 6K][dzn^T 6K][W^T 6K][bias][ds][red][bars]
-constexpr int kSbStageX = 0, kSbStageF = 16384, kSbX = 32768, kSbF = 65536, kSbUp = 90112,
-              kSbWs = 122880, kSbZs = 129024, kSbZt = 135168, kSbWt = 141312,
-              kSbBias = 147456, kSbDs = 147584, kSbRed = 147712, kSbBar = 148224,
-              kSbBytes = 148224 + 64;
-
-__global__ void __launch_bounds__(128, 1) k_tc_slice_bwd(const __grid_constant__ TcParams p) {
-  extern __shared__ __align__(16) uint8_t sm_raw[];
-  uint8_t* sm = align_smem(sm_raw);
-  const int t = threadIdx.x, warp = t >> 5;
-  const int bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
-  Ctl c = prologue_begin<512>(sm, kSbBar);
-  float* bias_s = (float*)(sm + kSbBias);
-  float* ds_s = (float*)(sm + kSbDs);
-  const float* Wb = p.W + (int64_t)b * p.swb + (int64_t)h * p.swh;
-  const float* dzb = p.M + (int64_t)bh * 32 * 32;
-  put_small_split(sm + kSbWs, Wb, false);   // logits: W
-  put_small_split(sm + kSbZs, dzb, false);  // dw: dz_num
-  put_small_split(sm + kSbZt, dzb, true);   // dfx: dz_num^T
-  put_small_split(sm + kSbWt, Wb, true);    // dx: W^T
-  if (t < 32) {
-    bias_s[t] = p.bias[(int64_t)b * p.sbb + (int64_t)h * p.sbh + t];
-    ds_s[t] = p.ds[(int64_t)bh * 32 + t];
-  }
-  init_fourth_block(sm + kSbX, true);
-  init_fourth_block(sm + kSbUp, false);
-  const float inv_tau = __frcp_rn(p.tau[h]);
-  prologue_end(c);
-  // TMEM: logits / dfx at 0, dw / dx at 128, dW-pool at 256
-  const uint32_t tA = c.tmem, tB = c.tmem + 128, tC = c.tmem + 256;
-  const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
-  const uint64_t dXa = smem_desc(smem_u32(sm + kSbX), 128, kRS4);
-  const uint64_t dFa = smem_desc(smem_u32(sm + kSbF), 128, kRS3);
-  const uint64_t dUa = smem_desc(smem_u32(sm + kSbUp), 128, kRS4);
-  const uint64_t dWs = smem_desc(smem_u32(sm + kSbWs), 128, 512);
-  const uint64_t dZs = smem_desc(smem_u32(sm + kSbZs), 128, 512);
-  const uint64_t dZt = smem_desc(smem_u32(sm + kSbZt), 128, 512);
-  const uint64_t dWt = smem_desc(smem_u32(sm + kSbWt), 128, 512);
-  const uint64_t dUpP = smem_desc(smem_u32(sm + kSbUp), kRS4, 128);
-  const uint64_t dXb = smem_desc(smem_u32(sm + kSbX), kRS4, 128);
-  float accw[32], accb = 0.f, dt_acc = 0.f;
-#pragma unroll
-  for (int i = 0; i < 32; ++i) accw[i] = 0.f;
-  int tile = blockIdx.x;
-  if (t == 0 && tile < p.ntiles) tma_tile(p, sm + kSbStageX, sm + kSbStageF, h, tile, b, c.bar_tma);
-  for (; tile < p.ntiles; tile += p.P) {
-    const int n0 = tile * kTile;
-    const bool valid = n0 + t < p.N;
-    mbar_wait(c.bar_tma, c.ph_tma, p.status);
-    c.ph_tma ^= 1;
-    {
-      float x[32], f[32];
-      read_row(sm + kSbStageX, t, x);
-      read_row(sm + kSbStageF, t, f);
-      put_row_split(sm + kSbX, kRS4, t, x);
-      put_row_split(sm + kSbF, kRS3, t, f);
-    }
-    to_async_barrier();
-    if (t == 0) {
-      prefetch(p, sm + kSbStageX, sm + kSbStageF, h, tile, b, c.bar_tma);
-      mma_wide(tA, dXa, dWs);  // logits = x W^T
-      mma_wide(tB, dFa, dZs);  // dw = fx dz_num^T
-      mma_commit(c.bar_mma);
-    }
-    wait_mma(c.bar_mma, c.ph_mma, p.status);
-    {
-      float w[32], lgc[32], dw[32];
-      ld_wide(tA + lane_off, w);
-      softmax_row(w, bias_s, inv_tau, valid, lgc);
-      ld_wide(tB + lane_off, dw);
-#pragma unroll
-      for (int g = 0; g < 32; ++g) dw[g] += ds_s[g];
-      const float rdt = jacobian_row(w, dw, lgc, inv_tau);
-      if (valid) dt_acc += rdt;
-      put_row_split(sm + kSbF, kRS3, t, w);    // over the consumed fx split
-      put_row_split(sm + kSbUp, kRS4, t, dw);  // dl / tau
-    }
-    to_async_barrier();
-    if (t == 0) {
-      mma_wide(tA, dFa, dZt);                   // dfx = w dz_num
-      mma_wide(tB, dUa, dWt);                   // dx = (dl/tau) W
-      mma_pool(tC, dUpP, dXb, kRS4, kIdPool1);  // dW += (dl/tau)^T x, db
-      mma_commit(c.bar_mma);
-    }
-    wait_mma(c.bar_mma, c.ph_mma, p.status);
-    {
-      float v[32];
-      ld_wide(tA + lane_off, v);
-      if (valid)
-        store_row(p.out2 + (int64_t)b * p.so2[0] + (int64_t)(n0 + t) * p.so2[1] +
-                      (int64_t)h * p.so2[2],
-                  v);
-      ld_wide(tB + lane_off, v);
-      if (valid)
-        store_row(p.out + (int64_t)b * p.so[0] + (int64_t)(n0 + t) * p.so[1] +
-                      (int64_t)h * p.so[2],
-                  v);
-    }
-    if (warp < 3) ld_pool(tC + lane_off, accw, true, &accb);
-  }
-  const int64_t slot = (int64_t)bh * p.P + blockIdx.x;
-  float* xch = (float*)(sm + kSbX);
-  tc_fence_before();
-  pool_write(xch, accw, 32, p.partA + slot * 32 * 32);
-  pool_write(xch, &accb, 1, p.partS + slot * 32);
-  const float tot = cta_sum128(dt_acc, (float*)(sm + kSbRed));
-  if (t == 0) p.partDt[slot] = -inv_tau * tot;
+  pool_write<T>(xch, acct, p.partB + slot * 32 * 32, th);
+  pool_write<T>(xch, accw, p.partA + slot * 32 * 32, th);
+  rowsum_write<T>(xch, accb, p.partS + slot * 32, th);
+  const float tot = cta_sum_nt<NT>(dt_acc, (float*)(sm + kDbO));
+  if (threadIdx.x == 0) p.partDt[slot] = -inv_tau * kLn2 * tot;
   epilogue<512>(c);
 }
 
@@ -777,48 +1058,58 @@ static cudaError_t set_smem(const void* k, int bytes) {
 
 std::atomic<uint64_t> g_tc_launches{0};
 
+template <typename K>
+static cudaError_t launch_tc(K kernel, int T, int bytes, const TcParams& p, cudaStream_t s) {
+  const cudaError_t e = set_smem((const void*)kernel, bytes + kSmemPad);
+  if (e != cudaSuccess) return e;
+  kernel<<<dim3(p.P, p.B * p.H), 128 * T, bytes + kSmemPad, s>>>(p);
+  return cudaSuccess;
+}
+
 cudaError_t run_tc(TcKind k, const TcParams& p, cudaStream_t s) {
-  const dim3 grid(p.P, p.B * p.H);
   cudaError_t e = cudaSuccess;
   switch (k) {
-    case TcKind::SliceFwd:
-      e = set_smem((const void*)k_tc_slice_fwd, kSfBytes + kSmemPad);
-      if (e != cudaSuccess) return e;
-      k_tc_slice_fwd<<<grid, 128, kSfBytes + kSmemPad, s>>>(p);
-      break;
+    case TcKind::SliceFwd: e = launch_tc(k_tc_slice_fwd, kTSliceFwd, kSfBytes, p, s); break;
     case TcKind::DesliceFwd:
-      e = set_smem((const void*)k_tc_deslice_fwd, kDfBytes + kSmemPad);
-      if (e != cudaSuccess) return e;
-      k_tc_deslice_fwd<<<grid, 128, kDfBytes + kSmemPad, s>>>(p);
+      e = launch_tc(k_tc_deslice_fwd, kTDesliceFwd, kDfBytes, p, s);
       break;
-    case TcKind::SliceBwd:
-      e = set_smem((const void*)k_tc_slice_bwd, kSbBytes + kSmemPad);
-      if (e != cudaSuccess) return e;
-      k_tc_slice_bwd<<<grid, 128, kSbBytes + kSmemPad, s>>>(p);
-      break;
+    case TcKind::SliceBwd: e = launch_tc(k_tc_slice_bwd, kTSliceBwd, kSbBytes, p, s); break;
     case TcKind::DesliceBwd:
-      e = set_smem((const void*)k_tc_deslice_bwd, kDbBytes + kSmemPad);
-      if (e != cudaSuccess) return e;
-      k_tc_deslice_bwd<<<grid, 128, kDbBytes + kSmemPad, s>>>(p);
+      e = launch_tc(k_tc_deslice_bwd, kTDesliceBwd, kDbBytes, p, s);
       break;
-    default:
-      return cudaErrorInvalidValue;
+    default: return cudaErrorInvalidValue;
   }
+  if (e != cudaSuccess) return e;
   g_launches.fetch_add(1, std::memory_order_relaxed);
   g_tc_launches.fetch_add(1, std::memory_order_relaxed);
   return cudaGetLastError();
 }
 
-// Co-resident CTAs per SM each kernel is sized for (shared memory and TMEM):
-// slice fwd 102 KB + 256 columns, deslice fwd 52 KB + 128 columns, the
-// backward kernels 145 / 171 KB + all 512 columns.
+// Co-resident CTAs per SM each kernel is sized for (shared memory, TMEM and
+// registers): the grid holds this many CTAs per SM.
 int tc_ctas_per_sm(TcKind k) {
   switch (k) {
-    case TcKind::SliceFwd: return 2;
-    case TcKind::DesliceFwd: return 4;
-    default: return 1;
+    case TcKind::SliceFwd: return kCtasSliceFwd;
+    case TcKind::DesliceFwd: return kCtasDesliceFwd;
+    case TcKind::SliceBwd: return kCtasSliceBwd;
+    case TcKind::DesliceBwd: return kCtasDesliceBwd;
   }
+  return 1;
 }
+
+// shared memory per SM (228 KB) holds the co-resident CTAs, each with its
+// alignment pad and the 1 KB the runtime reserves per CTA
+static_assert((kSfBytes + kSmemPad + 1024) * kCtasSliceFwd <= 228 * 1024, "slice fwd smem");
+static_assert((kDfBytes + kSmemPad + 1024) * kCtasDesliceFwd <= 228 * 1024, "deslice fwd smem");
+static_assert((kSbBytes + kSmemPad + 1024) * kCtasSliceBwd <= 228 * 1024, "slice bwd smem");
+static_assert(kDbBytes + kSmemPad <= 227 * 1024, "deslice bwd smem");
+// TMEM per SM (512 columns) holds the co-resident CTAs' allocations
+static_assert(256 * kCtasSliceFwd <= 512 && 256 * kCtasDesliceFwd <= 512 &&
+                  256 * kCtasSliceBwd <= 512 && 512 * kCtasDesliceBwd <= 512,
+              "TMEM columns");
+static_assert(kSfWS % 16 == 0 && kSfF % 16 == 0 && kSbUp % 16 == 0 && kDbUp % 16 == 0 &&
+                  kDfTs % 16 == 0 && kDbWst % 16 == 0,
+              "operand alignment");
 
 }  // namespace tcx
 }  // namespace fs
