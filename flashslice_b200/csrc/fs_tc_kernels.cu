@@ -171,6 +171,19 @@ __device__ __forceinline__ void tld<16>(uint32_t a, uint32_t (&r)[16]) {
         "=r"(r[14]), "=r"(r[15])
       : "r"(a));
 }
+template <>
+__device__ __forceinline__ void tld<32>(uint32_t a, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(a));
+}
 __device__ __forceinline__ void tld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
@@ -188,6 +201,16 @@ __device__ __forceinline__ void tst<8>(uint32_t a, const uint32_t (&r)[8]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(a),
       "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+      : "memory");
+}
+template <>
+__device__ __forceinline__ void tst<16>(uint32_t a, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15, %16};" ::"r"(a),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15])
       : "memory");
 }
 __device__ __forceinline__ void tst_wait() {
@@ -319,12 +342,53 @@ __device__ __forceinline__ void put_small_stacked(uint8_t* dst, const float* M) 
   }
 }
 
-template <int C>
-__device__ __forceinline__ void store_cols(float* rowp, int cs, const float (&v)[C]) {
+// A result tile written to a point tensor with whole 32-byte sectors: this
+// warp's 32 rows (lanes 32 q ..) and C columns (from cs C) are read back from
+// TMEM in the 16x256b shape, in which thread t holds rows 16 half + t / 4 and
+// 16 half + 8 + t / 4 and columns 2 (t % 4), +1 of each 8-column chunk, so
+// four threads store 32 contiguous bytes of a row. (Stored straight from the
+// 32x32b shape, each thread's row is a different point, 1 KB or more apart,
+// and every store instruction half-fills 32 sectors.) The result is one
+// 32-column accumulator (NW = 32) or an N-stacked one whose column groups
+// are added small first (NW = 96). Rows at or past `nvalid` are not written.
+template <int NW, int C>
+__device__ __forceinline__ void store_result(uint32_t tcol, int q, int cs, float* row0,
+                                             int64_t row_stride, int nvalid) {
+  const int t = threadIdx.x & 31;
+  constexpr int J = C / 8;
+  constexpr int NG = NW == 32 ? 1 : 3;
+  float v[2][J][4];
 #pragma unroll
-  for (int i = 0; i < C / 4; ++i)
-    *(float4*)(rowp + cs * C + 4 * i) =
-        make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+  for (int hf = 0; hf < 2; ++hf)
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+      const uint32_t a = tcol + ((uint32_t)(32 * q + 16 * hf) << 16) + cs * C + 8 * j;
+      uint32_t r[NG][4];
+#pragma unroll
+      for (int g = 0; g < NG; ++g)
+        asm volatile("tcgen05.ld.sync.aligned.16x256b.x1.b32 {%0, %1, %2, %3}, [%4];"
+                     : "=r"(r[g][0]), "=r"(r[g][1]), "=r"(r[g][2]), "=r"(r[g][3])
+                     : "r"(a + 32 * g));
+      tld_wait();
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float x = __uint_as_float(r[0][e]);
+        if constexpr (NW == 96) x = (x + __uint_as_float(r[1][e])) + __uint_as_float(r[2][e]);
+        v[hf][j][e] = x;
+      }
+    }
+#pragma unroll
+  for (int hf = 0; hf < 2; ++hf)
+#pragma unroll
+    for (int sub = 0; sub < 2; ++sub) {
+      const int row = 32 * q + 16 * hf + 8 * sub + (t >> 2);
+      if (row < nvalid) {
+        float* rp = row0 + (int64_t)row * row_stride + cs * C + 2 * (t & 3);
+#pragma unroll
+        for (int j = 0; j < J; ++j)
+          *(float2*)(rp + 8 * j) = make_float2(v[hf][j][2 * sub], v[hf][j][2 * sub + 1]);
+      }
+    }
 }
 
 // ------------------------------------------------------------ MMA schedules
@@ -611,10 +675,39 @@ __device__ __forceinline__ void prefetch(const TcParams& p, uint8_t* st0, uint8_
   if (tile + p.P < p.ntiles) tma_tile(p, st0, st1, h, tile + p.P, b, bar);
 }
 
-// Per-kernel threads per point row and co-resident CTAs per SM (shared
-// memory, TMEM and registers sized for it).
-constexpr int kTSliceFwd = 2, kTDesliceFwd = 4, kTSliceBwd = 2, kTDesliceBwd = 4;
-constexpr int kCtasSliceFwd = 2, kCtasDesliceFwd = 2, kCtasSliceBwd = 2, kCtasDesliceBwd = 1;
+// Per-kernel threads per point row, co-resident CTAs per SM (shared memory,
+// TMEM and registers sized for it) and, for deslice forward, the width of its
+// wide products. Each can be set at build time (-DFS_TC_SF_T=... etc.).
+#ifndef FS_TC_SF_T
+#define FS_TC_SF_T 2
+#endif
+#ifndef FS_TC_SF_CTAS
+#define FS_TC_SF_CTAS 2
+#endif
+#ifndef FS_TC_DF_T
+#define FS_TC_DF_T 2
+#endif
+#ifndef FS_TC_DF_CTAS
+#define FS_TC_DF_CTAS 4
+#endif
+#ifndef FS_TC_DF_NW
+#define FS_TC_DF_NW 32
+#endif
+#ifndef FS_TC_SB_T
+#define FS_TC_SB_T 2
+#endif
+#ifndef FS_TC_SB_CTAS
+#define FS_TC_SB_CTAS 2
+#endif
+#ifndef FS_TC_DB_T
+#define FS_TC_DB_T 4
+#endif
+constexpr int kTSliceFwd = FS_TC_SF_T, kTDesliceFwd = FS_TC_DF_T, kTSliceBwd = FS_TC_SB_T,
+              kTDesliceBwd = FS_TC_DB_T;
+constexpr int kCtasSliceFwd = FS_TC_SF_CTAS, kCtasDesliceFwd = FS_TC_DF_CTAS,
+              kCtasSliceBwd = FS_TC_SB_CTAS, kCtasDesliceBwd = 1;
+constexpr int kNwDf = FS_TC_DF_NW;                 // 32 or 96
+constexpr int kDfCols = kNwDf == 32 ? 128 : 256;   // TMEM columns of deslice forward
 
 // ------------------------------------------------------------ slice forward
 // smem: [stage x][stage fx][WS split: w][F split: fx][W][bias][red][bars]
@@ -694,11 +787,12 @@ __global__ void __launch_bounds__(128 * kTSliceFwd, kCtasSliceFwd)
 }
 
 // ------------------------------------------------------------ deslice forward
-// smem: [stage x][W][tokens (stacked)][bias][red][bars]
-// TMEM (256 columns): logits -> out (N-stacked) at 0, the point operand (x,
-// then w) at 96.
+// smem: [stage x][W][tokens][bias][red][bars]
+// TMEM (kDfCols columns): logits -> out at 0 (NW columns), the point operand
+// (x, then w) after it.
+static_assert(kSmall == kSmallStk, "tokens buffer holds either layout");
 constexpr int kDfStageX = 0, kDfWs = kStage, kDfTs = kDfWs + kSmall,
-              kDfBias = kDfTs + kSmallStk, kDfRed = kDfBias + 128,
+              kDfBias = kDfTs + kSmall, kDfRed = kDfBias + 128,
               kDfBar = kDfRed + 2 * kTDesliceFwd * 512, kDfBytes = kDfBar + 64;
 
 __global__ void __launch_bounds__(128 * kTDesliceFwd, kCtasDesliceFwd)
@@ -708,16 +802,20 @@ __global__ void __launch_bounds__(128 * kTDesliceFwd, kCtasDesliceFwd)
   uint8_t* sm = align_smem(sm_raw);
   const Th<T> th;
   const int bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
-  Ctl c = prologue_begin<256>(sm, kDfBar);
+  Ctl c = prologue_begin<kDfCols>(sm, kDfBar);
   float* red0 = (float*)(sm + kDfRed);
   float* red1 = red0 + T * 128;
   put_small<NT>(sm + kDfWs, p.W + (int64_t)b * p.swb + (int64_t)h * p.swh);
-  put_small_stacked<NT>(sm + kDfTs, p.M + (int64_t)bh * 32 * 32);
+  if constexpr (kNwDf == 32)
+    put_small<NT>(sm + kDfTs, p.M + (int64_t)bh * 32 * 32);
+  else
+    put_small_stacked<NT>(sm + kDfTs, p.M + (int64_t)bh * 32 * 32);
   const RowConst rc = row_const<NT>((float*)(sm + kDfBias),
                                     p.bias + (int64_t)b * p.sbb + (int64_t)h * p.sbh, p.tau[h]);
   prologue_end(c);
-  const uint32_t tL = c.tmem, tA = c.tmem + 96;
-  const uint64_t dWs = desc_smallK(sm + kDfWs), dTs = desc_stacked(sm + kDfTs);
+  const uint32_t tL = c.tmem, tA = c.tmem + kNwDf;
+  const uint64_t dWs = desc_smallK(sm + kDfWs);
+  const uint64_t dTs = kNwDf == 32 ? desc_smallM(sm + kDfTs) : desc_stacked(sm + kDfTs);
   int tile = blockIdx.x;
   if (threadIdx.x == 0 && tile < p.ntiles)
     tma_tile(p, sm + kDfStageX, nullptr, h, tile, b, c.bar_tma);
@@ -734,31 +832,29 @@ __global__ void __launch_bounds__(128 * kTDesliceFwd, kCtasDesliceFwd)
     to_async_barrier();
     if (threadIdx.x == 0) {
       prefetch(p, sm + kDfStageX, nullptr, h, tile, b, c.bar_tma);
-      wide_ts<96, false>(tL, tA, dWs);  // logits = x W^T
+      wide_ts<kNwDf, false>(tL, tA, dWs);  // logits = x W^T
       mma_commit(c.bar_mma);
     }
     wait_mma(c.bar_mma, c.ph_mma, p.status);
     {
       float lg[C];
-      ld_wide<96, C>(tL + th.lane_off, th.cs, lg);
+      ld_wide<kNwDf, C>(tL + th.lane_off, th.cs, lg);
       softmax_cols<T, C>(lg, rc, true, nullptr, red0, red1, th);
       Split<C>(lg).to_tmem(tA + th.lane_off, th.cs);  // w, over the consumed x
       tst_wait();
     }
     to_async_barrier();
     if (threadIdx.x == 0) {
-      wide_ts<96, true>(tL, tA, dTs);  // out = w tokens, over the consumed logits
+      wide_ts<kNwDf, true>(tL, tA, dTs);  // out = w tokens, over the consumed logits
       mma_commit(c.bar_mma);
     }
     wait_mma(c.bar_mma, c.ph_mma, p.status);
-    float o[C];
-    ld_wide<96, C>(tL + th.lane_off, th.cs, o);
-    if (n0 + th.row < p.N)
-      store_cols<C>(p.out + (int64_t)b * p.so[0] + (int64_t)(n0 + th.row) * p.so[1] +
-                        (int64_t)h * p.so[2],
-                    th.cs, o);
+    store_result<kNwDf, C>(tL, th.q, th.cs,
+                           p.out + (int64_t)b * p.so[0] + (int64_t)n0 * p.so[1] +
+                               (int64_t)h * p.so[2],
+                           p.so[1], p.N - n0);
   }
-  epilogue<256>(c);
+  epilogue<kDfCols>(c);
 }
 
 // ------------------------------------------------------------ slice backward
@@ -852,19 +948,14 @@ __global__ void __launch_bounds__(128 * kTSliceBwd, kCtasSliceBwd)
       mma_commit(c.bar_mma);
     }
     wait_mma(c.bar_mma, c.ph_mma, p.status);
-    {
-      float v[C];
-      ld_wide<32, C>(tDfx + th.lane_off, th.cs, v);
-      if (valid)
-        store_cols<C>(p.out2 + (int64_t)b * p.so2[0] + (int64_t)(n0 + th.row) * p.so2[1] +
-                          (int64_t)h * p.so2[2],
-                      th.cs, v);
-      ld_wide<32, C>(tDx + th.lane_off, th.cs, v);
-      if (valid)
-        store_cols<C>(p.out + (int64_t)b * p.so[0] + (int64_t)(n0 + th.row) * p.so[1] +
-                          (int64_t)h * p.so[2],
-                      th.cs, v);
-    }
+    store_result<32, C>(tDfx, th.q, th.cs,
+                        p.out2 + (int64_t)b * p.so2[0] + (int64_t)n0 * p.so2[1] +
+                            (int64_t)h * p.so2[2],
+                        p.so2[1], p.N - n0);
+    store_result<32, C>(tDx, th.q, th.cs,
+                        p.out + (int64_t)b * p.so[0] + (int64_t)n0 * p.so[1] +
+                            (int64_t)h * p.so[2],
+                        p.so[1], p.N - n0);
     if (th.q < 3) drain_pool<C>(tP + th.lane_off, th.cs, accw);
   }
   const int64_t slot = (int64_t)bh * p.P + blockIdx.x;
@@ -968,14 +1059,10 @@ __global__ void __launch_bounds__(128 * kTDesliceBwd, kCtasDesliceBwd)
       mma_commit(c.bar_mma);
     }
     wait_mma(c.bar_mma, c.ph_mma, p.status);
-    {
-      float v[C];
-      ld_wide<96, C>(tL + th.lane_off, th.cs, v);
-      if (valid)
-        store_cols<C>(p.out + (int64_t)b * p.so[0] + (int64_t)(n0 + th.row) * p.so[1] +
-                          (int64_t)h * p.so[2],
-                      th.cs, v);
-    }
+    store_result<96, C>(tL, th.q, th.cs,
+                        p.out + (int64_t)b * p.so[0] + (int64_t)n0 * p.so[1] +
+                            (int64_t)h * p.so[2],
+                        p.so[1], p.N - n0);
     if (th.q < 3) {
       drain_pool<C>(tP1 + th.lane_off, th.cs, acct);
       drain_pool<C>(tP2 + th.lane_off, th.cs, accw);
@@ -1104,7 +1191,7 @@ static_assert((kDfBytes + kSmemPad + 1024) * kCtasDesliceFwd <= 228 * 1024, "des
 static_assert((kSbBytes + kSmemPad + 1024) * kCtasSliceBwd <= 228 * 1024, "slice bwd smem");
 static_assert(kDbBytes + kSmemPad <= 227 * 1024, "deslice bwd smem");
 // TMEM per SM (512 columns) holds the co-resident CTAs' allocations
-static_assert(256 * kCtasSliceFwd <= 512 && 256 * kCtasDesliceFwd <= 512 &&
+static_assert(256 * kCtasSliceFwd <= 512 && kDfCols * kCtasDesliceFwd <= 512 &&
                   256 * kCtasSliceBwd <= 512 && 512 * kCtasDesliceBwd <= 512,
               "TMEM columns");
 static_assert(kSfWS % 16 == 0 && kSfF % 16 == 0 && kSbUp % 16 == 0 && kDbUp % 16 == 0 &&
