@@ -700,12 +700,12 @@ __device__ __forceinline__ void prefetch(const TcParams& p, uint8_t* st0, uint8_
 #define FS_TC_SB_CTAS 2
 #endif
 #ifndef FS_TC_DB_T
-#define FS_TC_DB_T 4
+#define FS_TC_DB_T 2
 #endif
 constexpr int kTSliceFwd = FS_TC_SF_T, kTDesliceFwd = FS_TC_DF_T, kTSliceBwd = FS_TC_SB_T,
               kTDesliceBwd = FS_TC_DB_T;
 constexpr int kCtasSliceFwd = FS_TC_SF_CTAS, kCtasDesliceFwd = FS_TC_DF_CTAS,
-              kCtasSliceBwd = FS_TC_SB_CTAS, kCtasDesliceBwd = 1;
+              kCtasSliceBwd = FS_TC_SB_CTAS, kCtasDesliceBwd = 2;
 constexpr int kNwDf = FS_TC_DF_NW;                 // 32 or 96
 constexpr int kDfCols = kNwDf == 32 ? 128 : 256;   // TMEM columns of deslice forward
 
@@ -969,16 +969,19 @@ __global__ void __launch_bounds__(128 * kTSliceBwd, kCtasSliceBwd)
 }
 
 // ------------------------------------------------------------ deslice backward
-// smem: [stage x][stage dout][X split][O split: dout][WP split: w][UP split: dl/tau]
-//       [W][W stacked][tokens][bias][red][bars]
-// TMEM (512 columns): logits -> dx (N-stacked) at 0, dw at 96, the dtokens
-// pool at 192 and the dW pool at 288, point operands x -> dl/tau at 384 and
-// dout at 432.
-constexpr int kDbStageX = 0, kDbStageO = kStage, kDbX = 2 * kStage, kDbO = kDbX + kSplit,
-              kDbWp = kDbO + kSplit, kDbUp = kDbWp + kSplit + kTail,
-              kDbWs = kDbUp + kSplit + kTail, kDbWst = kDbWs + kSmall,
-              kDbTs = kDbWst + kSmallStk, kDbBias = kDbTs + kSmall, kDbRed = kDbBias + 128,
-              kDbBar = kDbRed + 3 * kTDesliceBwd * 512, kDbBytes = kDbBar + 64;
+// Sized for two CTAs per SM (shared memory 111 KB, TMEM 224 columns).
+// smem: [X split][O split: dout][WP split: w | stage x][UP split: dl/tau |
+//       stage dout][W][tokens][bias][red][bars]
+// The staging tiles share the pool operands' buffers: the next tile's x is
+// loaded into WP once the dtokens pool is done with it, its d_out into UP
+// once the dW pool is.
+// TMEM: logits (N-stacked) at 0, dw at 96, point operands x -> dl/tau at
+// 128 and dout at 176; then dx at 0 and one pool at 32 (dtokens, then dW).
+constexpr int kDbX = 0, kDbO = kSplit, kDbWp = 2 * kSplit, kDbUp = 3 * kSplit,
+              kDbWs = 4 * kSplit, kDbTs = kDbWs + kSmall, kDbBias = kDbTs + kSmall,
+              kDbRed = kDbBias + 128, kDbBar = kDbRed + 3 * kTDesliceBwd * 512,
+              kDbBytes = kDbBar + 64;
+static_assert(kDbWp % 1024 == 0 && kDbUp % 1024 == 0, "staging tiles need 1 KB alignment");
 
 __global__ void __launch_bounds__(128 * kTDesliceBwd, kCtasDesliceBwd)
     k_tc_deslice_bwd(const __grid_constant__ TcParams p) {
@@ -987,39 +990,39 @@ __global__ void __launch_bounds__(128 * kTDesliceBwd, kCtasDesliceBwd)
   uint8_t* sm = align_smem(sm_raw);
   const Th<T> th;
   const int bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
-  Ctl c = prologue_begin<512>(sm, kDbBar);
+  Ctl c = prologue_begin<256>(sm, kDbBar);
   float* red0 = (float*)(sm + kDbRed);
   float* red1 = red0 + T * 128;
   float* red2 = red1 + T * 128;
-  const float* Wb = p.W + (int64_t)b * p.swb + (int64_t)h * p.swh;
-  put_small<NT>(sm + kDbWs, Wb);
-  put_small_stacked<NT>(sm + kDbWst, Wb);
+  put_small<NT>(sm + kDbWs, p.W + (int64_t)b * p.swb + (int64_t)h * p.swh);
   put_small<NT>(sm + kDbTs, p.M + (int64_t)bh * 32 * 32);
   const RowConst rc = row_const<NT>((float*)(sm + kDbBias),
                                     p.bias + (int64_t)b * p.sbb + (int64_t)h * p.sbh, p.tau[h]);
   const float inv_tau = __frcp_rn(p.tau[h]);
   prologue_end(c);
-  const uint32_t tL = c.tmem, tDw = c.tmem + 96, tP1 = c.tmem + 192, tP2 = c.tmem + 288,
-                 tX = c.tmem + 384, tO = c.tmem + 432;
+  const uint32_t tL = c.tmem, tDw = c.tmem + 96, tX = c.tmem + 128, tO = c.tmem + 176;
+  const uint32_t tDx = c.tmem, tP = c.tmem + 32;
   const uint64_t dXb = desc_stacked(sm + kDbX), dOb = desc_stacked(sm + kDbO),
                  dWp = desc_stacked(sm + kDbWp), dUp = desc_stacked(sm + kDbUp);
-  const uint64_t dWk = desc_smallK(sm + kDbWs), dWst = desc_stacked(sm + kDbWst),
+  const uint64_t dWk = desc_smallK(sm + kDbWs), dWm = desc_smallM(sm + kDbWs),
                  dTk = desc_smallK(sm + kDbTs);
+  uint8_t* stX = sm + kDbWp;
+  uint8_t* stO = sm + kDbUp;
   float acct[C], accw[C], accb[C], dt_acc = 0.f;
 #pragma unroll
   for (int i = 0; i < C; ++i) acct[i] = accw[i] = accb[i] = 0.f;
   int tile = blockIdx.x;
-  if (threadIdx.x == 0 && tile < p.ntiles)
-    tma_tile(p, sm + kDbStageX, sm + kDbStageO, h, tile, b, c.bar_tma);
+  if (threadIdx.x == 0 && tile < p.ntiles) tma_tile(p, stX, stO, h, tile, b, c.bar_tma);
   for (; tile < p.ntiles; tile += p.P) {
     const int n0 = tile * kTile;
     const bool valid = n0 + th.row < p.N;
+    const bool more = tile + p.P < p.ntiles;
     mbar_wait(c.bar_tma, c.ph_tma, p.status);
     c.ph_tma ^= 1;
     {
       float x[C], o[C];
-      read_cols<C>(sm + kDbStageX, th.row, th.cs, x);
-      read_cols<C>(sm + kDbStageO, th.row, th.cs, o);
+      read_cols<C>(stX, th.row, th.cs, x);
+      read_cols<C>(stO, th.row, th.cs, o);
       const Split<C> xs(x);
       xs.to_smem(sm + kDbX, th.row, th.cs);
       xs.to_tmem(tX + th.lane_off, th.cs);
@@ -1030,9 +1033,8 @@ __global__ void __launch_bounds__(128 * kTDesliceBwd, kCtasDesliceBwd)
     }
     to_async_barrier();
     if (threadIdx.x == 0) {
-      prefetch(p, sm + kDbStageX, sm + kDbStageO, h, tile, b, c.bar_tma);
       wide_ts<96, false>(tL, tX, dWk);   // logits = x W^T
-      wide_ts<96, false>(tDw, tO, dTk);  // dw = d_out tok^T
+      wide_ts<32, false>(tDw, tO, dTk);  // dw = d_out tok^T
       mma_commit(c.bar_mma);
     }
     wait_mma(c.bar_mma, c.ph_mma, p.status);
@@ -1040,33 +1042,44 @@ __global__ void __launch_bounds__(128 * kTDesliceBwd, kCtasDesliceBwd)
       float w[C], lgc[C], dw[C];
       ld_wide<96, C>(tL + th.lane_off, th.cs, w);
       softmax_cols<T, C>(w, rc, valid, lgc, red0, red1, th);
-      ld_wide<96, C>(tDw + th.lane_off, th.cs, dw);
+      ld_wide<32, C>(tDw + th.lane_off, th.cs, dw);
       const float rdt = jacobian_cols<T, C>(w, dw, lgc, inv_tau, red2, th);
       if (valid) dt_acc += rdt;
-      Split<C>(w).to_smem(sm + kDbWp, th.row, th.cs);
-      const Split<C> us(dw);  // dl / tau
-      us.to_smem(sm + kDbUp, th.row, th.cs);
-      us.to_tmem(tX + th.lane_off, th.cs);  // over the consumed x
+      Split<C>(w).to_smem(sm + kDbWp, th.row, th.cs);  // over the consumed x stage
+      const Split<C> us(dw);                            // dl / tau
+      us.to_smem(sm + kDbUp, th.row, th.cs);           // over the consumed dout stage
+      us.to_tmem(tX + th.lane_off, th.cs);             // over the consumed x operand
 #pragma unroll
       for (int k = 0; k < C / 2; ++k) put2(accb, k, __fadd2_rn(f2(accb, k), f2(dw, k)));
       tst_wait();
     }
     to_async_barrier();
     if (threadIdx.x == 0) {
-      wide_ts<96, true>(tL, tX, dWst);  // dx = (dl/tau) W
-      mma_pool(tP1, dWp, dOb);          // dtokens += w^T d_out
-      mma_pool(tP2, dUp, dXb);          // dW += (dl/tau)^T x
+      wide_ts<32, true>(tDx, tX, dWm);  // dx = (dl/tau) W
+      mma_pool(tP, dWp, dOb);           // dtokens += w^T d_out
       mma_commit(c.bar_mma);
     }
     wait_mma(c.bar_mma, c.ph_mma, p.status);
-    store_result<96, C>(tL, th.q, th.cs,
+    store_result<32, C>(tDx, th.q, th.cs,
                         p.out + (int64_t)b * p.so[0] + (int64_t)n0 * p.so[1] +
                             (int64_t)h * p.so[2],
                         p.so[1], p.N - n0);
-    if (th.q < 3) {
-      drain_pool<C>(tP1 + th.lane_off, th.cs, acct);
-      drain_pool<C>(tP2 + th.lane_off, th.cs, accw);
+    if (th.q < 3) drain_pool<C>(tP + th.lane_off, th.cs, acct);
+    tc_fence_before();
+    __syncthreads();  // the pool region is read out; WP is free
+    tc_fence_after();
+    if (threadIdx.x == 0) {
+      if (more) {
+        mbar_arrive_expect_tx(c.bar_tma, 2 * kStage);
+        tma_load_4d(stX, &p.mx, 0, h, (tile + p.P) * kTile, b, c.bar_tma);
+      }
+      mma_pool(tP, dUp, dXb);  // dW += (dl/tau)^T x
+      mma_commit(c.bar_mma);
     }
+    wait_mma(c.bar_mma, c.ph_mma, p.status);
+    if (threadIdx.x == 0 && more)  // UP is free once the dW pool is done
+      tma_load_4d(stO, &p.mv, 0, h, (tile + p.P) * kTile, b, c.bar_tma);
+    if (th.q < 3) drain_pool<C>(tP + th.lane_off, th.cs, accw);
   }
   const int64_t slot = (int64_t)bh * p.P + blockIdx.x;
   float* xch = (float*)(sm + kDbX);
@@ -1076,7 +1089,7 @@ __global__ void __launch_bounds__(128 * kTDesliceBwd, kCtasDesliceBwd)
   rowsum_write<T>(xch, accb, p.partS + slot * 32, th);
   const float tot = cta_sum_nt<NT>(dt_acc, (float*)(sm + kDbO));
   if (threadIdx.x == 0) p.partDt[slot] = -inv_tau * kLn2 * tot;
-  epilogue<512>(c);
+  epilogue<256>(c);
 }
 
 // ------------------------------------------------------------ host side
@@ -1189,13 +1202,13 @@ int tc_ctas_per_sm(TcKind k) {
 static_assert((kSfBytes + kSmemPad + 1024) * kCtasSliceFwd <= 228 * 1024, "slice fwd smem");
 static_assert((kDfBytes + kSmemPad + 1024) * kCtasDesliceFwd <= 228 * 1024, "deslice fwd smem");
 static_assert((kSbBytes + kSmemPad + 1024) * kCtasSliceBwd <= 228 * 1024, "slice bwd smem");
-static_assert(kDbBytes + kSmemPad <= 227 * 1024, "deslice bwd smem");
+static_assert((kDbBytes + kSmemPad + 1024) * kCtasDesliceBwd <= 228 * 1024, "deslice bwd smem");
 // TMEM per SM (512 columns) holds the co-resident CTAs' allocations
 static_assert(256 * kCtasSliceFwd <= 512 && kDfCols * kCtasDesliceFwd <= 512 &&
-                  256 * kCtasSliceBwd <= 512 && 512 * kCtasDesliceBwd <= 512,
+                  256 * kCtasSliceBwd <= 512 && 256 * kCtasDesliceBwd <= 512,
               "TMEM columns");
 static_assert(kSfWS % 16 == 0 && kSfF % 16 == 0 && kSbUp % 16 == 0 && kDbUp % 16 == 0 &&
-                  kDfTs % 16 == 0 && kDbWst % 16 == 0,
+                  kDfTs % 16 == 0,
               "operand alignment");
 
 }  // namespace tcx
