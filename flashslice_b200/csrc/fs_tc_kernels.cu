@@ -107,29 +107,6 @@ __device__ __forceinline__ void named_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
-// Combine one value per thread across the T threads of a row (fixed order).
-// `red` holds T * 128 floats and is not reused until a CTA-wide barrier.
-template <int T, bool MAX>
-__device__ __forceinline__ float row_combine(float v, float* red, const Th<T>& th) {
-  if constexpr (T == 1) {
-    return v;
-  } else {
-    red[th.cs * 128 + th.row] = v;
-    named_sync(1 + th.q, 32 * T);
-    float r[T];
-#pragma unroll
-    for (int c = 0; c < T; ++c) r[c] = red[c * 128 + th.row];
-    if constexpr (MAX) {
-      float m = r[0];
-#pragma unroll
-      for (int c = 1; c < T; ++c) m = fmaxf(m, r[c]);
-      return m;
-    } else {
-      return tree_sum(r);
-    }
-  }
-}
-
 // ------------------------------------------------------------ paired fp32
 __device__ __forceinline__ float2 f2(const float* v, int k) { return make_float2(v[2 * k], v[2 * k + 1]); }
 __device__ __forceinline__ void put2(float* v, int k, float2 x) {
@@ -357,26 +334,21 @@ __device__ __forceinline__ void store_result(uint32_t tcol, int q, int cs, float
   const int t = threadIdx.x & 31;
   constexpr int J = C / 8;
   constexpr int NG = NW == 32 ? 1 : 3;
-  float v[2][J][4];
+  uint32_t r[2][J][NG][4];
 #pragma unroll
   for (int hf = 0; hf < 2; ++hf)
 #pragma unroll
-    for (int j = 0; j < J; ++j) {
-      const uint32_t a = tcol + ((uint32_t)(32 * q + 16 * hf) << 16) + cs * C + 8 * j;
-      uint32_t r[NG][4];
+    for (int j = 0; j < J; ++j)
 #pragma unroll
-      for (int g = 0; g < NG; ++g)
+      for (int g = 0; g < NG; ++g) {
+        const uint32_t a =
+            tcol + ((uint32_t)(32 * q + 16 * hf) << 16) + cs * C + 8 * j + 32 * g;
         asm volatile("tcgen05.ld.sync.aligned.16x256b.x1.b32 {%0, %1, %2, %3}, [%4];"
-                     : "=r"(r[g][0]), "=r"(r[g][1]), "=r"(r[g][2]), "=r"(r[g][3])
-                     : "r"(a + 32 * g));
-      tld_wait();
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        float x = __uint_as_float(r[0][e]);
-        if constexpr (NW == 96) x = (x + __uint_as_float(r[1][e])) + __uint_as_float(r[2][e]);
-        v[hf][j][e] = x;
+                     : "=r"(r[hf][j][g][0]), "=r"(r[hf][j][g][1]), "=r"(r[hf][j][g][2]),
+                       "=r"(r[hf][j][g][3])
+                     : "r"(a));
       }
-    }
+  tld_wait();
 #pragma unroll
   for (int hf = 0; hf < 2; ++hf)
 #pragma unroll
@@ -385,8 +357,17 @@ __device__ __forceinline__ void store_result(uint32_t tcol, int q, int cs, float
       if (row < nvalid) {
         float* rp = row0 + (int64_t)row * row_stride + cs * C + 2 * (t & 3);
 #pragma unroll
-        for (int j = 0; j < J; ++j)
-          *(float2*)(rp + 8 * j) = make_float2(v[hf][j][2 * sub], v[hf][j][2 * sub + 1]);
+        for (int j = 0; j < J; ++j) {
+          float2 v = make_float2(__uint_as_float(r[hf][j][0][2 * sub]),
+                                 __uint_as_float(r[hf][j][0][2 * sub + 1]));
+          if constexpr (NW == 96) {
+            v = __fadd2_rn(v, make_float2(__uint_as_float(r[hf][j][1][2 * sub]),
+                                          __uint_as_float(r[hf][j][1][2 * sub + 1])));
+            v = __fadd2_rn(v, make_float2(__uint_as_float(r[hf][j][2][2 * sub]),
+                                          __uint_as_float(r[hf][j][2][2 * sub + 1])));
+          }
+          *(float2*)(rp + 8 * j) = v;
+        }
       }
     }
 }
@@ -473,11 +454,22 @@ __device__ __forceinline__ void to_async_barrier() {
   tc_fence_after();
 }
 
-__device__ __forceinline__ void wait_mma(uint64_t* bar, uint32_t& phase, int* status) {
-  mbar_wait(bar, phase, status);
-  phase ^= 1;
+// Kernel control block: the TMA barrier and up to five MMA-completion
+// barriers (one per group of MMAs committed together), each completing once
+// per tile, with their phases.
+constexpr int kNumBars = 6;
+struct Ctl {
+  uint64_t* bar;  // [0] TMA, [1..5] MMA groups
+  uint32_t tmem;
+  uint32_t ph[kNumBars];
+};
+
+__device__ __forceinline__ void wait_bar(Ctl& c, int k, int* status) {
+  mbar_wait(c.bar + k, c.ph[k], status);
+  c.ph[k] ^= 1;
   tc_fence_after();
 }
+__device__ __forceinline__ void commit(Ctl& c, int k) { mma_commit(c.bar + k); }
 
 // ------------------------------------------------------------ row math
 // Per-head row constants in shared memory: the logit scale in log2 units
@@ -495,54 +487,113 @@ __device__ __forceinline__ RowConst row_const(float* bias_s, const float* bias, 
   return RowConst{scale, bias_s};
 }
 
-// raw logits (x W^T) -> softmax weights in place (rows past N get zero
-// weights); keeps the centred logit in log2 units, (logit - rowmax) log2(e),
-// in lgc when given
-template <int T, int C>
-__device__ __forceinline__ void softmax_cols(float (&lg)[C], const RowConst& rc, bool valid,
-                                             float* lgc, float* red0, float* red1,
-                                             const Th<T>& th) {
+// Row statistics combined across the T threads of a row in one exchange
+// (fixed order): the row maximum m of the scaled logits, s = sum 2^(l - m)
+// and u = sum 2^(l - m) dw. Each thread contributes its columns' values
+// relative to its own maximum; `red` holds 3 T 128 floats, not reused until
+// a CTA-wide barrier.
+struct RowStat {
+  float m, s, u;
+};
+template <int T, bool U>
+__device__ __forceinline__ RowStat row_stat(float ml, float sl, float ul, float* red,
+                                            const Th<T>& th) {
+  if constexpr (T == 1) {
+    return RowStat{ml, sl, ul};
+  } else {
+    red[th.cs * 128 + th.row] = ml;
+    red[(T + th.cs) * 128 + th.row] = sl;
+    if (U) red[(2 * T + th.cs) * 128 + th.row] = ul;
+    named_sync(1 + th.q, 32 * T);
+    float mt[T], st[T], ut[T];
+#pragma unroll
+    for (int c = 0; c < T; ++c) {
+      mt[c] = red[c * 128 + th.row];
+      st[c] = red[(T + c) * 128 + th.row];
+      ut[c] = U ? red[(2 * T + c) * 128 + th.row] : 0.f;
+    }
+    float m = mt[0];
+#pragma unroll
+    for (int c = 1; c < T; ++c) m = fmaxf(m, mt[c]);
+#pragma unroll
+    for (int c = 0; c < T; ++c) {
+      const float f = exp2f(mt[c] - m);
+      st[c] *= f;
+      ut[c] *= f;
+    }
+    return RowStat{m, tree_sum(st), U ? tree_sum(ut) : 0.f};
+  }
+}
+
+// raw logits (x W^T) -> scaled logits relative to this thread's maximum:
+// d = l - max, e = 2^d; returns the thread's maximum
+template <int C>
+__device__ __forceinline__ float row_exp(const float (&acc)[C], const RowConst& rc, int cs,
+                                         float (&d)[C], float (&e)[C]) {
   const float2 sc = make_float2(rc.scale, rc.scale);
-  const float2* b2 = (const float2*)(rc.bias2 + th.cs * C);
-  float m = -INFINITY;
+  const float2* b2 = (const float2*)(rc.bias2 + cs * C);
+  float mx[C / 2];
 #pragma unroll
   for (int k = 0; k < C / 2; ++k) {
-    const float2 v = __ffma2_rn(f2(lg, k), sc, b2[k]);
-    put2(lg, k, v);
-    m = fmaxf(m, fmaxf(v.x, v.y));
+    const float2 v = __ffma2_rn(f2(acc, k), sc, b2[k]);
+    put2(d, k, v);
+    mx[k] = fmaxf(v.x, v.y);
   }
-  m = row_combine<T, true>(m, red0, th);
+#pragma unroll
+  for (int s = C / 4; s > 0; s >>= 1)
+#pragma unroll
+    for (int i = 0; i < s; ++i) mx[i] = fmaxf(mx[i], mx[i + s]);
+  const float m = mx[0];
   const float2 nm = make_float2(-m, -m);
 #pragma unroll
   for (int k = 0; k < C / 2; ++k) {
-    const float2 d = __fadd2_rn(f2(lg, k), nm);
-    if (lgc) put2(lgc, k, d);
-    put2(lg, k, make_float2(exp2f(d.x), exp2f(d.y)));
+    const float2 v = __fadd2_rn(f2(d, k), nm);
+    put2(d, k, v);
+    put2(e, k, make_float2(exp2f(v.x), exp2f(v.y)));
   }
-  const float s = row_combine<T, false>(tree_sum2(lg), red1, th);
-  const float r = valid ? __frcp_rn(s) : 0.f;
-  const float2 r2 = make_float2(r, r);
-#pragma unroll
-  for (int k = 0; k < C / 2; ++k) put2(lg, k, __fmul2_rn(f2(lg, k), r2));
+  return m;
 }
 
-// softmax Jacobian of one row: dl = w (dw - sum w dw); returns this thread's
-// part of sum_g dl lgc (centred: sum_g dl = 0 exactly, so this is sum_g dl *
-// logit without a common offset multiplying the rounding residue of sum_g
-// dl; in log2 units) and leaves dl / tau in dw
+// Softmax (forward): raw logits -> weights in place (rows past N get zero
+// weights). One exchange per row.
 template <int T, int C>
-__device__ __forceinline__ float jacobian_cols(const float (&w)[C], float (&dw)[C],
-                                               const float (&lgc)[C], float inv_tau, float* red,
-                                               const Th<T>& th) {
-  float tmp[C];
+__device__ __forceinline__ void softmax_fwd(float (&lg)[C], const RowConst& rc, bool valid,
+                                            float* red, const Th<T>& th) {
+  float d[C], e[C];
+  const float ml = row_exp<C>(lg, rc, th.cs, d, e);
+  const RowStat st = row_stat<T, false>(ml, tree_sum2(e), 0.f, red, th);
+  const float f = valid ? exp2f(ml - st.m) / st.s : 0.f;
+  const float2 f2v = make_float2(f, f);
 #pragma unroll
-  for (int k = 0; k < C / 2; ++k) put2(tmp, k, __fmul2_rn(f2(w, k), f2(dw, k)));
-  const float gs = row_combine<T, false>(tree_sum2(tmp), red, th);
-  const float2 ng = make_float2(-gs, -gs), it = make_float2(inv_tau, inv_tau);
+  for (int k = 0; k < C / 2; ++k) put2(lg, k, __fmul2_rn(f2(e, k), f2v));
+}
+
+// Softmax and its Jacobian (backward) in one exchange per row: raw logits in
+// lg -> weights w; upstream dw -> dl / tau with dl = w (dw - sum w dw).
+// Returns this thread's part of sum_g dl (logit - rowmax), in log2 units
+// (centred: sum_g dl = 0 exactly, so this is sum_g dl * logit without a
+// common offset multiplying the rounding residue of sum_g dl).
+template <int T, int C>
+__device__ __forceinline__ float softmax_bwd(float (&lg)[C], float (&dw)[C], const RowConst& rc,
+                                             float inv_tau, bool valid, float* red,
+                                             const Th<T>& th) {
+  float d[C], e[C], tmp[C];
+  const float ml = row_exp<C>(lg, rc, th.cs, d, e);
+#pragma unroll
+  for (int k = 0; k < C / 2; ++k) put2(tmp, k, __fmul2_rn(f2(e, k), f2(dw, k)));
+  const RowStat st = row_stat<T, true>(ml, tree_sum2(e), tree_sum2(tmp), red, th);
+  const float dm = ml - st.m;
+  const float rs = __frcp_rn(st.s);
+  const float f = valid ? exp2f(dm) * rs : 0.f;
+  const float gs = st.u * rs;
+  const float2 f2v = make_float2(f, f), ng = make_float2(-gs, -gs), dm2 = make_float2(dm, dm),
+               it = make_float2(inv_tau, inv_tau);
 #pragma unroll
   for (int k = 0; k < C / 2; ++k) {
-    const float2 dl = __fmul2_rn(f2(w, k), __fadd2_rn(f2(dw, k), ng));
-    put2(tmp, k, __fmul2_rn(dl, f2(lgc, k)));
+    const float2 w = __fmul2_rn(f2(e, k), f2v);
+    put2(lg, k, w);
+    const float2 dl = __fmul2_rn(w, __fadd2_rn(f2(dw, k), ng));
+    put2(tmp, k, __fmul2_rn(dl, __fadd2_rn(f2(d, k), dm2)));
     put2(dw, k, __fmul2_rn(dl, it));
   }
   return tree_sum2(tmp);
@@ -613,19 +664,13 @@ __device__ __forceinline__ float cta_sum_nt(float v, float* red) {
 }
 
 // ------------------------------------------------------------ prologue
-struct Ctl {
-  uint64_t* bar_tma;
-  uint64_t* bar_mma;
-  uint32_t tmem;
-  uint32_t ph_tma, ph_mma;
-};
+constexpr int kBarBytes = 128;  // kNumBars mbarriers and the TMEM address slot
 
 template <int NCOLS>
 __device__ __forceinline__ Ctl prologue_begin(uint8_t* sm, int bar_off) {
   Ctl c;
-  c.bar_tma = (uint64_t*)(sm + bar_off);
-  c.bar_mma = c.bar_tma + 1;
-  uint32_t* tslot = (uint32_t*)(c.bar_tma + 2);
+  c.bar = (uint64_t*)(sm + bar_off);
+  uint32_t* tslot = (uint32_t*)(c.bar + kNumBars);
   if ((threadIdx.x >> 5) == 0) {
     tmem_alloc(tslot, NCOLS);
     // Give up the right to allocate again: until a CTA does, the SM admits
@@ -634,18 +679,19 @@ __device__ __forceinline__ Ctl prologue_begin(uint8_t* sm, int bar_off) {
     tmem_relinquish();
   }
   if (threadIdx.x == 0) {
-    mbar_init(c.bar_tma, 1);
-    mbar_init(c.bar_mma, 1);
+#pragma unroll
+    for (int k = 0; k < kNumBars; ++k) mbar_init(c.bar + k, 1);
     fence_barrier_init();
   }
-  c.ph_tma = c.ph_mma = 0;
+#pragma unroll
+  for (int k = 0; k < kNumBars; ++k) c.ph[k] = 0;
   c.tmem = 0;
   return c;
 }
 
 __device__ __forceinline__ void prologue_end(Ctl& c) {
   to_async_barrier();
-  c.tmem = *(const uint32_t*)(c.bar_tma + 2);
+  c.tmem = *(const uint32_t*)(c.bar + kNumBars);
 }
 
 template <int NCOLS>
@@ -679,10 +725,7 @@ __device__ __forceinline__ void prefetch(const TcParams& p, uint8_t* st0, uint8_
 // TMEM and registers sized for it) and, for deslice forward, the width of its
 // wide products. Each can be set at build time (-DFS_TC_SF_T=... etc.).
 #ifndef FS_TC_SF_T
-#define FS_TC_SF_T 2
-#endif
-#ifndef FS_TC_SF_CTAS
-#define FS_TC_SF_CTAS 2
+#define FS_TC_SF_T 1
 #endif
 #ifndef FS_TC_DF_T
 #define FS_TC_DF_T 2
@@ -696,29 +739,33 @@ __device__ __forceinline__ void prefetch(const TcParams& p, uint8_t* st0, uint8_
 #ifndef FS_TC_SB_T
 #define FS_TC_SB_T 2
 #endif
-#ifndef FS_TC_SB_CTAS
-#define FS_TC_SB_CTAS 2
-#endif
 #ifndef FS_TC_DB_T
 #define FS_TC_DB_T 2
 #endif
 constexpr int kTSliceFwd = FS_TC_SF_T, kTDesliceFwd = FS_TC_DF_T, kTSliceBwd = FS_TC_SB_T,
               kTDesliceBwd = FS_TC_DB_T;
-constexpr int kCtasSliceFwd = FS_TC_SF_CTAS, kCtasDesliceFwd = FS_TC_DF_CTAS,
-              kCtasSliceBwd = FS_TC_SB_CTAS, kCtasDesliceBwd = 2;
+constexpr int kCtasSliceFwd = 2, kCtasDesliceFwd = FS_TC_DF_CTAS, kCtasSliceBwd = 2,
+              kCtasDesliceBwd = 2;
 constexpr int kNwDf = FS_TC_DF_NW;                 // 32 or 96
 constexpr int kDfCols = kNwDf == 32 ? 128 : 256;   // TMEM columns of deslice forward
 
+// MMA-completion barrier groups
+enum : int { kBarTma = 0, kG1 = 1, kG2 = 2, kG3 = 3, kG4 = 4, kG5 = 5 };
+
+// bytes of the row-statistics exchange for T threads per row and n values
+__host__ __device__ constexpr int red_bytes(int T, int n) { return T == 1 ? 0 : n * T * 512; }
+
 // ------------------------------------------------------------ slice forward
-// smem: [stage x][stage fx][WS split: w][F split: fx][W][bias][red][bars]
+// smem: [stage x][stage fx][WS split: w][F split: fx, two tiles][W][bias][red][bars]
 // TMEM (256 columns): logits (N-stacked) at 0, z pool at 96, the x point
-// operand at 192. TMEM a thread writes at the start of a tile is disjoint
-// from every column read at the end of the previous one: a warp that is done
-// with a tile may write while another warp of the same lanes still reads.
-constexpr int kSfStageX = 0, kSfStageF = kStage, kSfWS = 2 * kStage,
-              kSfF = kSfWS + kSplit + kTail, kSfWs = kSfF + kSplit, kSfBias = kSfWs + kSmall,
-              kSfRed = kSfBias + 128, kSfBar = kSfRed + 2 * kTSliceFwd * 512,
-              kSfBytes = kSfBar + 64;
+// operand at 192.
+// The loop is skewed by one stage: while the tensor core forms tile i's pool,
+// the threads split tile i+1 (into the other F buffer) and issue its logits;
+// the pool is drained while those run.
+// (WS needs no tail: its M-stacked reads past the end land in F.)
+constexpr int kSfStageX = 0, kSfStageF = kStage, kSfWS = 2 * kStage, kSfF = kSfWS + kSplit,
+              kSfWs = kSfF + 2 * kSplit, kSfBias = kSfWs + kSmall, kSfRed = kSfBias + 128,
+              kSfBar = kSfRed + red_bytes(kTSliceFwd, 2), kSfBytes = kSfBar + kBarBytes;
 
 __global__ void __launch_bounds__(128 * kTSliceFwd, kCtasSliceFwd)
     k_tc_slice_fwd(const __grid_constant__ TcParams p) {
@@ -728,54 +775,62 @@ __global__ void __launch_bounds__(128 * kTSliceFwd, kCtasSliceFwd)
   const Th<T> th;
   const int bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
   Ctl c = prologue_begin<256>(sm, kSfBar);
-  float* red0 = (float*)(sm + kSfRed);
-  float* red1 = red0 + T * 128;
+  float* red = (float*)(sm + kSfRed);
   put_small<NT>(sm + kSfWs, p.W + (int64_t)b * p.swb + (int64_t)h * p.swh);
   const RowConst rc = row_const<NT>((float*)(sm + kSfBias),
                                     p.bias + (int64_t)b * p.sbb + (int64_t)h * p.sbh, p.tau[h]);
   prologue_end(c);
   const uint32_t tL = c.tmem, tP = c.tmem + 96, tX = c.tmem + 192;
-  const uint64_t dWs = desc_smallK(sm + kSfWs);
-  const uint64_t dWp = desc_stacked(sm + kSfWS), dFp = desc_stacked(sm + kSfF);
+  const uint64_t dWs = desc_smallK(sm + kSfWs), dWp = desc_stacked(sm + kSfWS);
   float accz[C], accs[C];
 #pragma unroll
   for (int i = 0; i < C; ++i) accz[i] = accs[i] = 0.f;
-  int tile = blockIdx.x;
-  if (threadIdx.x == 0 && tile < p.ntiles)
-    tma_tile(p, sm + kSfStageX, sm + kSfStageF, h, tile, b, c.bar_tma);
-  for (; tile < p.ntiles; tile += p.P) {
+  // split one tile's rows from the staging buffers (x into TMEM, fx into F[buf])
+  auto split_tile = [&](int buf) {
+    wait_bar(c, kBarTma, p.status);
+    float x[C], f[C];
+    read_cols<C>(sm + kSfStageX, th.row, th.cs, x);
+    read_cols<C>(sm + kSfStageF, th.row, th.cs, f);
+    Split<C>(x).to_tmem(tX + th.lane_off, th.cs);
+    Split<C>(f).to_smem(sm + kSfF + buf * kSplit, th.row, th.cs);
+    tst_wait();
+  };
+  int tile = blockIdx.x, buf = 0;
+  if (threadIdx.x == 0) tma_tile(p, sm + kSfStageX, sm + kSfStageF, h, tile, b, c.bar);
+  split_tile(0);
+  to_async_barrier();
+  if (threadIdx.x == 0) {
+    prefetch(p, sm + kSfStageX, sm + kSfStageF, h, tile, b, c.bar);
+    wide_ts<96, false>(tL, tX, dWs);  // logits = x W^T
+    commit(c, kG1);
+  }
+  for (; tile < p.ntiles; tile += p.P, buf ^= 1) {
     const int n0 = tile * kTile;
-    mbar_wait(c.bar_tma, c.ph_tma, p.status);
-    c.ph_tma ^= 1;
-    {
-      float x[C], f[C];
-      read_cols<C>(sm + kSfStageX, th.row, th.cs, x);
-      read_cols<C>(sm + kSfStageF, th.row, th.cs, f);
-      Split<C>(x).to_tmem(tX + th.lane_off, th.cs);
-      Split<C>(f).to_smem(sm + kSfF, th.row, th.cs);
-      tst_wait();
-    }
-    to_async_barrier();
-    if (threadIdx.x == 0) {
-      prefetch(p, sm + kSfStageX, sm + kSfStageF, h, tile, b, c.bar_tma);
-      wide_ts<96, false>(tL, tX, dWs);  // logits = x W^T
-      mma_commit(c.bar_mma);
-    }
-    wait_mma(c.bar_mma, c.ph_mma, p.status);
+    const bool more = tile + p.P < p.ntiles;
+    wait_bar(c, kG1, p.status);
     {
       float lg[C];
       ld_wide<96, C>(tL + th.lane_off, th.cs, lg);
-      softmax_cols<T, C>(lg, rc, n0 + th.row < p.N, nullptr, red0, red1, th);
+      softmax_fwd<T, C>(lg, rc, n0 + th.row < p.N, red, th);
       Split<C>(lg).to_smem(sm + kSfWS, th.row, th.cs);
 #pragma unroll
       for (int k = 0; k < C / 2; ++k) put2(accs, k, __fadd2_rn(f2(accs, k), f2(lg, k)));
     }
     to_async_barrier();
     if (threadIdx.x == 0) {
-      mma_pool(tP, dWp, dFp);  // z += w^T fx
-      mma_commit(c.bar_mma);
+      mma_pool(tP, dWp, desc_stacked(sm + kSfF + buf * kSplit));  // z += w^T fx
+      commit(c, kG2);
     }
-    wait_mma(c.bar_mma, c.ph_mma, p.status);
+    if (more) {
+      split_tile(buf ^ 1);
+      to_async_barrier();
+      if (threadIdx.x == 0) {
+        prefetch(p, sm + kSfStageX, sm + kSfStageF, h, tile + p.P, b, c.bar);
+        wide_ts<96, false>(tL, tX, dWs);
+        commit(c, kG1);
+      }
+    }
+    wait_bar(c, kG2, p.status);
     if (th.q < 3) drain_pool<C>(tP + th.lane_off, th.cs, accz);
   }
   const int64_t slot = (int64_t)bh * p.P + blockIdx.x;
@@ -793,7 +848,7 @@ __global__ void __launch_bounds__(128 * kTSliceFwd, kCtasSliceFwd)
 static_assert(kSmall == kSmallStk, "tokens buffer holds either layout");
 constexpr int kDfStageX = 0, kDfWs = kStage, kDfTs = kDfWs + kSmall,
               kDfBias = kDfTs + kSmall, kDfRed = kDfBias + 128,
-              kDfBar = kDfRed + 2 * kTDesliceFwd * 512, kDfBytes = kDfBar + 64;
+              kDfBar = kDfRed + red_bytes(kTDesliceFwd, 2), kDfBytes = kDfBar + kBarBytes;
 
 __global__ void __launch_bounds__(128 * kTDesliceFwd, kCtasDesliceFwd)
     k_tc_deslice_fwd(const __grid_constant__ TcParams p) {
@@ -803,8 +858,7 @@ __global__ void __launch_bounds__(128 * kTDesliceFwd, kCtasDesliceFwd)
   const Th<T> th;
   const int bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
   Ctl c = prologue_begin<kDfCols>(sm, kDfBar);
-  float* red0 = (float*)(sm + kDfRed);
-  float* red1 = red0 + T * 128;
+  float* red = (float*)(sm + kDfRed);
   put_small<NT>(sm + kDfWs, p.W + (int64_t)b * p.swb + (int64_t)h * p.swh);
   if constexpr (kNwDf == 32)
     put_small<NT>(sm + kDfTs, p.M + (int64_t)bh * 32 * 32);
@@ -817,12 +871,10 @@ __global__ void __launch_bounds__(128 * kTDesliceFwd, kCtasDesliceFwd)
   const uint64_t dWs = desc_smallK(sm + kDfWs);
   const uint64_t dTs = kNwDf == 32 ? desc_smallM(sm + kDfTs) : desc_stacked(sm + kDfTs);
   int tile = blockIdx.x;
-  if (threadIdx.x == 0 && tile < p.ntiles)
-    tma_tile(p, sm + kDfStageX, nullptr, h, tile, b, c.bar_tma);
+  if (threadIdx.x == 0) tma_tile(p, sm + kDfStageX, nullptr, h, tile, b, c.bar);
   for (; tile < p.ntiles; tile += p.P) {
     const int n0 = tile * kTile;
-    mbar_wait(c.bar_tma, c.ph_tma, p.status);
-    c.ph_tma ^= 1;
+    wait_bar(c, kBarTma, p.status);
     {
       float x[C];
       read_cols<C>(sm + kDfStageX, th.row, th.cs, x);
@@ -831,24 +883,24 @@ __global__ void __launch_bounds__(128 * kTDesliceFwd, kCtasDesliceFwd)
     }
     to_async_barrier();
     if (threadIdx.x == 0) {
-      prefetch(p, sm + kDfStageX, nullptr, h, tile, b, c.bar_tma);
+      prefetch(p, sm + kDfStageX, nullptr, h, tile, b, c.bar);
       wide_ts<kNwDf, false>(tL, tA, dWs);  // logits = x W^T
-      mma_commit(c.bar_mma);
+      commit(c, kG1);
     }
-    wait_mma(c.bar_mma, c.ph_mma, p.status);
+    wait_bar(c, kG1, p.status);
     {
       float lg[C];
       ld_wide<kNwDf, C>(tL + th.lane_off, th.cs, lg);
-      softmax_cols<T, C>(lg, rc, true, nullptr, red0, red1, th);
+      softmax_fwd<T, C>(lg, rc, true, red, th);
       Split<C>(lg).to_tmem(tA + th.lane_off, th.cs);  // w, over the consumed x
       tst_wait();
     }
     to_async_barrier();
     if (threadIdx.x == 0) {
       wide_ts<kNwDf, true>(tL, tA, dTs);  // out = w tokens, over the consumed logits
-      mma_commit(c.bar_mma);
+      commit(c, kG2);
     }
-    wait_mma(c.bar_mma, c.ph_mma, p.status);
+    wait_bar(c, kG2, p.status);
     store_result<kNwDf, C>(tL, th.q, th.cs,
                            p.out + (int64_t)b * p.so[0] + (int64_t)n0 * p.so[1] +
                                (int64_t)h * p.so[2],
@@ -863,10 +915,12 @@ __global__ void __launch_bounds__(128 * kTDesliceFwd, kCtasDesliceFwd)
 // 160 and fx at 208; then dfx at 0, dx at 32, the dW pool at 64 and point
 // operands w at 160 and dl/tau at 208. The operands written at the start of
 // a tile are disjoint from the columns read at the end of the previous one.
+// MMAs are committed in groups (logits; dw; dfx and dx; the pool) so that
+// the threads start on each result while the next group runs.
 constexpr int kSbStageX = 0, kSbStageF = kStage, kSbX = 2 * kStage, kSbUp = kSbX + kSplit,
               kSbWs = kSbUp + kSplit + kTail, kSbZs = kSbWs + kSmall, kSbBias = kSbZs + kSmall,
               kSbDs = kSbBias + 128, kSbRed = kSbDs + 128,
-              kSbBar = kSbRed + 3 * kTSliceBwd * 512, kSbBytes = kSbBar + 64;
+              kSbBar = kSbRed + red_bytes(kTSliceBwd, 3), kSbBytes = kSbBar + kBarBytes;
 
 __global__ void __launch_bounds__(128 * kTSliceBwd, kCtasSliceBwd)
     k_tc_slice_bwd(const __grid_constant__ TcParams p) {
@@ -877,9 +931,7 @@ __global__ void __launch_bounds__(128 * kTSliceBwd, kCtasSliceBwd)
   const int bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
   Ctl c = prologue_begin<256>(sm, kSbBar);
   float* ds_s = (float*)(sm + kSbDs);
-  float* red0 = (float*)(sm + kSbRed);
-  float* red1 = red0 + T * 128;
-  float* red2 = red1 + T * 128;
+  float* red = (float*)(sm + kSbRed);
   put_small<NT>(sm + kSbWs, p.W + (int64_t)b * p.swb + (int64_t)h * p.swh);
   put_small<NT>(sm + kSbZs, p.M + (int64_t)bh * 32 * 32);
   const RowConst rc = row_const<NT>((float*)(sm + kSbBias),
@@ -897,13 +949,11 @@ __global__ void __launch_bounds__(128 * kTSliceBwd, kCtasSliceBwd)
 #pragma unroll
   for (int i = 0; i < C; ++i) accw[i] = accb[i] = 0.f;
   int tile = blockIdx.x;
-  if (threadIdx.x == 0 && tile < p.ntiles)
-    tma_tile(p, sm + kSbStageX, sm + kSbStageF, h, tile, b, c.bar_tma);
+  if (threadIdx.x == 0) tma_tile(p, sm + kSbStageX, sm + kSbStageF, h, tile, b, c.bar);
   for (; tile < p.ntiles; tile += p.P) {
     const int n0 = tile * kTile;
     const bool valid = n0 + th.row < p.N;
-    mbar_wait(c.bar_tma, c.ph_tma, p.status);
-    c.ph_tma ^= 1;
+    wait_bar(c, kBarTma, p.status);
     {
       float x[C], f[C];
       read_cols<C>(sm + kSbStageX, th.row, th.cs, x);
@@ -916,21 +966,22 @@ __global__ void __launch_bounds__(128 * kTSliceBwd, kCtasSliceBwd)
     }
     to_async_barrier();
     if (threadIdx.x == 0) {
-      prefetch(p, sm + kSbStageX, sm + kSbStageF, h, tile, b, c.bar_tma);
-      wide_ts<96, false>(tL, tX, dWk);   // logits = x W^T
+      prefetch(p, sm + kSbStageX, sm + kSbStageF, h, tile, b, c.bar);
+      wide_ts<96, false>(tL, tX, dWk);  // logits = x W^T
+      commit(c, kG1);
       wide_ts<32, false>(tDw, tF, dZk);  // dw = fx dz_num^T
-      mma_commit(c.bar_mma);
+      commit(c, kG2);
     }
-    wait_mma(c.bar_mma, c.ph_mma, p.status);
     {
-      float w[C], lgc[C], dw[C];
+      float w[C], dw[C];
+      wait_bar(c, kG1, p.status);
       ld_wide<96, C>(tL + th.lane_off, th.cs, w);
-      softmax_cols<T, C>(w, rc, valid, lgc, red0, red1, th);
+      wait_bar(c, kG2, p.status);
       ld_wide<32, C>(tDw + th.lane_off, th.cs, dw);
       const float2* ds2 = (const float2*)(ds_s + th.cs * C);
 #pragma unroll
       for (int k = 0; k < C / 2; ++k) put2(dw, k, __fadd2_rn(f2(dw, k), ds2[k]));
-      const float rdt = jacobian_cols<T, C>(w, dw, lgc, inv_tau, red2, th);
+      const float rdt = softmax_bwd<T, C>(w, dw, rc, inv_tau, valid, red, th);
       if (valid) dt_acc += rdt;
       Split<C>(w).to_tmem(tW + th.lane_off, th.cs);
       const Split<C> us(dw);  // dl / tau
@@ -944,10 +995,11 @@ __global__ void __launch_bounds__(128 * kTSliceBwd, kCtasSliceBwd)
     if (threadIdx.x == 0) {
       wide_ts<32, true>(tDfx, tW, dZm);  // dfx = w dz_num
       wide_ts<32, true>(tDx, tU, dWm);   // dx = (dl/tau) W
-      mma_pool(tP, dUp, dXb);            // dW += (dl/tau)^T x
-      mma_commit(c.bar_mma);
+      commit(c, kG3);
+      mma_pool(tP, dUp, dXb);  // dW += (dl/tau)^T x
+      commit(c, kG4);
     }
-    wait_mma(c.bar_mma, c.ph_mma, p.status);
+    wait_bar(c, kG3, p.status);
     store_result<32, C>(tDfx, th.q, th.cs,
                         p.out2 + (int64_t)b * p.so2[0] + (int64_t)n0 * p.so2[1] +
                             (int64_t)h * p.so2[2],
@@ -956,6 +1008,7 @@ __global__ void __launch_bounds__(128 * kTSliceBwd, kCtasSliceBwd)
                         p.out + (int64_t)b * p.so[0] + (int64_t)n0 * p.so[1] +
                             (int64_t)h * p.so[2],
                         p.so[1], p.N - n0);
+    wait_bar(c, kG4, p.status);
     if (th.q < 3) drain_pool<C>(tP + th.lane_off, th.cs, accw);
   }
   const int64_t slot = (int64_t)bh * p.P + blockIdx.x;
@@ -979,8 +1032,8 @@ __global__ void __launch_bounds__(128 * kTSliceBwd, kCtasSliceBwd)
 // 128 and dout at 176; then dx at 0 and one pool at 32 (dtokens, then dW).
 constexpr int kDbX = 0, kDbO = kSplit, kDbWp = 2 * kSplit, kDbUp = 3 * kSplit,
               kDbWs = 4 * kSplit, kDbTs = kDbWs + kSmall, kDbBias = kDbTs + kSmall,
-              kDbRed = kDbBias + 128, kDbBar = kDbRed + 3 * kTDesliceBwd * 512,
-              kDbBytes = kDbBar + 64;
+              kDbRed = kDbBias + 128, kDbBar = kDbRed + red_bytes(kTDesliceBwd, 3),
+              kDbBytes = kDbBar + kBarBytes;
 static_assert(kDbWp % 1024 == 0 && kDbUp % 1024 == 0, "staging tiles need 1 KB alignment");
 
 __global__ void __launch_bounds__(128 * kTDesliceBwd, kCtasDesliceBwd)
@@ -991,9 +1044,7 @@ __global__ void __launch_bounds__(128 * kTDesliceBwd, kCtasDesliceBwd)
   const Th<T> th;
   const int bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
   Ctl c = prologue_begin<256>(sm, kDbBar);
-  float* red0 = (float*)(sm + kDbRed);
-  float* red1 = red0 + T * 128;
-  float* red2 = red1 + T * 128;
+  float* red = (float*)(sm + kDbRed);
   put_small<NT>(sm + kDbWs, p.W + (int64_t)b * p.swb + (int64_t)h * p.swh);
   put_small<NT>(sm + kDbTs, p.M + (int64_t)bh * 32 * 32);
   const RowConst rc = row_const<NT>((float*)(sm + kDbBias),
@@ -1012,13 +1063,12 @@ __global__ void __launch_bounds__(128 * kTDesliceBwd, kCtasDesliceBwd)
 #pragma unroll
   for (int i = 0; i < C; ++i) acct[i] = accw[i] = accb[i] = 0.f;
   int tile = blockIdx.x;
-  if (threadIdx.x == 0 && tile < p.ntiles) tma_tile(p, stX, stO, h, tile, b, c.bar_tma);
+  if (threadIdx.x == 0) tma_tile(p, stX, stO, h, tile, b, c.bar);
   for (; tile < p.ntiles; tile += p.P) {
     const int n0 = tile * kTile;
     const bool valid = n0 + th.row < p.N;
     const bool more = tile + p.P < p.ntiles;
-    mbar_wait(c.bar_tma, c.ph_tma, p.status);
-    c.ph_tma ^= 1;
+    wait_bar(c, kBarTma, p.status);
     {
       float x[C], o[C];
       read_cols<C>(stX, th.row, th.cs, x);
@@ -1033,17 +1083,18 @@ __global__ void __launch_bounds__(128 * kTDesliceBwd, kCtasDesliceBwd)
     }
     to_async_barrier();
     if (threadIdx.x == 0) {
-      wide_ts<96, false>(tL, tX, dWk);   // logits = x W^T
+      wide_ts<96, false>(tL, tX, dWk);  // logits = x W^T
+      commit(c, kG1);
       wide_ts<32, false>(tDw, tO, dTk);  // dw = d_out tok^T
-      mma_commit(c.bar_mma);
+      commit(c, kG2);
     }
-    wait_mma(c.bar_mma, c.ph_mma, p.status);
     {
-      float w[C], lgc[C], dw[C];
+      float w[C], dw[C];
+      wait_bar(c, kG1, p.status);
       ld_wide<96, C>(tL + th.lane_off, th.cs, w);
-      softmax_cols<T, C>(w, rc, valid, lgc, red0, red1, th);
+      wait_bar(c, kG2, p.status);
       ld_wide<32, C>(tDw + th.lane_off, th.cs, dw);
-      const float rdt = jacobian_cols<T, C>(w, dw, lgc, inv_tau, red2, th);
+      const float rdt = softmax_bwd<T, C>(w, dw, rc, inv_tau, valid, red, th);
       if (valid) dt_acc += rdt;
       Split<C>(w).to_smem(sm + kDbWp, th.row, th.cs);  // over the consumed x stage
       const Split<C> us(dw);                            // dl / tau
@@ -1056,29 +1107,31 @@ __global__ void __launch_bounds__(128 * kTDesliceBwd, kCtasDesliceBwd)
     to_async_barrier();
     if (threadIdx.x == 0) {
       wide_ts<32, true>(tDx, tX, dWm);  // dx = (dl/tau) W
-      mma_pool(tP, dWp, dOb);           // dtokens += w^T d_out
-      mma_commit(c.bar_mma);
+      commit(c, kG3);
+      mma_pool(tP, dWp, dOb);  // dtokens += w^T d_out
+      commit(c, kG4);
     }
-    wait_mma(c.bar_mma, c.ph_mma, p.status);
+    wait_bar(c, kG3, p.status);
     store_result<32, C>(tDx, th.q, th.cs,
                         p.out + (int64_t)b * p.so[0] + (int64_t)n0 * p.so[1] +
                             (int64_t)h * p.so[2],
                         p.so[1], p.N - n0);
+    wait_bar(c, kG4, p.status);
     if (th.q < 3) drain_pool<C>(tP + th.lane_off, th.cs, acct);
     tc_fence_before();
     __syncthreads();  // the pool region is read out; WP is free
     tc_fence_after();
     if (threadIdx.x == 0) {
       if (more) {
-        mbar_arrive_expect_tx(c.bar_tma, 2 * kStage);
-        tma_load_4d(stX, &p.mx, 0, h, (tile + p.P) * kTile, b, c.bar_tma);
+        mbar_arrive_expect_tx(c.bar + kBarTma, 2 * kStage);
+        tma_load_4d(stX, &p.mx, 0, h, (tile + p.P) * kTile, b, c.bar + kBarTma);
       }
       mma_pool(tP, dUp, dXb);  // dW += (dl/tau)^T x
-      mma_commit(c.bar_mma);
+      commit(c, kG5);
     }
-    wait_mma(c.bar_mma, c.ph_mma, p.status);
+    wait_bar(c, kG5, p.status);
     if (threadIdx.x == 0 && more)  // UP is free once the dW pool is done
-      tma_load_4d(stO, &p.mv, 0, h, (tile + p.P) * kTile, b, c.bar_tma);
+      tma_load_4d(stO, &p.mv, 0, h, (tile + p.P) * kTile, b, c.bar + kBarTma);
     if (th.q < 3) drain_pool<C>(tP + th.lane_off, th.cs, accw);
   }
   const int64_t slot = (int64_t)bh * p.P + blockIdx.x;
