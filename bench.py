@@ -126,6 +126,28 @@ def zero_grads(*ts):
             t.grad = None
 
 
+PROFILE_SUMMARY = os.path.join(ROOT, "profiles", "tc_kernels_ncu_full_small.md")
+
+
+def profile_traffic(op, rows):
+    """DRAM bytes (read + write) of one launch of `op`'s kernel, from the
+    committed ncu capture summary (measured at 8M point rows and scaled by
+    the rows processed, traffic growing in proportion); None without it."""
+    try:
+        with open(PROFILE_SUMMARY) as f:
+            lines = f.read().splitlines()
+    except OSError:
+        return None
+    for ln in lines:
+        cells = [c.strip() for c in ln.strip().strip("|").split("|")]
+        if len(cells) == 2 and cells[0] == op:
+            try:
+                return int(int(cells[1]) * rows / float(8 << 20))
+            except ValueError:
+                return None
+    return None
+
+
 def op_timings(K, x, fx, W, b, tau, r, dot, reps=3):
     """Per-op device time (ms) of one round, each op launched directly on the
     current stream between CUDA events; median over reps."""
@@ -424,7 +446,8 @@ def main():
     round_bytes = sum(UNITS.values()) * unit_bytes
     roofline = {"bound": "hbm", "kernel": top, "achieved": round(achieved, 1),
                 "peak": peak, "peak_source": peak_src, "unit": "GB/s",
-                "frac": round(achieved / peak, 4), "traffic": None,
+                "frac": round(achieved / peak, 4),
+                "traffic": profile_traffic(top, cfg["B"] * n_local * cfg["H"]),
                 "algorithmic_bytes_per_launch": algo,
                 "op_ms": {k: round(v, 4) for k, v in opt.items()},
                 "round_frac": round(round_bytes / (ms * 1e-3) / 1e9 / peak, 4)}

@@ -728,7 +728,7 @@ __device__ __forceinline__ void prefetch(const TcParams& p, uint8_t* st0, uint8_
 #define FS_TC_SF_T 1
 #endif
 #ifndef FS_TC_DF_T
-#define FS_TC_DF_T 2
+#define FS_TC_DF_T 1
 #endif
 #ifndef FS_TC_DF_CTAS
 #define FS_TC_DF_CTAS 4
