@@ -54,8 +54,14 @@ CONFIGS = {
     "cfg5": dict(B=1, N=1 << 24, H=8, D=32, DV=32, G=64, weight="hgd", tau="half",
                  dtype=torch.float32, dot="ieee", split=True),
 }
-# algorithmic (B, N, H, width) tensors each op moves (bench_kernels.py:45)
-UNITS = {"slice_fwd": 2, "deslice_fwd": 2, "slice_bwd": 4, "deslice_bwd": 3}
+# (N, H, 32) fp32 tensors each op of the tied round reads or writes: slice
+# forward x, fx; deslice forward x, out; dtokens pass x, d_out; coupled
+# backward x, fx, d_out, dx, dfx -- 11 in all, the round's credited bytes
+# (the reference's own count, bench_kernels.py:45: 2 + 2 + 4 + 3).
+UNITS = {"slice_fwd": 2, "deslice_fwd": 2, "dtokens": 2, "coupled_bwd": 5}
+# the kernel each op runs (for the traffic of the committed ncu capture)
+KERNEL_OF = {"slice_fwd": "slice_fwd", "deslice_fwd": "deslice_fwd", "dtokens": "slice_fwd",
+             "coupled_bwd": "coupled_bwd"}
 
 
 def parse():
@@ -106,14 +112,11 @@ def make_inputs(cfg, n, device, seed):
 # --------------------------------------------------------------------------- steps
 
 def coupling_step(K, x, fx, W, b, tau, r, group=None):
-    """Forward + backward of one round through the public API (autograd)."""
+    """Forward + backward of one round through the public API: one
+    ``fused_coupling`` (slice -> z_num / (s + eps) -> deslice, tied backward),
+    points sharded over ``group``."""
     from flashslice_b200 import sharded
-    if group is None:
-        z, s = K.fused_slice(x, fx, W, b, tau)
-    else:
-        z, s = sharded.sharded_slice(x, fx, W, b, tau, group)
-    tok = z / (s + EPS)[..., None]
-    out = K.fused_deslice(x, W, b, tau, tok)
+    out = K.fused_coupling(x, fx, W, b, tau, eps=EPS, group=group)
     out.backward(r)
     if group is not None:
         sharded.reduce_grads([W, b, tau], group)
@@ -149,8 +152,10 @@ def profile_traffic(op, rows):
 
 
 def op_timings(K, x, fx, W, b, tau, r, dot, reps=3):
-    """Per-op device time (ms) of one round, each op launched directly on the
-    current stream between CUDA events; median over reps."""
+    """Per-op device time (ms) of one tied round, each op launched directly
+    on the current stream between CUDA events; median over reps. The ops are
+    the ones ``fused_coupling`` runs: slice forward, deslice forward, the
+    dtokens pass (a slice forward of d_out) and the coupled backward."""
     ops = torch.ops.flashslice
     bb = b if b is not None else W.new_zeros(W.shape[-2])
     Wd, bd, td = W.detach(), bb.detach(), tau.detach()
@@ -166,18 +171,18 @@ def op_timings(K, x, fx, W, b, tau, r, dot, reps=3):
         ev[2].record()
         ops.flash_deslice(xd, Wd, bd, td, tok, dot)
         ev[3].record()
-        _, dtok, _, _, _ = ops.flash_deslice_bwd(xd, Wd, bd, td, tok, r, dot)
+        dtok, _ = ops.flash_slice(xd, r, Wd, bd, td, dot)
         ev[4].record()
         dz = dtok / den
         ds = -(dtok * z).sum(-1) / (s + EPS) ** 2
         ev[5].record()
-        ops.flash_slice_bwd(xd, fd, Wd, bd, td, dz, ds, dot)
+        ops.coupled_bwd(xd, fd, r, Wd, bd, td, tok, dz, ds, dot)
         ev[6].record()
         torch.cuda.synchronize()
         times["slice_fwd"].append(ev[0].elapsed_time(ev[1]))
         times["deslice_fwd"].append(ev[2].elapsed_time(ev[3]))
-        times["deslice_bwd"].append(ev[3].elapsed_time(ev[4]))
-        times["slice_bwd"].append(ev[5].elapsed_time(ev[6]))
+        times["dtokens"].append(ev[3].elapsed_time(ev[4]))
+        times["coupled_bwd"].append(ev[5].elapsed_time(ev[6]))
     return {k: statistics.median(v) for k, v in times.items()}
 
 
@@ -423,7 +428,7 @@ def main():
                "h2d_bytes_per_step": (xh.numel() * xh.element_size()
                                       + fh.numel() * fh.element_size()),
                "d2h_bytes_per_step": res_bytes,
-               "path": "fused_slice/fused_deslice + autograd, inputs copied from pinned host "
+               "path": "fused_coupling + autograd, inputs copied from pinned host "
                        "memory and parameter gradients read back every step"}
 
     # per-op device times of the same round, for the roofline
@@ -447,7 +452,7 @@ def main():
     roofline = {"bound": "hbm", "kernel": top, "achieved": round(achieved, 1),
                 "peak": peak, "peak_source": peak_src, "unit": "GB/s",
                 "frac": round(achieved / peak, 4),
-                "traffic": profile_traffic(top, cfg["B"] * n_local * cfg["H"]),
+                "traffic": profile_traffic(KERNEL_OF[top], cfg["B"] * n_local * cfg["H"]),
                 "algorithmic_bytes_per_launch": algo,
                 "op_ms": {k: round(v, 4) for k, v in opt.items()},
                 "round_frac": round(round_bytes / (ms * 1e-3) / 1e9 / peak, 4)}

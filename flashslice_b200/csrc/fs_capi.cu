@@ -601,4 +601,65 @@ int fs_deslice_bwd(const fs_problem* p, const fs_tensor4* x_mid, const float* we
                     nullptr, dtokens, dW, db, dtau, workspace, workspace_bytes, stream);
 }
 
+int fs_coupled_supported(const fs_problem* p) {
+  if (check_problem(p) != FS_OK) return 0;
+  return setup(FS_OP_SLICE_BWD, *p).fused && tc_shape(*p) && !p->flags ? 1 : 0;
+}
+
+int fs_coupled_bwd(const fs_problem* p, const fs_tensor4* x_mid, const fs_tensor4* fx_mid,
+                   const fs_tensor4* d_out, const float* weight, const float* bias,
+                   const float* tau, const float* tokens, const float* dz_num, const float* ds,
+                   const fs_tensor4* dx_mid, const fs_tensor4* dfx_mid, float* dW, float* db,
+                   float* dtau, void* workspace, size_t workspace_bytes, void* stream) {
+  FS_CHECK(check_problem(p));
+  FS_CHECK(need(x_mid, "x_mid"));
+  FS_CHECK(need(fx_mid, "fx_mid"));
+  FS_CHECK(need(d_out, "d_out"));
+  FS_CHECK(need(weight, "weight"));
+  FS_CHECK(need(bias, "bias"));
+  FS_CHECK(need(tau, "tau"));
+  FS_CHECK(need(tokens, "tokens"));
+  FS_CHECK(need(dz_num, "dz_num"));
+  FS_CHECK(need(ds, "ds"));
+  FS_CHECK(need(dx_mid, "dx_mid"));
+  FS_CHECK(need(dfx_mid, "dfx_mid"));
+  FS_CHECK(need(dW, "dW"));
+  FS_CHECK(need(db, "db"));
+  FS_CHECK(need(dtau, "dtau"));
+  if (p->flags) return fail(FS_ERR_ARGUMENT, "the coupled backward takes no statistics");
+  const Setup s = setup(FS_OP_SLICE_BWD, *p);
+  FS_CHECK(check_ws(s, workspace, workspace_bytes));
+  if (!(s.fused && tc_shape(*p) && tc_tensor_ok(x_mid) && tc_tensor_ok(fx_mid) &&
+        tc_tensor_ok(d_out) && tc_tensor_ok(dx_mid) && tc_tensor_ok(dfx_mid)))
+    return fail(FS_ERR_UNSUPPORTED,
+                "the coupled backward serves fp32 single-tile problems with D = DV = G = 32 "
+                "(engine auto) and point tensors of unit width stride and 16-byte aligned "
+                "strides");
+  tcx::TcParams tq;
+  if (!tc_params(*p, tcx::TcKind::CoupledBwd, x_mid, fx_mid, weight, bias, tau, tq) ||
+      !tcx::make_point_map(&tq.mo, d_out->data, p->B, p->N, p->H, d_out->stride))
+    return fail(FS_ERR_UNSUPPORTED, "no TMA tensor map for the point tensors");
+  cudaStream_t st = (cudaStream_t)stream;
+  tq.M = tokens;
+  tq.M2 = dz_num;
+  tq.ds = ds;
+  tq.out = (float*)dx_mid->data;
+  tq.out2 = (float*)dfx_mid->data;
+  for (int i = 0; i < 4; ++i) {
+    tq.so[i] = dx_mid->stride[i];
+    tq.so2[i] = dfx_mid->stride[i];
+  }
+  // the partial buffers sized for the FMA kernels hold the (fewer) tensor-core CTAs'
+  tq.partA = at(workspace, s.partA);
+  tq.partS = at(workspace, s.partS);
+  tq.partDt = at(workspace, s.partDt);
+  route_note("coupled_bwd", "tensor-core", *p, x_mid, d_out);
+  FS_TRY(tcx::run_tc(tcx::TcKind::CoupledBwd, tq, st));
+  const int B = (int)p->B, H = (int)p->H, P = tq.P;
+  FS_TRY(run_reduce(tq.partA, dW, B, H, P, p->G * p->D, p->w_batch, p->w_heads, st));
+  FS_TRY(run_reduce(tq.partS, db, B, H, P, p->G, p->b_batch, p->b_heads, st));
+  FS_TRY(run_reduce(tq.partDt, dtau, B, H, P, 1, 1, H, st));
+  return FS_OK;
+}
+
 }  // extern "C"

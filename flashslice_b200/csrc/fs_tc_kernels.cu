@@ -1145,6 +1145,157 @@ __global__ void __launch_bounds__(128 * kTDesliceBwd, kCtasDesliceBwd)
   epilogue<256>(c);
 }
 
+// ------------------------------------------------------------ coupled backward
+// The backward of a whole coupling round (slice -> tokens -> deslice) once
+// the dtokens pass has run (dtokens = sum_n w^T d_out is a slice forward with
+// d_out in place of fx). Per point the two ops' gradients share the softmax
+// and are linear in the upstream dw, so with
+//   dw = d_out tok^T + fx dz_num^T + ds,  dl = w (dw - sum_g w dw),
+// one pass gives dx = (dl/tau) W, dW = (dl/tau)^T x, db = sum dl/tau and
+// dtau = -(1/tau) sum dl (logit - rowmax) for slice and deslice together,
+// and dfx = w dz_num; x is read once and dx written once, with no separate
+// sum of two dx tensors.
+// smem: [stage x][stage fx][X split][UP split: dl/tau | stage d_out][W]
+//       [tokens][dz_num][bias][ds][red][bars]
+// The d_out staging tile shares UP: the next tile's d_out is loaded once the
+// dW pool is done with UP.
+// TMEM (256 columns): logits at 0, d_out tok^T at 32, fx dz_num^T at 64 (two
+// accumulators, added in registers), point operands x at 96, fx at 144,
+// d_out at 192; then dfx at 0, dx at 32, the dW pool at 64, point operands w
+// at 160 and dl/tau at 208. The next tile's operands overlap the pool, so a
+// CTA-wide barrier ends each tile.
+constexpr int kTCoupledBwd = 2, kCtasCoupledBwd = 2;
+constexpr int kCbStageX = 0, kCbStageF = kStage, kCbX = 2 * kStage, kCbUp = kCbX + kSplit,
+              kCbWs = kCbUp + kSplit + kTail, kCbTs = kCbWs + kSmall, kCbZs = kCbTs + kSmall,
+              kCbBias = kCbZs + kSmall, kCbDs = kCbBias + 128, kCbRed = kCbDs + 128,
+              kCbBar = kCbRed + red_bytes(kTCoupledBwd, 3), kCbBytes = kCbBar + kBarBytes;
+static_assert(kCbUp % 1024 == 0, "the d_out staging tile needs 1 KB alignment");
+
+__global__ void __launch_bounds__(128 * kTCoupledBwd, kCtasCoupledBwd)
+    k_tc_coupled_bwd(const __grid_constant__ TcParams p) {
+  constexpr int T = kTCoupledBwd, NT = Th<T>::NT, C = Th<T>::C;
+  extern __shared__ __align__(16) uint8_t sm_raw[];
+  uint8_t* sm = align_smem(sm_raw);
+  const Th<T> th;
+  const int bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
+  Ctl c = prologue_begin<256>(sm, kCbBar);
+  float* ds_s = (float*)(sm + kCbDs);
+  float* red = (float*)(sm + kCbRed);
+  put_small<NT>(sm + kCbWs, p.W + (int64_t)b * p.swb + (int64_t)h * p.swh);
+  put_small<NT>(sm + kCbTs, p.M + (int64_t)bh * 32 * 32);
+  put_small<NT>(sm + kCbZs, p.M2 + (int64_t)bh * 32 * 32);
+  const RowConst rc = row_const<NT>((float*)(sm + kCbBias),
+                                    p.bias + (int64_t)b * p.sbb + (int64_t)h * p.sbh, p.tau[h]);
+  if (threadIdx.x < 32) ds_s[threadIdx.x] = p.ds[(int64_t)bh * 32 + threadIdx.x];
+  const float inv_tau = __frcp_rn(p.tau[h]);
+  prologue_end(c);
+  const uint32_t tL = c.tmem, tD1 = c.tmem + 32, tD2 = c.tmem + 64, tX = c.tmem + 96,
+                 tF = c.tmem + 144, tO = c.tmem + 192;
+  const uint32_t tDfx = c.tmem, tDx = c.tmem + 32, tP = c.tmem + 64, tW = c.tmem + 160,
+                 tU = c.tmem + 208;
+  const uint64_t dXb = desc_stacked(sm + kCbX), dUp = desc_stacked(sm + kCbUp);
+  const uint64_t dWk = desc_smallK(sm + kCbWs), dWm = desc_smallM(sm + kCbWs);
+  const uint64_t dTk = desc_smallK(sm + kCbTs);
+  const uint64_t dZk = desc_smallK(sm + kCbZs), dZm = desc_smallM(sm + kCbZs);
+  uint8_t* stX = sm + kCbStageX;
+  uint8_t* stF = sm + kCbStageF;
+  uint8_t* stO = sm + kCbUp;
+  float accw[C], accb[C], dt_acc = 0.f;
+#pragma unroll
+  for (int i = 0; i < C; ++i) accw[i] = accb[i] = 0.f;
+  int tile = blockIdx.x;
+  if (threadIdx.x == 0) {
+    mbar_arrive_expect_tx(c.bar + kBarTma, 3 * kStage);
+    tma_load_4d(stX, &p.mx, 0, h, tile * kTile, b, c.bar + kBarTma);
+    tma_load_4d(stF, &p.mv, 0, h, tile * kTile, b, c.bar + kBarTma);
+    tma_load_4d(stO, &p.mo, 0, h, tile * kTile, b, c.bar + kBarTma);
+  }
+  for (; tile < p.ntiles; tile += p.P) {
+    const int n0 = tile * kTile;
+    const bool valid = n0 + th.row < p.N;
+    const bool more = tile + p.P < p.ntiles;
+    wait_bar(c, kBarTma, p.status);
+    {
+      float x[C], f[C], o[C];
+      read_cols<C>(stX, th.row, th.cs, x);
+      read_cols<C>(stF, th.row, th.cs, f);
+      read_cols<C>(stO, th.row, th.cs, o);
+      const Split<C> xs(x);
+      xs.to_smem(sm + kCbX, th.row, th.cs);
+      xs.to_tmem(tX + th.lane_off, th.cs);
+      Split<C>(f).to_tmem(tF + th.lane_off, th.cs);
+      Split<C>(o).to_tmem(tO + th.lane_off, th.cs);
+      tst_wait();
+    }
+    to_async_barrier();
+    if (threadIdx.x == 0) {
+      if (more) {  // x and fx of the next tile; its d_out once UP is free
+        mbar_arrive_expect_tx(c.bar + kBarTma, 3 * kStage);
+        tma_load_4d(stX, &p.mx, 0, h, (tile + p.P) * kTile, b, c.bar + kBarTma);
+        tma_load_4d(stF, &p.mv, 0, h, (tile + p.P) * kTile, b, c.bar + kBarTma);
+      }
+      wide_ts<32, false>(tL, tX, dWk);  // logits = x W^T
+      commit(c, kG1);
+      wide_ts<32, false>(tD1, tO, dTk);  // d_out tok^T
+      wide_ts<32, false>(tD2, tF, dZk);  // fx dz_num^T
+      commit(c, kG2);
+    }
+    {
+      float w[C], dw[C], d2[C];
+      wait_bar(c, kG1, p.status);
+      ld_wide<32, C>(tL + th.lane_off, th.cs, w);
+      wait_bar(c, kG2, p.status);
+      ld_wide<32, C>(tD1 + th.lane_off, th.cs, dw);
+      ld_wide<32, C>(tD2 + th.lane_off, th.cs, d2);
+      const float2* ds2 = (const float2*)(ds_s + th.cs * C);
+#pragma unroll
+      for (int k = 0; k < C / 2; ++k)
+        put2(dw, k, __fadd2_rn(__fadd2_rn(f2(dw, k), f2(d2, k)), ds2[k]));
+      const float rdt = softmax_bwd<T, C>(w, dw, rc, inv_tau, valid, red, th);
+      if (valid) dt_acc += rdt;
+      Split<C>(w).to_tmem(tW + th.lane_off, th.cs);
+      const Split<C> us(dw);  // dl / tau
+      us.to_tmem(tU + th.lane_off, th.cs);
+      us.to_smem(sm + kCbUp, th.row, th.cs);  // over the consumed d_out stage
+#pragma unroll
+      for (int k = 0; k < C / 2; ++k) put2(accb, k, __fadd2_rn(f2(accb, k), f2(dw, k)));
+      tst_wait();
+    }
+    to_async_barrier();
+    if (threadIdx.x == 0) {
+      wide_ts<32, true>(tDfx, tW, dZm);  // dfx = w dz_num
+      wide_ts<32, true>(tDx, tU, dWm);   // dx = (dl/tau) W
+      commit(c, kG3);
+      mma_pool(tP, dUp, dXb);  // dW += (dl/tau)^T x
+      commit(c, kG4);
+    }
+    wait_bar(c, kG3, p.status);
+    store_result<32, C>(tDfx, th.q, th.cs,
+                        p.out2 + (int64_t)b * p.so2[0] + (int64_t)n0 * p.so2[1] +
+                            (int64_t)h * p.so2[2],
+                        p.so2[1], p.N - n0);
+    store_result<32, C>(tDx, th.q, th.cs,
+                        p.out + (int64_t)b * p.so[0] + (int64_t)n0 * p.so[1] +
+                            (int64_t)h * p.so[2],
+                        p.so[1], p.N - n0);
+    wait_bar(c, kG4, p.status);
+    if (threadIdx.x == 0 && more)  // UP is free once the dW pool is done
+      tma_load_4d(stO, &p.mo, 0, h, (tile + p.P) * kTile, b, c.bar + kBarTma);
+    if (th.q < 3) drain_pool<C>(tP + th.lane_off, th.cs, accw);
+    tc_fence_before();
+    __syncthreads();  // the pool is read out before the next tile's operands overwrite it
+    tc_fence_after();
+  }
+  const int64_t slot = (int64_t)bh * p.P + blockIdx.x;
+  float* xch = (float*)(sm + kCbX);
+  tc_fence_before();
+  pool_write<T>(xch, accw, p.partA + slot * 32 * 32, th);
+  rowsum_write<T>(xch, accb, p.partS + slot * 32, th);
+  const float tot = cta_sum_nt<NT>(dt_acc, (float*)(sm + kCbUp));
+  if (threadIdx.x == 0) p.partDt[slot] = -inv_tau * kLn2 * tot;
+  epilogue<256>(c);
+}
+
 // ------------------------------------------------------------ host side
 
 static __device__ int fs_tc_status_word;
@@ -1230,6 +1381,9 @@ cudaError_t run_tc(TcKind k, const TcParams& p, cudaStream_t s) {
     case TcKind::DesliceBwd:
       e = launch_tc(k_tc_deslice_bwd, kTDesliceBwd, kDbBytes, p, s);
       break;
+    case TcKind::CoupledBwd:
+      e = launch_tc(k_tc_coupled_bwd, kTCoupledBwd, kCbBytes, p, s);
+      break;
     default: return cudaErrorInvalidValue;
   }
   if (e != cudaSuccess) return e;
@@ -1246,6 +1400,7 @@ int tc_ctas_per_sm(TcKind k) {
     case TcKind::DesliceFwd: return kCtasDesliceFwd;
     case TcKind::SliceBwd: return kCtasSliceBwd;
     case TcKind::DesliceBwd: return kCtasDesliceBwd;
+    case TcKind::CoupledBwd: return kCtasCoupledBwd;
   }
   return 1;
 }
@@ -1256,6 +1411,7 @@ static_assert((kSfBytes + kSmemPad + 1024) * kCtasSliceFwd <= 228 * 1024, "slice
 static_assert((kDfBytes + kSmemPad + 1024) * kCtasDesliceFwd <= 228 * 1024, "deslice fwd smem");
 static_assert((kSbBytes + kSmemPad + 1024) * kCtasSliceBwd <= 228 * 1024, "slice bwd smem");
 static_assert((kDbBytes + kSmemPad + 1024) * kCtasDesliceBwd <= 228 * 1024, "deslice bwd smem");
+static_assert((kCbBytes + kSmemPad + 1024) * kCtasCoupledBwd <= 228 * 1024, "coupled bwd smem");
 // TMEM per SM (512 columns) holds the co-resident CTAs' allocations
 static_assert(256 * kCtasSliceFwd <= 512 && kDfCols * kCtasDesliceFwd <= 512 &&
                   256 * kCtasSliceBwd <= 512 && 256 * kCtasDesliceBwd <= 512,

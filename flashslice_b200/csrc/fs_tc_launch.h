@@ -11,17 +11,19 @@
 namespace fs {
 namespace tcx {
 
-enum class TcKind { SliceFwd, DesliceFwd, SliceBwd, DesliceBwd };
+enum class TcKind { SliceFwd, DesliceFwd, SliceBwd, DesliceBwd, CoupledBwd };
 
 struct TcParams {
   CUtensorMap mx;  // x_mid: (32, H, N, B) fp32 tiles of 128 points
   CUtensorMap mv;  // fx_mid or d_out, same shape
+  CUtensorMap mo;  // d_out of the coupled backward (mv is fx_mid there)
   int B, N, H, P, ntiles;
   const float* W;
   const float* bias;
   const float* tau;
   int64_t swb, swh, sbb, sbh;
   const float* M;   // tokens or dz_num (B, H, 32, 32)
+  const float* M2;  // dz_num of the coupled backward (M is tokens there)
   const float* ds;  // (B, H, 32)
   float* out;       // deslice out / dx_mid (B, N, H, 32), element strides so
   int64_t so[4];

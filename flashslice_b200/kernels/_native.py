@@ -61,6 +61,9 @@ SIGNATURES = {
     "fs_slice_fwd_noalloc": (ctypes.c_int, [_PP, _PT, _PT, _P, _P, _P, _P, _P, _P]),
     "fs_device_status": (ctypes.c_int, [ctypes.c_int]),
     "fs_tc_launch_count": (ctypes.c_uint64, []),
+    "fs_coupled_bwd": (ctypes.c_int, [_PP, _PT, _PT, _PT, _P, _P, _P, _P, _P, _P, _PT, _PT, _P,
+                                      _P, _P, _P, ctypes.c_size_t, _P]),
+    "fs_coupled_supported": (ctypes.c_int, [_PP]),
 }
 
 ENGINE_AUTO, ENGINE_FMA = 0, 1

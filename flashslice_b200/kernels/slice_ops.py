@@ -25,6 +25,8 @@ level asks for.
 
 import os
 
+import ctypes
+
 import torch
 
 from . import _native as nat
@@ -389,6 +391,51 @@ def native_deslice_bwd(x_mid, weight, bias, tau, tokens, stats, d_out, dot, fami
     return (dxm, dtok.to(tokens.dtype)) + _param_grads(c, weight, bias, tau, dW, db, dt)
 
 
+def _coupled_call(x_mid, fx_mid, weight, bias, tau, dot):
+    """The native problem of a coupled backward, or None when the coupled
+    kernel does not serve these inputs (shape, dtype, engine, layout)."""
+    if fx_mid.shape[3] != x_mid.shape[3] or x_mid.dtype != torch.float32 or \
+            fx_mid.dtype != torch.float32 or not x_mid.is_cuda:
+        return None
+    c = _Call(x_mid, fx_mid.shape[3], weight, bias, tau, dot, nat.FAMILY_SINGLE, 0,
+              torch.float32)
+    return c if nat.load().fs_coupled_supported(ctypes.byref(c.prob)) else None
+
+
+def native_coupled_bwd(x_mid, fx_mid, d_out, weight, bias, tau, tokens, dz_num, ds, dot):
+    """dx_mid, dfx_mid, dW, db, dtau of a whole coupling round (both ops'
+    contributions summed), or None when the coupled kernel does not serve the
+    inputs."""
+    _check_device(x_mid, fx_mid, d_out, weight, bias, tau, tokens, dz_num, ds)
+    B, N, H, D = x_mid.shape
+    if N == 0:
+        return None
+    c = _coupled_call(x_mid, fx_mid, weight, bias, tau, dot)
+    if c is None or d_out.dtype != torch.float32:
+        return None
+    dev = x_mid.device
+    dxm = torch.empty_like(x_mid)
+    dfx = torch.empty_like(fx_mid)
+    Bw, Hw = _lead2(weight, 2)
+    Bb, Hb = _lead2(bias, 1)
+    G = weight.shape[-2]
+    dW = torch.empty(Bw, Hw, G, D, device=dev, dtype=torch.float32)
+    db = torch.empty(Bb, Hb, G, device=dev, dtype=torch.float32)
+    dt = torch.empty(H, device=dev, dtype=torch.float32)
+    tok, dzn, dsf = _f32(tokens), _f32(dz_num), _f32(ds)
+    ws, nws = c.workspace(nat.OP_SLICE_BWD)
+    lib = nat.load()
+    with torch.cuda.device(dev):
+        rc = lib.fs_coupled_bwd(
+            c.prob, nat.t4(x_mid), nat.t4(fx_mid), nat.t4(d_out), nat.ptr(c.w), nat.ptr(c.b),
+            nat.ptr(c.tau), nat.ptr(tok), nat.ptr(dzn), nat.ptr(dsf), nat.t4(dxm), nat.t4(dfx),
+            nat.ptr(dW), nat.ptr(db), nat.ptr(dt), nat.ptr(ws), nws, nat.stream_of(x_mid))
+    if rc == nat.FS_ERR_UNSUPPORTED:
+        return None
+    nat.check(rc)
+    return (dxm, dfx) + _param_grads(c, weight, bias, tau, dW, db, dt)
+
+
 def native_stats(x_mid, weight, bias, tau, dot=0):
     """(B, H, 2, N) fp32 statistics of the slice logits."""
     _check_device(x_mid, weight, bias, tau)
@@ -421,6 +468,10 @@ _LIB.define("flash_deslice(Tensor x_mid, Tensor weight, Tensor bias, Tensor tau,
 _LIB.define("flash_deslice_bwd(Tensor x_mid, Tensor weight, Tensor bias, Tensor tau, "
             "Tensor tokens, Tensor d_out, int dot) "
             "-> (Tensor, Tensor, Tensor, Tensor, Tensor)")
+# No reference counterpart: the tied backward of a coupling round (below).
+_LIB.define("coupled_bwd(Tensor x_mid, Tensor fx_mid, Tensor d_out, Tensor weight, "
+            "Tensor bias, Tensor tau, Tensor tokens, Tensor dz_num, Tensor ds, int dot) "
+            "-> (Tensor, Tensor, Tensor, Tensor, Tensor)")
 
 
 def _slice_impl(x_mid, fx_mid, weight, bias, tau, dot):
@@ -445,10 +496,23 @@ def _deslice_bwd_impl(x_mid, weight, bias, tau, tokens, d_out, dot):
                               nat.FAMILY_SINGLE)
 
 
+def _coupled_bwd_impl(x_mid, fx_mid, d_out, weight, bias, tau, tokens, dz_num, ds, dot):
+    r = native_coupled_bwd(x_mid, fx_mid, d_out, weight, bias, tau, tokens, dz_num, ds, dot)
+    if r is not None:
+        return r
+    # inputs the coupled kernel does not serve: the two backward ops, summed
+    dxd, _, dwd, dbd, dtd = native_deslice_bwd(x_mid, weight, bias, tau, tokens, None, d_out,
+                                               dot, nat.FAMILY_SINGLE)
+    dxs, dfx, dws, dbs, dts = native_slice_bwd(x_mid, fx_mid, weight, bias, tau, None, dz_num,
+                                               ds, dot, nat.FAMILY_SINGLE)
+    return dxd + dxs, dfx, dwd + dws, dbd + dbs, dtd + dts
+
+
 _LIB.impl("flash_slice", _slice_impl, "CUDA")
 _LIB.impl("flash_slice_bwd", _slice_bwd_impl, "CUDA")
 _LIB.impl("flash_deslice", _deslice_impl, "CUDA")
 _LIB.impl("flash_deslice_bwd", _deslice_bwd_impl, "CUDA")
+_LIB.impl("coupled_bwd", _coupled_bwd_impl, "CUDA")
 
 
 @torch.library.register_fake("flashslice::flash_slice")
@@ -474,6 +538,12 @@ def _(x_mid, weight, bias, tau, tokens, dot):
 @torch.library.register_fake("flashslice::flash_deslice_bwd")
 def _(x_mid, weight, bias, tau, tokens, d_out, dot):
     return (torch.empty_like(x_mid), torch.empty_like(tokens), torch.empty_like(weight),
+            torch.empty_like(bias), torch.empty_like(tau))
+
+
+@torch.library.register_fake("flashslice::coupled_bwd")
+def _(x_mid, fx_mid, d_out, weight, bias, tau, tokens, dz_num, ds, dot):
+    return (torch.empty_like(x_mid), torch.empty_like(fx_mid), torch.empty_like(weight),
             torch.empty_like(bias), torch.empty_like(tau))
 
 
@@ -509,6 +579,116 @@ torch.library.register_autograd("flashslice::flash_slice", _slice_grad,
                                 setup_context=_slice_setup)
 torch.library.register_autograd("flashslice::flash_deslice", _deslice_grad,
                                 setup_context=_deslice_setup)
+
+
+# --------------------------------------------------------------------------- coupling round
+# Forward: z_num, s = slice; tokens = mix(z_num / (s + eps)); out = deslice.
+# Backward (tied; no reference counterpart as one op): the tokens' gradient
+# dtokens = sum_n w^T d_out is a slice forward with d_out in place of fx;
+# autograd through mix and the normalisation gives dz_num and ds; then one
+# coupled kernel forms the slice's and the deslice's remaining gradients
+# together (dx once, without summing two dx tensors). The reference runs the
+# two backward ops (slice_ops.py:822-885) and autograd adds their dx.
+
+def _tc_strides(t):
+    """t, or a contiguous copy when its layout is not one the tensor-core
+    kernels read (unit width stride, 16-byte aligned strides and base)."""
+    ok = t.stride(3) == 1 and all(st % 4 == 0 for st in t.stride()[:3]) and \
+        t.data_ptr() % 16 == 0
+    return t if ok else t.contiguous()
+
+
+def _rank_sum(t, group):
+    if group is None:
+        return t
+    from ..sharded import ordered_sum
+    return ordered_sum(t, group)
+
+
+class _CouplingRound(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x_mid, fx_mid, weight, bias, tau, eps, dot, mix, group, *params):
+        z, s = torch.ops.flashslice.flash_slice(x_mid, fx_mid, weight, bias, tau, dot)
+        z, s = _rank_sum(z, group), _rank_sum(s, group)
+        den = s + eps
+        tin = z / den[..., None]
+        graph = None
+        if mix is not None:
+            leaf = tin.detach().requires_grad_(True)
+            with torch.enable_grad():
+                tok_graph = mix(leaf)
+            graph = (leaf, tok_graph)
+            tok = tok_graph.detach()
+        else:
+            tok = tin
+        out = torch.ops.flashslice.flash_deslice(x_mid, weight, bias, tau, tok, dot)
+        ctx.save_for_backward(x_mid, fx_mid, weight, bias, tau, z, den, tok)
+        ctx.graph, ctx.params, ctx.dot, ctx.group = graph, params, dot, group
+        return out
+
+    @staticmethod
+    def backward(ctx, d_out):
+        x_mid, fx_mid, weight, bias, tau, z, den, tok = ctx.saved_tensors
+        d_out = _tc_strides(d_out)
+        dtok, _ = torch.ops.flashslice.flash_slice(x_mid, d_out, weight, bias, tau, ctx.dot)
+        dtok = _rank_sum(dtok, ctx.group)
+        pgrads = (None,) * len(ctx.params)
+        if ctx.graph is not None:
+            leaf, tok_graph = ctx.graph
+            g = torch.autograd.grad(tok_graph, (leaf,) + tuple(ctx.params), dtok,
+                                    allow_unused=True)
+            dtin = g[0] if g[0] is not None else torch.zeros_like(leaf)
+            pgrads = g[1:]
+            ctx.graph = None
+        else:
+            dtin = dtok
+        dz = dtin / den[..., None]
+        ds = -(dtin * z).sum(-1) / (den * den)
+        dx, dfx, dw, db, dtau = torch.ops.flashslice.coupled_bwd(
+            x_mid, fx_mid, d_out, weight, bias, tau, tok, dz, ds, ctx.dot)
+        need = ctx.needs_input_grad
+        grads = tuple(g if n else None for g, n in zip((dx, dfx, dw, db, dtau), need[:5]))
+        return grads + (None, None, None, None) + tuple(pgrads)
+
+
+def fused_coupling(x_mid, fx_mid, weight, bias, tau, mix=None, mix_params=None, eps=1e-5,
+                   group=None):
+    """One coupling round: z_num, s = fused_slice(...); tokens =
+    mix(z_num / (s + eps)[..., None]) (identity when mix is None); returns
+    fused_deslice(x_mid, weight, bias, tau, tokens). Same values as that
+    composition; its backward is tied: the two ops' point gradients are formed
+    in one pass over the points. ``mix`` is any differentiable function of the
+    (B, H, G, DV) tokens; the gradients of its parameters are returned only
+    for those listed in ``mix_params`` (by default the parameters of ``mix``
+    when it is a ``torch.nn.Module``). The blocked family, and calls with
+    gradients disabled, run the plain composition.
+
+    ``group``: a process group over which the points are sharded (each rank
+    passes its own points): z_num and s, and in the backward the tokens'
+    gradient, are summed over the ranks in rank order (bitwise the same on
+    every rank); the returned parameter gradients are this rank's part, to
+    be summed over the ranks like those of the op-by-op sharded coupling
+    (``flashslice_b200.sharded``)."""
+    weight, bias, G = _prep_wb(x_mid, weight, bias)
+    D, DV = x_mid.shape[3], fx_mid.shape[3]
+    _check_dims(D, G, DV)
+    dot = _dot_mode(x_mid)
+    if mix_params is None:
+        mix_params = [q for q in mix.parameters()] if isinstance(mix, torch.nn.Module) else []
+    params = tuple(q for q in mix_params if q.requires_grad)
+    if group is not None and torch.distributed.get_world_size(group) == 1:
+        group = None
+    if _use_blocked(D, G, DV, dot, x_mid.device) or not torch.is_grad_enabled():
+        if group is not None:
+            from ..sharded import sharded_coupling
+            return sharded_coupling(x_mid, fx_mid, weight, bias, tau, mix, eps, group)
+        z, s = fused_slice(x_mid, fx_mid, weight, bias, tau)
+        tok = z / (s + eps)[..., None]
+        if mix is not None:
+            tok = mix(tok)
+        return fused_deslice(x_mid, weight, bias, tau, tok)
+    return _CouplingRound.apply(x_mid, fx_mid, weight, bias, tau, eps, dot, mix, group,
+                                *params)
 
 
 # --------------------------------------------------------------------------- public API

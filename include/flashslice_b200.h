@@ -127,10 +127,12 @@ FS_API uint64_t fs_launch_count(void);
  * counterpart. */
 FS_API uint64_t fs_tc_launch_count(void);
 
-/* The current device's status word: 0, or the code of the first bounded
- * device-side wait that gave up (1) or a misaligned shared window (2) since
- * the last reset. Synchronises the device; clears the word when reset != 0.
- * A diagnostic of this library, no reference counterpart. */
+/* The current device's status word: 0, or 1 when a bounded device-side wait
+ * of a tensor-core kernel (on a TMA load or an MMA completion) gave up after
+ * 2 s since the last reset; the kernel then finished without the data it was
+ * waiting for, so its outputs are not valid. Synchronises the device; clears
+ * the word when reset != 0. A diagnostic of this library, no reference
+ * counterpart. */
 FS_API int fs_device_status(int reset);
 
 /* Bytes of workspace `op` needs for problem `p` (0 when it needs none). */
@@ -200,6 +202,29 @@ FS_API int fs_slice_fwd_noalloc(const fs_problem* p, const fs_tensor4* x_mid,
                                 const fs_tensor4* fx_mid, const float* weight,
                                 const float* bias, const float* tau, float* z_num,
                                 float* s, void* stream);
+
+/* Backward of a coupling round -- z_num, s = slice(x_mid, fx_mid); tokens =
+ * any function of z_num / (s + eps); out = deslice(x_mid, tokens) -- for
+ * both ops at once, given the upstream d_out of the deslice and dz_num, ds
+ * of the slice (from the tokens' gradient, which the caller forms with
+ * fs_slice_fwd(x_mid, d_out): dtokens = sum_n w^T d_out). Writes dx_mid and
+ * dfx_mid (the totals over both ops, so no second dx is summed) and dW, db,
+ * dtau (the totals). The reference runs the two backward ops separately
+ * (slice_ops.py:822-885) and autograd adds their dx; the results agree to
+ * rounding. Serves only what fs_coupled_supported accepts (otherwise
+ * FS_ERR_UNSUPPORTED); the workspace is fs_workspace_bytes(FS_OP_SLICE_BWD).
+ * No reference counterpart as one call. */
+FS_API int fs_coupled_bwd(const fs_problem* p, const fs_tensor4* x_mid,
+                          const fs_tensor4* fx_mid, const fs_tensor4* d_out,
+                          const float* weight, const float* bias, const float* tau,
+                          const float* tokens, const float* dz_num, const float* ds,
+                          const fs_tensor4* dx_mid, const fs_tensor4* dfx_mid, float* dW,
+                          float* db, float* dtau, void* workspace, size_t workspace_bytes,
+                          void* stream);
+
+/* 1 when fs_coupled_bwd serves problem p: single-tile family, fp32 points,
+ * D = DV = G = 32, engine auto, no statistics flags; 0 otherwise. */
+FS_API int fs_coupled_supported(const fs_problem* p);
 
 /* Per-point softmax statistics (B,H,2,N) of the slice logits, in
  * stats_mode's form (online or two-pass). */
