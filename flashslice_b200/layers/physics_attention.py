@@ -78,13 +78,23 @@ class Physics_Attention_Irregular_Mesh(nn.Module):
         return self.slice_down(mixed)
 
     def _forward_fused(self, x):
-        from ..kernels.slice_ops import fused_deslice, fused_slice
+        from ..kernels.slice_ops import (_dot_mode, _use_blocked, fused_coupling, fused_deslice,
+                                         fused_slice)
         B, N, _ = x.shape
         H, D = self.heads, self.dim_head
         # (B, N, H, D) views of the projections: the ops read them by strides
         fx_mid = self.in_project_fx(x).view(B, N, H, D)
         x_mid = self.in_project_x(x).view(B, N, H, D)
         tau = self.temperature.view(H)
+        G = self.in_project_slice.weight.shape[0]
+        if not self.untied_deslice and not _use_blocked(D, G, D, _dot_mode(x_mid), x.device):
+            # one round with the tied backward; the token attention is its mix
+            params = [q for m in (self.to_q, self.to_k, self.to_v, self.slice_down)
+                      for q in m.parameters()]
+            out = fused_coupling(x_mid, fx_mid, self.in_project_slice.weight,
+                                 self.in_project_slice.bias, tau, mix=self._mix,
+                                 mix_params=params, eps=1e-5)
+            return self.to_out(out.reshape(B, N, H * D)), None
         z_num, s, stats = fused_slice(x_mid, fx_mid, self.in_project_slice.weight,
                                       self.in_project_slice.bias, tau, return_stats=True)
         tokens = self._mix(z_num / (s + 1e-5).unsqueeze(-1))
