@@ -107,6 +107,15 @@ __device__ __forceinline__ void named_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
+// 2^x with the hardware's base-2 exponential (ex2.approx, subnormal results
+// flushed to zero): the softmax only needs it for x <= 0, where a flushed
+// result is a weight below 2^-126 of the row's largest.
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // ------------------------------------------------------------ paired fp32
 __device__ __forceinline__ float2 f2(const float* v, int k) { return make_float2(v[2 * k], v[2 * k + 1]); }
 __device__ __forceinline__ void put2(float* v, int k, float2 x) {
@@ -426,6 +435,23 @@ __device__ __forceinline__ void wide_ts(uint32_t d, uint32_t a, uint64_t bd) {
   }
 }
 
+// Wide product with N = 96 and the point operand in shared memory: A = point
+// rows of a stacked buffer read K-major (part p at +512 p), B = the small
+// operand's three parts stacked along N (K-major); six MMAs, A parts lo, mid,
+// hi accumulated one after the other.
+__device__ __forceinline__ void wide_ss96(uint32_t d, uint64_t ad, uint64_t bd) {
+  constexpr uint32_t id = idesc_bf16(128, 96, 0, 0);
+#pragma unroll
+  for (int pa = 0; pa < 3; ++pa)
+#pragma unroll
+    for (int ks = 0; ks < 2; ++ks)
+      mma_bf16(d, ad + ((pa * 512 + ks * 256) >> 4), bd + ((ks * 256) >> 4), id, (pa | ks) != 0);
+}
+
+__device__ __forceinline__ uint64_t desc_rowsA(const void* p) {
+  return smem_desc(smem_u32(p), 128, kRS);
+}
+
 // D (128 x 96) = pool over the tile's points: A = M-stacked slot parts, B =
 // N-stacked point parts; eight K steps of 16 points.
 __device__ __forceinline__ void mma_pool(uint32_t d, uint64_t ad, uint64_t bd) {
@@ -517,7 +543,7 @@ __device__ __forceinline__ RowStat row_stat(float ml, float sl, float ul, float*
     for (int c = 1; c < T; ++c) m = fmaxf(m, mt[c]);
 #pragma unroll
     for (int c = 0; c < T; ++c) {
-      const float f = exp2f(mt[c] - m);
+      const float f = ex2(mt[c] - m);
       st[c] *= f;
       ut[c] *= f;
     }
@@ -549,7 +575,7 @@ __device__ __forceinline__ float row_exp(const float (&acc)[C], const RowConst& 
   for (int k = 0; k < C / 2; ++k) {
     const float2 v = __fadd2_rn(f2(d, k), nm);
     put2(d, k, v);
-    put2(e, k, make_float2(exp2f(v.x), exp2f(v.y)));
+    put2(e, k, make_float2(ex2(v.x), ex2(v.y)));
   }
   return m;
 }
@@ -562,7 +588,7 @@ __device__ __forceinline__ void softmax_fwd(float (&lg)[C], const RowConst& rc, 
   float d[C], e[C];
   const float ml = row_exp<C>(lg, rc, th.cs, d, e);
   const RowStat st = row_stat<T, false>(ml, tree_sum2(e), 0.f, red, th);
-  const float f = valid ? exp2f(ml - st.m) / st.s : 0.f;
+  const float f = valid ? ex2(ml - st.m) / st.s : 0.f;
   const float2 f2v = make_float2(f, f);
 #pragma unroll
   for (int k = 0; k < C / 2; ++k) put2(lg, k, __fmul2_rn(f2(e, k), f2v));
@@ -584,7 +610,7 @@ __device__ __forceinline__ float softmax_bwd(float (&lg)[C], float (&dw)[C], con
   const RowStat st = row_stat<T, true>(ml, tree_sum2(e), tree_sum2(tmp), red, th);
   const float dm = ml - st.m;
   const float rs = __frcp_rn(st.s);
-  const float f = valid ? exp2f(dm) * rs : 0.f;
+  const float f = valid ? ex2(dm) * rs : 0.f;
   const float gs = st.u * rs;
   const float2 f2v = make_float2(f, f), ng = make_float2(-gs, -gs), dm2 = make_float2(dm, dm),
                it = make_float2(inv_tau, inv_tau);
@@ -725,7 +751,7 @@ __device__ __forceinline__ void prefetch(const TcParams& p, uint8_t* st0, uint8_
 // TMEM and registers sized for it) and, for deslice forward, the width of its
 // wide products. Each can be set at build time (-DFS_TC_SF_T=... etc.).
 #ifndef FS_TC_SF_T
-#define FS_TC_SF_T 1
+#define FS_TC_SF_T 2
 #endif
 #ifndef FS_TC_DF_T
 #define FS_TC_DF_T 1
@@ -756,16 +782,20 @@ enum : int { kBarTma = 0, kG1 = 1, kG2 = 2, kG3 = 3, kG4 = 4, kG5 = 5 };
 __host__ __device__ constexpr int red_bytes(int T, int n) { return T == 1 ? 0 : n * T * 512; }
 
 // ------------------------------------------------------------ slice forward
-// smem: [stage x][stage fx][WS split: w][F split: fx, two tiles][W][bias][red][bars]
+// smem: [stage x][WS split: w][F split: fx, two tiles][W][bias][red][bars]
+// Each fx tile is staged inside the F buffer its split will occupy (the
+// rows are read into registers, then the split overwrites them).
 // TMEM (256 columns): logits (N-stacked) at 0, z pool at 96, the x point
 // operand at 192.
 // The loop is skewed by one stage: while the tensor core forms tile i's pool,
 // the threads split tile i+1 (into the other F buffer) and issue its logits;
-// the pool is drained while those run.
+// the pool is drained while those run. Tile i+2's fx is loaded into tile i's
+// F buffer once tile i's pool is done with it.
 // (WS needs no tail: its M-stacked reads past the end land in F.)
-constexpr int kSfStageX = 0, kSfStageF = kStage, kSfWS = 2 * kStage, kSfF = kSfWS + kSplit,
-              kSfWs = kSfF + 2 * kSplit, kSfBias = kSfWs + kSmall, kSfRed = kSfBias + 128,
+constexpr int kSfStageX = 0, kSfWS = kStage, kSfF = kSfWS + kSplit, kSfWs = kSfF + 2 * kSplit,
+              kSfBias = kSfWs + kSmall, kSfRed = kSfBias + 128,
               kSfBar = kSfRed + red_bytes(kTSliceFwd, 2), kSfBytes = kSfBar + kBarBytes;
+static_assert(kSfF % 1024 == 0 && kSplit % 1024 == 0, "fx staging tiles need 1 KB alignment");
 
 __global__ void __launch_bounds__(128 * kTSliceFwd, kCtasSliceFwd)
     k_tc_slice_fwd(const __grid_constant__ TcParams p) {
@@ -782,31 +812,35 @@ __global__ void __launch_bounds__(128 * kTSliceFwd, kCtasSliceFwd)
   prologue_end(c);
   const uint32_t tL = c.tmem, tP = c.tmem + 96, tX = c.tmem + 192;
   const uint64_t dWs = desc_smallK(sm + kSfWs), dWp = desc_stacked(sm + kSfWS);
+  uint8_t* stX = sm + kSfStageX;
+  auto fbuf = [&](int i) { return sm + kSfF + i * kSplit; };
   float accz[C], accs[C];
 #pragma unroll
   for (int i = 0; i < C; ++i) accz[i] = accs[i] = 0.f;
-  // split one tile's rows from the staging buffers (x into TMEM, fx into F[buf])
+  // split one tile's rows (x into TMEM, fx from its staging in F[buf] into F[buf])
   auto split_tile = [&](int buf) {
     wait_bar(c, kBarTma, p.status);
     float x[C], f[C];
-    read_cols<C>(sm + kSfStageX, th.row, th.cs, x);
-    read_cols<C>(sm + kSfStageF, th.row, th.cs, f);
+    read_cols<C>(stX, th.row, th.cs, x);
+    read_cols<C>(fbuf(buf), th.row, th.cs, f);
+    __syncthreads();  // every staged fx row is in registers before F[buf] is overwritten
     Split<C>(x).to_tmem(tX + th.lane_off, th.cs);
-    Split<C>(f).to_smem(sm + kSfF + buf * kSplit, th.row, th.cs);
+    Split<C>(f).to_smem(fbuf(buf), th.row, th.cs);
     tst_wait();
   };
   int tile = blockIdx.x, buf = 0;
-  if (threadIdx.x == 0) tma_tile(p, sm + kSfStageX, sm + kSfStageF, h, tile, b, c.bar);
+  if (threadIdx.x == 0) tma_tile(p, stX, fbuf(0), h, tile, b, c.bar);
   split_tile(0);
   to_async_barrier();
   if (threadIdx.x == 0) {
-    prefetch(p, sm + kSfStageX, sm + kSfStageF, h, tile, b, c.bar);
+    prefetch(p, stX, fbuf(1), h, tile, b, c.bar);  // F[1] is unused yet
     wide_ts<96, false>(tL, tX, dWs);  // logits = x W^T
     commit(c, kG1);
   }
   for (; tile < p.ntiles; tile += p.P, buf ^= 1) {
     const int n0 = tile * kTile;
     const bool more = tile + p.P < p.ntiles;
+    const bool more2 = tile + 2 * p.P < p.ntiles;
     wait_bar(c, kG1, p.status);
     {
       float lg[C];
@@ -818,23 +852,28 @@ __global__ void __launch_bounds__(128 * kTSliceFwd, kCtasSliceFwd)
     }
     to_async_barrier();
     if (threadIdx.x == 0) {
-      mma_pool(tP, dWp, desc_stacked(sm + kSfF + buf * kSplit));  // z += w^T fx
+      mma_pool(tP, dWp, desc_stacked(fbuf(buf)));  // z += w^T fx
       commit(c, kG2);
     }
     if (more) {
       split_tile(buf ^ 1);
       to_async_barrier();
       if (threadIdx.x == 0) {
-        prefetch(p, sm + kSfStageX, sm + kSfStageF, h, tile + p.P, b, c.bar);
+        if (more2) {  // tile i+2: its x now, its fx once tile i's pool is done with F[buf]
+          mbar_arrive_expect_tx(c.bar + kBarTma, 2 * kStage);
+          tma_load_4d(stX, &p.mx, 0, h, (tile + 2 * p.P) * kTile, b, c.bar + kBarTma);
+        }
         wide_ts<96, false>(tL, tX, dWs);
         commit(c, kG1);
       }
     }
     wait_bar(c, kG2, p.status);
+    if (threadIdx.x == 0 && more2)
+      tma_load_4d(fbuf(buf), &p.mv, 0, h, (tile + 2 * p.P) * kTile, b, c.bar + kBarTma);
     if (th.q < 3) drain_pool<C>(tP + th.lane_off, th.cs, accz);
   }
   const int64_t slot = (int64_t)bh * p.P + blockIdx.x;
-  float* xch = (float*)(sm + kSfF);
+  float* xch = (float*)fbuf(0);
   tc_fence_before();
   pool_write<T>(xch, accz, p.partA + slot * 32 * 32, th);
   rowsum_write<T>(xch, accs, p.partS + slot * 32, th);
@@ -1159,11 +1198,13 @@ __global__ void __launch_bounds__(128 * kTDesliceBwd, kCtasDesliceBwd)
 //       [tokens][dz_num][bias][ds][red][bars]
 // The d_out staging tile shares UP: the next tile's d_out is loaded once the
 // dW pool is done with UP.
-// TMEM (256 columns): logits at 0, d_out tok^T at 32, fx dz_num^T at 64 (two
-// accumulators, added in registers), point operands x at 96, fx at 144,
-// d_out at 192; then dfx at 0, dx at 32, the dW pool at 64, point operands w
-// at 160 and dl/tau at 208. The next tile's operands overlap the pool, so a
-// CTA-wide barrier ends each tile.
+// TMEM (256 columns): logits (N-stacked, from the x split in shared memory)
+// at 0, d_out tok^T at 96, fx dz_num^T at 128 (two accumulators, added in
+// registers), point operands fx at 160 and d_out at 208; then dfx at 0, dx
+// at 32, the dW pool at 64, point operands w at 160 and dl/tau at 208. The
+// operands written at the start of a tile are disjoint from the columns read
+// at its end. The pool is issued first in the second group, so that the
+// next tile's d_out (staged in UP) loads while dfx and dx are formed.
 constexpr int kTCoupledBwd = 2, kCtasCoupledBwd = 2;
 constexpr int kCbStageX = 0, kCbStageF = kStage, kCbX = 2 * kStage, kCbUp = kCbX + kSplit,
               kCbWs = kCbUp + kSplit + kTail, kCbTs = kCbWs + kSmall, kCbZs = kCbTs + kSmall,
@@ -1189,11 +1230,12 @@ __global__ void __launch_bounds__(128 * kTCoupledBwd, kCtasCoupledBwd)
   if (threadIdx.x < 32) ds_s[threadIdx.x] = p.ds[(int64_t)bh * 32 + threadIdx.x];
   const float inv_tau = __frcp_rn(p.tau[h]);
   prologue_end(c);
-  const uint32_t tL = c.tmem, tD1 = c.tmem + 32, tD2 = c.tmem + 64, tX = c.tmem + 96,
-                 tF = c.tmem + 144, tO = c.tmem + 192;
+  const uint32_t tL = c.tmem, tD1 = c.tmem + 96, tD2 = c.tmem + 128, tF = c.tmem + 160,
+                 tO = c.tmem + 208;
   const uint32_t tDfx = c.tmem, tDx = c.tmem + 32, tP = c.tmem + 64, tW = c.tmem + 160,
                  tU = c.tmem + 208;
-  const uint64_t dXb = desc_stacked(sm + kCbX), dUp = desc_stacked(sm + kCbUp);
+  const uint64_t dXa = desc_rowsA(sm + kCbX), dXb = desc_stacked(sm + kCbX),
+                 dUp = desc_stacked(sm + kCbUp);
   const uint64_t dWk = desc_smallK(sm + kCbWs), dWm = desc_smallM(sm + kCbWs);
   const uint64_t dTk = desc_smallK(sm + kCbTs);
   const uint64_t dZk = desc_smallK(sm + kCbZs), dZm = desc_smallM(sm + kCbZs);
@@ -1220,9 +1262,7 @@ __global__ void __launch_bounds__(128 * kTCoupledBwd, kCtasCoupledBwd)
       read_cols<C>(stX, th.row, th.cs, x);
       read_cols<C>(stF, th.row, th.cs, f);
       read_cols<C>(stO, th.row, th.cs, o);
-      const Split<C> xs(x);
-      xs.to_smem(sm + kCbX, th.row, th.cs);
-      xs.to_tmem(tX + th.lane_off, th.cs);
+      Split<C>(x).to_smem(sm + kCbX, th.row, th.cs);
       Split<C>(f).to_tmem(tF + th.lane_off, th.cs);
       Split<C>(o).to_tmem(tO + th.lane_off, th.cs);
       tst_wait();
@@ -1234,7 +1274,7 @@ __global__ void __launch_bounds__(128 * kTCoupledBwd, kCtasCoupledBwd)
         tma_load_4d(stX, &p.mx, 0, h, (tile + p.P) * kTile, b, c.bar + kBarTma);
         tma_load_4d(stF, &p.mv, 0, h, (tile + p.P) * kTile, b, c.bar + kBarTma);
       }
-      wide_ts<32, false>(tL, tX, dWk);  // logits = x W^T
+      wide_ss96(tL, dXa, dWk);  // logits = x W^T
       commit(c, kG1);
       wide_ts<32, false>(tD1, tO, dTk);  // d_out tok^T
       wide_ts<32, false>(tD2, tF, dZk);  // fx dz_num^T
@@ -1243,7 +1283,7 @@ __global__ void __launch_bounds__(128 * kTCoupledBwd, kCtasCoupledBwd)
     {
       float w[C], dw[C], d2[C];
       wait_bar(c, kG1, p.status);
-      ld_wide<32, C>(tL + th.lane_off, th.cs, w);
+      ld_wide<96, C>(tL + th.lane_off, th.cs, w);
       wait_bar(c, kG2, p.status);
       ld_wide<32, C>(tD1 + th.lane_off, th.cs, dw);
       ld_wide<32, C>(tD2 + th.lane_off, th.cs, d2);
@@ -1263,13 +1303,17 @@ __global__ void __launch_bounds__(128 * kTCoupledBwd, kCtasCoupledBwd)
     }
     to_async_barrier();
     if (threadIdx.x == 0) {
+      mma_pool(tP, dUp, dXb);  // dW += (dl/tau)^T x
+      commit(c, kG3);
       wide_ts<32, true>(tDfx, tW, dZm);  // dfx = w dz_num
       wide_ts<32, true>(tDx, tU, dWm);   // dx = (dl/tau) W
-      commit(c, kG3);
-      mma_pool(tP, dUp, dXb);  // dW += (dl/tau)^T x
       commit(c, kG4);
     }
     wait_bar(c, kG3, p.status);
+    if (threadIdx.x == 0 && more)  // UP is free once the dW pool is done
+      tma_load_4d(stO, &p.mo, 0, h, (tile + p.P) * kTile, b, c.bar + kBarTma);
+    if (th.q < 3) drain_pool<C>(tP + th.lane_off, th.cs, accw);
+    wait_bar(c, kG4, p.status);
     store_result<32, C>(tDfx, th.q, th.cs,
                         p.out2 + (int64_t)b * p.so2[0] + (int64_t)n0 * p.so2[1] +
                             (int64_t)h * p.so2[2],
@@ -1278,13 +1322,6 @@ __global__ void __launch_bounds__(128 * kTCoupledBwd, kCtasCoupledBwd)
                         p.out + (int64_t)b * p.so[0] + (int64_t)n0 * p.so[1] +
                             (int64_t)h * p.so[2],
                         p.so[1], p.N - n0);
-    wait_bar(c, kG4, p.status);
-    if (threadIdx.x == 0 && more)  // UP is free once the dW pool is done
-      tma_load_4d(stO, &p.mo, 0, h, (tile + p.P) * kTile, b, c.bar + kBarTma);
-    if (th.q < 3) drain_pool<C>(tP + th.lane_off, th.cs, accw);
-    tc_fence_before();
-    __syncthreads();  // the pool is read out before the next tile's operands overwrite it
-    tc_fence_after();
   }
   const int64_t slot = (int64_t)bh * p.P + blockIdx.x;
   float* xch = (float*)(sm + kCbX);

@@ -16,8 +16,9 @@ from .slice_ops import (fused_slice, fused_deslice, fused_coupling, unsupported_
                         tile_table)
 from . import blocked  # noqa: F401  -- registers the flashslice::*_blk ops
 from .blocked import set_block_g, set_stats_mode, stats_mode
+from ._state import set_engine
 
 __all__ = ["fused_slice", "fused_deslice", "fused_coupling", "unsupported_dims",
            "single_tile_dims",
            "set_dot_mode", "set_kernel_mode", "set_block_g", "set_stats_mode",
-           "stats_mode", "set_tile_table", "tile_table"]
+           "stats_mode", "set_tile_table", "tile_table", "set_engine"]
