@@ -607,8 +607,8 @@ def _rank_sum(t, group):
 
 class _CouplingRound(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x_mid, fx_mid, weight, bias, tau, eps, dot, mix, group, *params):
-        z, s = torch.ops.flashslice.flash_slice(x_mid, fx_mid, weight, bias, tau, dot)
+    def forward(ctx, x_mid, fx_mid, weight, bias, tau, eps, dot, mix, group, ops, *params):
+        z, s = ops.flash_slice(x_mid, fx_mid, weight, bias, tau, dot)
         z, s = _rank_sum(z, group), _rank_sum(s, group)
         den = s + eps
         tin = z / den[..., None]
@@ -621,17 +621,19 @@ class _CouplingRound(torch.autograd.Function):
             tok = tok_graph.detach()
         else:
             tok = tin
-        out = torch.ops.flashslice.flash_deslice(x_mid, weight, bias, tau, tok, dot)
+        out = ops.flash_deslice(x_mid, weight, bias, tau, tok, dot)
         ctx.save_for_backward(x_mid, fx_mid, weight, bias, tau, z, den, tok)
-        ctx.graph, ctx.params, ctx.dot, ctx.group = graph, params, dot, group
+        ctx.graph, ctx.params, ctx.dot, ctx.group, ctx.ops = graph, params, dot, group, ops
         return out
 
     @staticmethod
     def backward(ctx, d_out):
         x_mid, fx_mid, weight, bias, tau, z, den, tok = ctx.saved_tensors
         d_out = _tc_strides(d_out)
-        dtok, _ = torch.ops.flashslice.flash_slice(x_mid, d_out, weight, bias, tau, ctx.dot)
-        dtok = _rank_sum(dtok, ctx.group)
+        # this rank's part of the tokens' gradient; back through mix it gives
+        # this rank's part of the mix parameters' gradients (summed over the
+        # ranks like W's), then the tokens-in gradient is summed over ranks
+        dtok, _ = ctx.ops.flash_slice(x_mid, d_out, weight, bias, tau, ctx.dot)
         pgrads = (None,) * len(ctx.params)
         if ctx.graph is not None:
             leaf, tok_graph = ctx.graph
@@ -642,17 +644,18 @@ class _CouplingRound(torch.autograd.Function):
             ctx.graph = None
         else:
             dtin = dtok
+        dtin = _rank_sum(dtin, ctx.group)
         dz = dtin / den[..., None]
         ds = -(dtin * z).sum(-1) / (den * den)
-        dx, dfx, dw, db, dtau = torch.ops.flashslice.coupled_bwd(
+        dx, dfx, dw, db, dtau = ctx.ops.coupled_bwd(
             x_mid, fx_mid, d_out, weight, bias, tau, tok, dz, ds, ctx.dot)
         need = ctx.needs_input_grad
         grads = tuple(g if n else None for g, n in zip((dx, dfx, dw, db, dtau), need[:5]))
-        return grads + (None, None, None, None) + tuple(pgrads)
+        return grads + (None, None, None, None, None) + tuple(pgrads)
 
 
 def fused_coupling(x_mid, fx_mid, weight, bias, tau, mix=None, mix_params=None, eps=1e-5,
-                   group=None):
+                   group=None, _ops=None):
     """One coupling round: z_num, s = fused_slice(...); tokens =
     mix(z_num / (s + eps)[..., None]) (identity when mix is None); returns
     fused_deslice(x_mid, weight, bias, tau, tokens). Same values as that
@@ -664,11 +667,15 @@ def fused_coupling(x_mid, fx_mid, weight, bias, tau, mix=None, mix_params=None, 
     gradients disabled, run the plain composition.
 
     ``group``: a process group over which the points are sharded (each rank
-    passes its own points): z_num and s, and in the backward the tokens'
-    gradient, are summed over the ranks in rank order (bitwise the same on
-    every rank); the returned parameter gradients are this rank's part, to
-    be summed over the ranks like those of the op-by-op sharded coupling
-    (``flashslice_b200.sharded``)."""
+    passes its own points): z_num and s, and in the backward the gradient of
+    the normalised tokens, are summed over the ranks in rank order (bitwise
+    the same on every rank); the returned gradients of W, b, tau and the mix
+    parameters are this rank's part, to be summed over the ranks like those
+    of the op-by-op sharded coupling (``flashslice_b200.sharded``).
+
+    ``_ops`` replaces the three ops the round calls (``flash_slice``,
+    ``flash_deslice``, ``coupled_bwd``; tests run the rank logic on CPU
+    with eager stand-ins)."""
     weight, bias, G = _prep_wb(x_mid, weight, bias)
     D, DV = x_mid.shape[3], fx_mid.shape[3]
     _check_dims(D, G, DV)
@@ -678,7 +685,8 @@ def fused_coupling(x_mid, fx_mid, weight, bias, tau, mix=None, mix_params=None, 
     params = tuple(q for q in mix_params if q.requires_grad)
     if group is not None and torch.distributed.get_world_size(group) == 1:
         group = None
-    if _use_blocked(D, G, DV, dot, x_mid.device) or not torch.is_grad_enabled():
+    if _ops is None and (_use_blocked(D, G, DV, dot, x_mid.device) or
+                         not torch.is_grad_enabled()):
         if group is not None:
             from ..sharded import sharded_coupling
             return sharded_coupling(x_mid, fx_mid, weight, bias, tau, mix, eps, group)
@@ -688,7 +696,7 @@ def fused_coupling(x_mid, fx_mid, weight, bias, tau, mix=None, mix_params=None, 
             tok = mix(tok)
         return fused_deslice(x_mid, weight, bias, tau, tok)
     return _CouplingRound.apply(x_mid, fx_mid, weight, bias, tau, eps, dot, mix, group,
-                                *params)
+                                _ops if _ops is not None else torch.ops.flashslice, *params)
 
 
 # --------------------------------------------------------------------------- public API

@@ -35,8 +35,10 @@ def ordered_sum(t, group=None):
     if world == 1:
         return t.clone()
     t = t.contiguous()
-    buf = torch.empty((world,) + tuple(t.shape), dtype=t.dtype, device=t.device)
-    dist.all_gather_into_tensor(buf, t, group=group)
+    # a flat (world * numel) output: the layout every backend accepts
+    flat = torch.empty(world * t.numel(), dtype=t.dtype, device=t.device)
+    dist.all_gather_into_tensor(flat, t.reshape(-1), group=group)
+    buf = flat.view((world,) + tuple(t.shape))
     out = buf[0].clone()
     for r in range(1, world):
         out += buf[r]
