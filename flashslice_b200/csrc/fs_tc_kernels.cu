@@ -15,11 +15,13 @@
 //    small operand's parts are stacked along N ([B_lo | B_mid | B_hi]) and the
 //    point operand's parts lo, mid, hi accumulated one after the other (six
 //    MMAs, all nine partial products); the three column groups are added in
-//    registers. With NW = 32 (where TMEM is short) the six partial products
-//    above the fp32 rounding level (lo*lo, lo*mid and mid*lo are below 2^-26
-//    of the result) go into one 32-column accumulator (twelve MMAs). The
-//    point operand is read from TMEM, where each thread writes its own row: a
-//    tensor-core read of shared memory runs at about 128 bytes per clock.
+//    registers. Where TMEM is short, NW = 64 accumulates [x B_mid | x B_hi]
+//    (eight MMAs: A hi times B_lo goes into the B_mid group) and NW = 32 the
+//    six partial products above the fp32 rounding level (lo*lo, lo*mid and
+//    mid*lo are below 2^-26 of the result) in one 32-column accumulator
+//    (twelve MMAs). The point operand is read from TMEM, where each thread
+//    writes its own row: a tensor-core read of shared memory runs at about
+//    128 bytes per clock.
 //  * "pool" products (sums over the tile's points, M = slots): the slot
 //    operand's parts are stacked along M ([A_lo; A_mid; A_hi; unused], M =
 //    128) and the point operand's along N ([B_lo | B_mid | B_hi], N = 96):
@@ -204,9 +206,9 @@ __device__ __forceinline__ void tst_wait() {
 }
 
 // This thread's C columns of a wide result at taddr (lane included): one
-// 32-column accumulator (NW = 32), or the sum of the three column groups of
-// an N-stacked one (NW = 96; groups x B_lo, x B_mid, x B_hi, added small
-// first).
+// 32-column accumulator (NW = 32), or the sum of the column groups of an
+// N-stacked one, added small first (NW = 64: groups x B_mid, x B_hi; NW = 96:
+// x B_lo, x B_mid, x B_hi).
 template <int NW, int C>
 __device__ __forceinline__ void ld_wide(uint32_t taddr, int cs, float (&v)[C]) {
   if constexpr (NW == 32) {
@@ -215,6 +217,15 @@ __device__ __forceinline__ void ld_wide(uint32_t taddr, int cs, float (&v)[C]) {
     tld_wait();
 #pragma unroll
     for (int i = 0; i < C; ++i) v[i] = __uint_as_float(r[i]);
+  } else if constexpr (NW == 64) {
+    uint32_t a[C], b[C];
+    tld<C>(taddr + cs * C, a);
+    tld<C>(taddr + 32 + cs * C, b);
+    tld_wait();
+#pragma unroll
+    for (int k = 0; k < C / 2; ++k)
+      put2(v, k, __fadd2_rn(make_float2(__uint_as_float(a[2 * k]), __uint_as_float(a[2 * k + 1])),
+                            make_float2(__uint_as_float(b[2 * k]), __uint_as_float(b[2 * k + 1]))));
   } else {
     uint32_t a[C], b[C], c[C];
     tld<C>(taddr + cs * C, a);
@@ -336,13 +347,14 @@ __device__ __forceinline__ void put_small_stacked(uint8_t* dst, const float* M) 
 // 32x32b shape, each thread's row is a different point, 1 KB or more apart,
 // and every store instruction half-fills 32 sectors.) The result is one
 // 32-column accumulator (NW = 32) or an N-stacked one whose column groups
-// are added small first (NW = 96). Rows at or past `nvalid` are not written.
+// are added small first (NW = 64, 96). Rows at or past `nvalid` are not
+// written.
 template <int NW, int C>
 __device__ __forceinline__ void store_result(uint32_t tcol, int q, int cs, float* row0,
                                              int64_t row_stride, int nvalid) {
   const int t = threadIdx.x & 31;
   constexpr int J = C / 8;
-  constexpr int NG = NW == 32 ? 1 : 3;
+  constexpr int NG = NW / 32;
   uint32_t r[2][J][NG][4];
 #pragma unroll
   for (int hf = 0; hf < 2; ++hf)
@@ -369,12 +381,10 @@ __device__ __forceinline__ void store_result(uint32_t tcol, int q, int cs, float
         for (int j = 0; j < J; ++j) {
           float2 v = make_float2(__uint_as_float(r[hf][j][0][2 * sub]),
                                  __uint_as_float(r[hf][j][0][2 * sub + 1]));
-          if constexpr (NW == 96) {
-            v = __fadd2_rn(v, make_float2(__uint_as_float(r[hf][j][1][2 * sub]),
-                                          __uint_as_float(r[hf][j][1][2 * sub + 1])));
-            v = __fadd2_rn(v, make_float2(__uint_as_float(r[hf][j][2][2 * sub]),
-                                          __uint_as_float(r[hf][j][2][2 * sub + 1])));
-          }
+#pragma unroll
+          for (int g = 1; g < NG; ++g)
+            v = __fadd2_rn(v, make_float2(__uint_as_float(r[hf][j][g][2 * sub]),
+                                          __uint_as_float(r[hf][j][g][2 * sub + 1])));
           *(float2*)(rp + 8 * j) = v;
         }
       }
@@ -406,17 +416,59 @@ __device__ __forceinline__ void mma_ts(uint32_t d, uint32_t a, uint64_t b, uint3
       : "memory");
 }
 
+// The NW = 64 schedule (below) of D = A1 B1^T, or with S = 2 of
+// D = A1 B1^T + A2 B2^T into one accumulator, the two products' partial
+// products interleaved so that the small ones still go first.
+template <bool MN, int S>
+__device__ __forceinline__ void wide_ts64_pair(uint32_t d, uint32_t a1, uint64_t b1, uint32_t a2,
+                                               uint64_t b2) {
+  constexpr uint32_t id64 = idesc_bf16(128, 64, 0, MN ? 1 : 0);
+  constexpr uint32_t id32 = idesc_bf16(128, 32, 0, MN ? 1 : 0);
+  constexpr int kstep = MN ? 2 * kRS : 256;  // bytes per K step of 16
+  constexpr int mid = MN ? 512 : 2048;       // offset of B_mid
+  const uint32_t a[2] = {a1, a2};
+  const uint64_t b[2] = {b1, b2};
+#pragma unroll
+  for (int pa = 0; pa < 2; ++pa)
+#pragma unroll
+    for (int s = 0; s < S; ++s)
+#pragma unroll
+      for (int ks = 0; ks < 2; ++ks)
+        mma_ts(d, a[s] + pa * 16 + ks * 8, b[s] + ((mid + ks * kstep) >> 4), id64,
+               (pa | s | ks) != 0);
+#pragma unroll
+  for (int s = 0; s < S; ++s)
+#pragma unroll
+    for (int ks = 0; ks < 2; ++ks)
+      mma_ts(d, a[s] + 32 + ks * 8, b[s] + ((ks * kstep) >> 4), id32, true);
+#pragma unroll
+  for (int s = 0; s < S; ++s)
+#pragma unroll
+    for (int ks = 0; ks < 2; ++ks)
+      mma_ts(d, a[s] + 32 + ks * 8, b[s] + ((mid + ks * kstep) >> 4), id64, true);
+}
+
 // Wide product D = A B^T, A = point rows in TMEM at `a` (K = 32), B = small
 // operand at bd:
 //  * NW = 32: twelve MMAs into one 32-column accumulator; bd is the three-part
 //    small operand, read K-major (B[n][k] = M[n][k]) or, MN, MN-major per
 //    part (B[n][k] = M[k][n]);
+//  * NW = 64: eight MMAs into a 64-column accumulator [x B_mid | x B_hi]:
+//    A lo and mid times [B_mid | B_hi], A hi times B_lo (into the B_mid
+//    group: the same outputs), A hi times [B_mid | B_hi] -- seven of the
+//    nine partial products, all above the fp32 rounding level; bd as for
+//    NW = 96 (both layouts hold B_mid and B_hi next to each other along N,
+//    so [B_mid | B_hi] is one N = 64 operand);
 //  * NW = 96: six MMAs into a 96-column N-stacked accumulator; bd is the
 //    three-part small operand read K-major (B[n][k] = M[n][k]) or, MN, the
 //    stacked copy of M (B[n][k] = M[k][n]).
+// An MMA with N <= 96 takes about as long as one with N = 32, so NW = 96
+// and NW = 64 cost half and two thirds of NW = 32.
 template <int NW, bool MN>
 __device__ __forceinline__ void wide_ts(uint32_t d, uint32_t a, uint64_t bd) {
-  if constexpr (NW == 32) {
+  if constexpr (NW == 64) {
+    wide_ts64_pair<MN, 1>(d, a, bd, a, bd);
+  } else if constexpr (NW == 32) {
     constexpr uint32_t id = idesc_bf16(128, 32, 0, MN ? 1 : 0);
 #pragma unroll
     for (int i = 0; i < 6; ++i)
@@ -760,7 +812,7 @@ __device__ __forceinline__ void prefetch(const TcParams& p, uint8_t* st0, uint8_
 #define FS_TC_DF_CTAS 4
 #endif
 #ifndef FS_TC_DF_NW
-#define FS_TC_DF_NW 32
+#define FS_TC_DF_NW 64
 #endif
 #ifndef FS_TC_SB_T
 #define FS_TC_SB_T 2
@@ -772,8 +824,8 @@ constexpr int kTSliceFwd = FS_TC_SF_T, kTDesliceFwd = FS_TC_DF_T, kTSliceBwd = F
               kTDesliceBwd = FS_TC_DB_T;
 constexpr int kCtasSliceFwd = 2, kCtasDesliceFwd = FS_TC_DF_CTAS, kCtasSliceBwd = 2,
               kCtasDesliceBwd = 2;
-constexpr int kNwDf = FS_TC_DF_NW;                 // 32 or 96
-constexpr int kDfCols = kNwDf == 32 ? 128 : 256;   // TMEM columns of deslice forward
+constexpr int kNwDf = FS_TC_DF_NW;                 // 32, 64 or 96
+constexpr int kDfCols = kNwDf == 96 ? 256 : 128;   // TMEM columns of deslice forward
 
 // MMA-completion barrier groups
 enum : int { kBarTma = 0, kG1 = 1, kG2 = 2, kG3 = 3, kG4 = 4, kG5 = 5 };
@@ -1008,7 +1060,7 @@ __global__ void __launch_bounds__(128 * kTSliceBwd, kCtasSliceBwd)
       prefetch(p, sm + kSbStageX, sm + kSbStageF, h, tile, b, c.bar);
       wide_ts<96, false>(tL, tX, dWk);  // logits = x W^T
       commit(c, kG1);
-      wide_ts<32, false>(tDw, tF, dZk);  // dw = fx dz_num^T
+      wide_ts<64, false>(tDw, tF, dZk);  // dw = fx dz_num^T
       commit(c, kG2);
     }
     {
@@ -1016,7 +1068,7 @@ __global__ void __launch_bounds__(128 * kTSliceBwd, kCtasSliceBwd)
       wait_bar(c, kG1, p.status);
       ld_wide<96, C>(tL + th.lane_off, th.cs, w);
       wait_bar(c, kG2, p.status);
-      ld_wide<32, C>(tDw + th.lane_off, th.cs, dw);
+      ld_wide<64, C>(tDw + th.lane_off, th.cs, dw);
       const float2* ds2 = (const float2*)(ds_s + th.cs * C);
 #pragma unroll
       for (int k = 0; k < C / 2; ++k) put2(dw, k, __fadd2_rn(f2(dw, k), ds2[k]));
@@ -1061,14 +1113,14 @@ __global__ void __launch_bounds__(128 * kTSliceBwd, kCtasSliceBwd)
 }
 
 // ------------------------------------------------------------ deslice backward
-// Sized for two CTAs per SM (shared memory 111 KB, TMEM 224 columns).
+// Sized for two CTAs per SM (shared memory 111 KB, TMEM 256 columns).
 // smem: [X split][O split: dout][WP split: w | stage x][UP split: dl/tau |
 //       stage dout][W][tokens][bias][red][bars]
 // The staging tiles share the pool operands' buffers: the next tile's x is
 // loaded into WP once the dtokens pool is done with it, its d_out into UP
 // once the dW pool is.
 // TMEM: logits (N-stacked) at 0, dw at 96, point operands x -> dl/tau at
-// 128 and dout at 176; then dx at 0 and one pool at 32 (dtokens, then dW).
+// 160 and dout at 208; then dx at 0 and one pool at 32 (dtokens, then dW).
 constexpr int kDbX = 0, kDbO = kSplit, kDbWp = 2 * kSplit, kDbUp = 3 * kSplit,
               kDbWs = 4 * kSplit, kDbTs = kDbWs + kSmall, kDbBias = kDbTs + kSmall,
               kDbRed = kDbBias + 128, kDbBar = kDbRed + red_bytes(kTDesliceBwd, 3),
@@ -1090,7 +1142,7 @@ __global__ void __launch_bounds__(128 * kTDesliceBwd, kCtasDesliceBwd)
                                     p.bias + (int64_t)b * p.sbb + (int64_t)h * p.sbh, p.tau[h]);
   const float inv_tau = __frcp_rn(p.tau[h]);
   prologue_end(c);
-  const uint32_t tL = c.tmem, tDw = c.tmem + 96, tX = c.tmem + 128, tO = c.tmem + 176;
+  const uint32_t tL = c.tmem, tDw = c.tmem + 96, tX = c.tmem + 160, tO = c.tmem + 208;
   const uint32_t tDx = c.tmem, tP = c.tmem + 32;
   const uint64_t dXb = desc_stacked(sm + kDbX), dOb = desc_stacked(sm + kDbO),
                  dWp = desc_stacked(sm + kDbWp), dUp = desc_stacked(sm + kDbUp);
@@ -1124,7 +1176,7 @@ __global__ void __launch_bounds__(128 * kTDesliceBwd, kCtasDesliceBwd)
     if (threadIdx.x == 0) {
       wide_ts<96, false>(tL, tX, dWk);  // logits = x W^T
       commit(c, kG1);
-      wide_ts<32, false>(tDw, tO, dTk);  // dw = d_out tok^T
+      wide_ts<64, false>(tDw, tO, dTk);  // dw = d_out tok^T
       commit(c, kG2);
     }
     {
@@ -1132,7 +1184,7 @@ __global__ void __launch_bounds__(128 * kTDesliceBwd, kCtasDesliceBwd)
       wait_bar(c, kG1, p.status);
       ld_wide<96, C>(tL + th.lane_off, th.cs, w);
       wait_bar(c, kG2, p.status);
-      ld_wide<32, C>(tDw + th.lane_off, th.cs, dw);
+      ld_wide<64, C>(tDw + th.lane_off, th.cs, dw);
       const float rdt = softmax_bwd<T, C>(w, dw, rc, inv_tau, valid, red, th);
       if (valid) dt_acc += rdt;
       Split<C>(w).to_smem(sm + kDbWp, th.row, th.cs);  // over the consumed x stage
@@ -1199,13 +1251,16 @@ __global__ void __launch_bounds__(128 * kTDesliceBwd, kCtasDesliceBwd)
 // The d_out staging tile shares UP: the next tile's d_out is loaded once the
 // dW pool is done with UP.
 // TMEM (256 columns): logits (N-stacked, from the x split in shared memory)
-// at 0, d_out tok^T at 96, fx dz_num^T at 128 (two accumulators, added in
-// registers), point operands fx at 160 and d_out at 208; then dfx at 0, dx
+// at 0, d_out tok^T + fx dz_num^T at 96 (one 64-column accumulator), point
+// operands fx at 160 and d_out at 208; then dfx at 0, dx
 // at 32, the dW pool at 64, point operands w at 160 and dl/tau at 208. The
 // operands written at the start of a tile are disjoint from the columns read
 // at its end. The pool is issued first in the second group, so that the
 // next tile's d_out (staged in UP) loads while dfx and dx are formed.
-constexpr int kTCoupledBwd = 2, kCtasCoupledBwd = 2;
+#ifndef FS_TC_CB_T
+#define FS_TC_CB_T 2
+#endif
+constexpr int kTCoupledBwd = FS_TC_CB_T, kCtasCoupledBwd = 2;
 constexpr int kCbStageX = 0, kCbStageF = kStage, kCbX = 2 * kStage, kCbUp = kCbX + kSplit,
               kCbWs = kCbUp + kSplit + kTail, kCbTs = kCbWs + kSmall, kCbZs = kCbTs + kSmall,
               kCbBias = kCbZs + kSmall, kCbDs = kCbBias + 128, kCbRed = kCbDs + 128,
@@ -1230,8 +1285,7 @@ __global__ void __launch_bounds__(128 * kTCoupledBwd, kCtasCoupledBwd)
   if (threadIdx.x < 32) ds_s[threadIdx.x] = p.ds[(int64_t)bh * 32 + threadIdx.x];
   const float inv_tau = __frcp_rn(p.tau[h]);
   prologue_end(c);
-  const uint32_t tL = c.tmem, tD1 = c.tmem + 96, tD2 = c.tmem + 128, tF = c.tmem + 160,
-                 tO = c.tmem + 208;
+  const uint32_t tL = c.tmem, tD = c.tmem + 96, tF = c.tmem + 160, tO = c.tmem + 208;
   const uint32_t tDfx = c.tmem, tDx = c.tmem + 32, tP = c.tmem + 64, tW = c.tmem + 160,
                  tU = c.tmem + 208;
   const uint64_t dXa = desc_rowsA(sm + kCbX), dXb = desc_stacked(sm + kCbX),
@@ -1276,21 +1330,18 @@ __global__ void __launch_bounds__(128 * kTCoupledBwd, kCtasCoupledBwd)
       }
       wide_ss96(tL, dXa, dWk);  // logits = x W^T
       commit(c, kG1);
-      wide_ts<32, false>(tD1, tO, dTk);  // d_out tok^T
-      wide_ts<32, false>(tD2, tF, dZk);  // fx dz_num^T
+      wide_ts64_pair<false, 2>(tD, tO, dTk, tF, dZk);  // d_out tok^T + fx dz_num^T
       commit(c, kG2);
     }
     {
-      float w[C], dw[C], d2[C];
+      float w[C], dw[C];
       wait_bar(c, kG1, p.status);
       ld_wide<96, C>(tL + th.lane_off, th.cs, w);
       wait_bar(c, kG2, p.status);
-      ld_wide<32, C>(tD1 + th.lane_off, th.cs, dw);
-      ld_wide<32, C>(tD2 + th.lane_off, th.cs, d2);
+      ld_wide<64, C>(tD + th.lane_off, th.cs, dw);
       const float2* ds2 = (const float2*)(ds_s + th.cs * C);
 #pragma unroll
-      for (int k = 0; k < C / 2; ++k)
-        put2(dw, k, __fadd2_rn(__fadd2_rn(f2(dw, k), f2(d2, k)), ds2[k]));
+      for (int k = 0; k < C / 2; ++k) put2(dw, k, __fadd2_rn(f2(dw, k), ds2[k]));
       const float rdt = softmax_bwd<T, C>(w, dw, rc, inv_tau, valid, red, th);
       if (valid) dt_acc += rdt;
       Split<C>(w).to_tmem(tW + th.lane_off, th.cs);
