@@ -130,7 +130,9 @@ bool tc_params(const fs_problem& p, tcx::TcKind k, const fs_tensor4* x, const fs
   q.H = (int)p.H;
   q.ntiles = (int)((p.N + 127) / 128);
   const int64_t BH = p.B * p.H;
-  int64_t P = (tcx::tc_ctas_per_sm(k) * kSmCount + BH - 1) / BH;
+  // CTAs per (b, h): as many as fill the co-resident slots of all SMs without
+  // going over (a CTA past them would run in a second wave after the others)
+  int64_t P = tcx::tc_ctas_per_sm(k) * kSmCount / BH;
   if (P > q.ntiles) P = q.ntiles;
   q.P = (int)(P < 1 ? 1 : P);
   q.W = W;
