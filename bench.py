@@ -189,19 +189,62 @@ def op_timings(K, x, fx, W, b, tau, r, dot, reps=3):
 # --------------------------------------------------------------------------- clocks
 
 class ClockSampler:
-    """nvidia-smi samples (every 200 ms) over the timed region."""
+    """SM clock and clock-event reasons of this rank's GPU over the timed
+    region: NVML read every 5 ms by a thread (the timed region of a few
+    tens of ms holds no sample of nvidia-smi's 200 ms loop), or nvidia-smi
+    samples when NVML cannot be loaded. Read-only queries."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
     NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+    # NVML clock-event reason bits of the names above, and the power brake
+    BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+            "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80}
+    PERIOD_S = 0.005
 
     def __init__(self, index):
         self.index = index
         self.proc = None
         self.path = None
+        self.nvml = None
+        self.samples = []
+
+    def _handle(self, nv):
+        try:
+            pr = torch.cuda.get_device_properties(self.index)
+            bus = "%08x:%02x:%02x.0" % (pr.pci_domain_id, pr.pci_bus_id, pr.pci_device_id)
+            return nv.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            return nv.nvmlDeviceGetHandleByIndex(self.index)
+
+    def _sample(self):
+        nv, h = self.nvml
+        sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+        mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+        rs = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+        self.samples.append((float(sm), float(mx), int(rs)))
+
+    def _loop(self):
+        while not self.done.is_set():
+            try:
+                self._sample()
+            except Exception:
+                return
+            self.done.wait(self.PERIOD_S)
 
     def start(self):
+        try:
+            import threading
+            import pynvml as nv
+            nv.nvmlInit()
+            self.nvml = (nv, self._handle(nv))
+            self.done = threading.Event()
+            self.thread = threading.Thread(target=self._loop, daemon=True)
+            self.thread.start()
+            return
+        except Exception:
+            self.nvml = None
         try:
             fd, self.path = tempfile.mkstemp(suffix=".csv")
             os.close(fd)
@@ -212,7 +255,30 @@ class ClockSampler:
         except OSError:
             self.proc = None
 
+    def _summary(self, sm, mx, reasons, source):
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx),
+                "reasons": sorted(reasons), "samples": len(sm), "source": source}
+
     def stop(self):
+        if self.nvml is not None:
+            self.done.set()
+            self.thread.join(timeout=5)
+            nv = self.nvml[0]
+            try:
+                if not self.samples:
+                    self._sample()
+            except Exception:
+                pass
+            try:
+                nv.nvmlShutdown()
+            except Exception:
+                pass
+            reasons = {name for name, bit in self.BITS.items()
+                       if any(r & bit for _, _, r in self.samples)}
+            return self._summary([s[0] for s in self.samples], [s[1] for s in self.samples],
+                                 reasons, "nvml every %d ms" % round(1e3 * self.PERIOD_S))
         if self.proc is None:
             return None
         self.proc.terminate()
@@ -237,10 +303,7 @@ class ClockSampler:
                             reasons.add(name)
         finally:
             os.unlink(self.path)
-        if not sm:
-            return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx),
-                "reasons": sorted(reasons), "samples": len(sm)}
+        return self._summary(sm, mx, reasons, "nvidia-smi every 200 ms")
 
 
 # --------------------------------------------------------------------------- CPU legs
