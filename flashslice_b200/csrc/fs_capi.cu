@@ -392,6 +392,15 @@ int fs_compute_stats(const fs_problem* p, const fs_tensor4* x_mid, const float* 
   return run_stats(*p, s, x_mid, weight, bias, tau, stats, (cudaStream_t)stream);
 }
 
+int fs_rank_sum(const float* parts, float* out, int world, int64_t n, void* stream) {
+  if (!parts || !out) return fail(FS_ERR_ARGUMENT, "rank_sum: null pointer");
+  if (world < 1 || n < 0) return fail(FS_ERR_ARGUMENT, "rank_sum: world %d, n %lld", world,
+                                      (long long)n);
+  if (n == 0) return FS_OK;
+  FS_TRY(run_reduce(parts, out, 1, 1, world, n, 1, 1, (cudaStream_t)stream));
+  return FS_OK;
+}
+
 int fs_slice_fwd(const fs_problem* p, const fs_tensor4* x_mid, const fs_tensor4* fx_mid,
                  const float* weight, const float* bias, const float* tau, const float* stats_in,
                  float* stats_out, float* z_num, float* s_out, void* workspace,

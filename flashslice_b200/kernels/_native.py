@@ -64,6 +64,7 @@ SIGNATURES = {
     "fs_coupled_bwd": (ctypes.c_int, [_PP, _PT, _PT, _PT, _P, _P, _P, _P, _P, _P, _PT, _PT, _P,
                                       _P, _P, _P, ctypes.c_size_t, _P]),
     "fs_coupled_supported": (ctypes.c_int, [_PP]),
+    "fs_rank_sum": (ctypes.c_int, [_P, _P, ctypes.c_int, ctypes.c_int64, _P]),
 }
 
 ENGINE_AUTO, ENGINE_FMA = 0, 1

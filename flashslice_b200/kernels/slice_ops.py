@@ -605,11 +605,18 @@ def _rank_sum(t, group):
     return ordered_sum(t, group)
 
 
+def _rank_sum_many(ts, group):
+    if group is None:
+        return ts
+    from ..sharded import ordered_sum_many
+    return ordered_sum_many(ts, group)
+
+
 class _CouplingRound(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x_mid, fx_mid, weight, bias, tau, eps, dot, mix, group, ops, *params):
         z, s = ops.flash_slice(x_mid, fx_mid, weight, bias, tau, dot)
-        z, s = _rank_sum(z, group), _rank_sum(s, group)
+        z, s = _rank_sum_many([z, s], group)
         den = s + eps
         tin = z / den[..., None]
         graph = None

@@ -29,20 +29,47 @@ def shard_range(n, rank, world):
     return start, start + base + (1 if rank >= world - rem else 0)
 
 
-def ordered_sum(t, group=None):
-    """Sum of ``t`` over the ranks of ``group`` in rank order (no autograd)."""
-    world = dist.get_world_size(group)
-    if world == 1:
-        return t.clone()
-    t = t.contiguous()
-    # a flat (world * numel) output: the layout every backend accepts
-    flat = torch.empty(world * t.numel(), dtype=t.dtype, device=t.device)
-    dist.all_gather_into_tensor(flat, t.reshape(-1), group=group)
-    buf = flat.view((world,) + tuple(t.shape))
+def _fold(buf):
+    """Sum of the (world, n) rows of ``buf`` in rank order: one native launch
+    (``fs_rank_sum``) for fp32 on the GPU, torch adds otherwise (CPU ranks)."""
+    if buf.is_cuda and buf.dtype == torch.float32:
+        from .kernels import _native as nat
+        out = torch.empty(buf.shape[1:], dtype=buf.dtype, device=buf.device)
+        stream = torch.cuda.current_stream(buf.device).cuda_stream
+        nat.check(nat.load().fs_rank_sum(buf.data_ptr(), out.data_ptr(), buf.shape[0],
+                                         out.numel(), stream))
+        return out
     out = buf[0].clone()
-    for r in range(1, world):
+    for r in range(1, buf.shape[0]):
         out += buf[r]
     return out
+
+
+def ordered_sum_many(ts, group=None):
+    """Each tensor of ``ts`` summed over the ranks of ``group`` in rank order
+    (no autograd), through one all-gather of their concatenation."""
+    world = dist.get_world_size(group)
+    if world == 1:
+        return [t.clone() for t in ts]
+    dtype = ts[0].dtype
+    if any(t.dtype != dtype for t in ts):
+        return [ordered_sum(t, group) for t in ts]
+    flat_in = torch.cat([t.reshape(-1) for t in ts]) if len(ts) > 1 else ts[0].reshape(-1)
+    n = flat_in.numel()
+    # a flat (world * n) output: the layout every backend accepts
+    flat = torch.empty(world * n, dtype=dtype, device=flat_in.device)
+    dist.all_gather_into_tensor(flat, flat_in.contiguous(), group=group)
+    total = _fold(flat.view(world, n))
+    out, off = [], 0
+    for t in ts:
+        out.append(total[off:off + t.numel()].view(t.shape))
+        off += t.numel()
+    return out
+
+
+def ordered_sum(t, group=None):
+    """Sum of ``t`` over the ranks of ``group`` in rank order (no autograd)."""
+    return ordered_sum_many([t], group)[0]
 
 
 class _RankSum(torch.autograd.Function):
@@ -90,7 +117,10 @@ def sharded_coupling(x_mid, fx_mid, weight, bias, tau, mix=None, eps=1e-5, group
 
 def reduce_grads(params, group=None):
     """Sum the gradients of replicated parameters over the ranks, in rank
-    order, in place (the data-parallel gradient of the sharded coupling)."""
-    for p in params:
-        if p is not None and p.grad is not None:
-            p.grad.copy_(ordered_sum(p.grad, group))
+    order, in place (the data-parallel gradient of the sharded coupling);
+    one all-gather for all of them."""
+    grads = [p.grad for p in params if p is not None and p.grad is not None]
+    if not grads:
+        return
+    for g, tot in zip(grads, ordered_sum_many(grads, group)):
+        g.copy_(tot)

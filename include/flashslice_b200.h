@@ -232,6 +232,13 @@ FS_API int fs_compute_stats(const fs_problem* p, const fs_tensor4* x_mid,
                      const float* weight, const float* bias, const float* tau,
                      float* stats, void* stream);
 
+/* out[e] = sum over r = 0 .. world-1, in that order, of parts[r * n + e]:
+ * the rank-order sum of a (world, n) fp32 buffer gathered from the ranks of a
+ * process group, one launch on `stream`. Replaces the per-rank Python adds
+ * of the multi-GPU wrapper (the reference plans the sharded coupling in
+ * ROADMAP.md:69-73 and has no kernel for it). */
+FS_API int fs_rank_sum(const float* parts, float* out, int world, int64_t n, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

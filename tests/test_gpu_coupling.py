@@ -148,3 +148,20 @@ def test_coupled_bwd_abi_refuses_unsupported(env):
     assert lib.fs_coupled_supported(ctypes.byref(p)) == 1
     p.engine = nat.ENGINE_FMA
     assert lib.fs_coupled_supported(ctypes.byref(p)) == 0
+
+
+def test_rank_sum_native(env):
+    """fs_rank_sum: the rank-order sum of a gathered (world, n) buffer, bitwise
+    the sequential fold (rank 0 + rank 1 + ...), one native launch."""
+    K, st, lib = env
+    from flashslice_b200 import sharded
+    g = torch.Generator(device="cuda").manual_seed(3)
+    for world, n in [(2, 1), (3, 1000), (8, 33_825)]:
+        buf = torch.randn(world, n, device="cuda", generator=g)
+        n0 = lib.fs_launch_count()
+        got = sharded._fold(buf)
+        assert lib.fs_launch_count() - n0 == 1
+        ref = buf[0].clone()
+        for r in range(1, world):
+            ref += buf[r]
+        assert torch.equal(got, ref)
