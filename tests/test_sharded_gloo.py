@@ -6,6 +6,7 @@ against the same round on one process."""
 import os
 import socket
 
+import numpy as np
 import pytest
 import torch
 import torch.distributed as dist
@@ -53,6 +54,21 @@ def _round(fn, x, fx, W, b, tau, r, M, tied=False, **kw):
     return out.detach(), [t.grad for t in L] + [Mp.grad]
 
 
+def _plain(v, back=False):
+    """Tensors <-> numpy arrays, recursively: results cross the queue by value
+    (a tensor is passed as a file descriptor that the parent fetches from the
+    child, which may have exited by then)."""
+    if isinstance(v, dict):
+        return {k: _plain(u, back) for k, u in v.items()}
+    if isinstance(v, (list, tuple)):
+        return type(v)(_plain(u, back) for u in v)
+    if back and isinstance(v, np.ndarray):
+        return torch.from_numpy(v)
+    if not back and isinstance(v, torch.Tensor):
+        return v.detach().numpy().copy()
+    return v
+
+
 def _worker(rank, world, port, q):
     try:
         os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -81,7 +97,7 @@ def _worker(rank, world, port, q):
             for i in (2, 3, 4, 5):
                 g[i] = sharded.ordered_sum(g[i])
         res.update(out1=out1, g1=g1, out2=out2, g2=g2)
-        q.put((rank, res))
+        q.put((rank, _plain(res)))
         dist.destroy_process_group()
     except Exception as e:  # report instead of hanging the parent
         q.put((rank, repr(e)))
@@ -101,7 +117,7 @@ def _run_ranks(world=2):
     for p in procs:
         p.start()
     try:
-        res = dict(q.get(timeout=180) for _ in procs)
+        res = {r: _plain(v, back=True) for r, v in (q.get(timeout=180) for _ in procs)}
     finally:
         for p in procs:
             p.join(timeout=60)
