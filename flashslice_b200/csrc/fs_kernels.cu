@@ -450,7 +450,12 @@ __global__ void __launch_bounds__(NT) k_blk_bwd_n(Params p) {
       p.delta[(int64_t)bh * 2 * N + n] = delta;
       p.delta[(int64_t)bh * 2 * N + N + n] = lrow;
     }
-    if (SLICE) row_scale(os + t * L.ors, L.dvt, inv_l);
+    if (SLICE) {
+      row_scale(os + t * L.ors, L.dvt, inv_l);
+      // dfx is complete: store it now, its rows may hold dx next
+      __syncthreads();
+      store_rows<T, NT>(os, L.ors, p.o2, b, h, n0, N, DV);
+    }
     float rdt = 0.f;
     first = true;
     for (int g0 = 0; g0 < G; g0 += GB) {
@@ -478,7 +483,6 @@ __global__ void __launch_bounds__(NT) k_blk_bwd_n(Params p) {
     row_scale(ps + t * L.prs, L.dt, inv_tau);
     if (n < N) dt_acc += rdt;
     __syncthreads();
-    if (SLICE) store_rows<T, NT>(os, L.ors, p.o2, b, h, n0, N, DV);
     store_rows<T, NT>(ps, L.prs, p.o1, b, h, n0, N, D);
   }
   __syncthreads();

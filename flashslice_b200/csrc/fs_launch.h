@@ -62,7 +62,12 @@ inline Plan make_plan(Kind k, int D, int DV, int nt) {
     pl.oV = take(nt * pl.vrs);
   if (any({K::FusedDesliceFwd, K::DesliceFwdStats, K::DesliceFwdOnline, K::SliceBwdN}))
     pl.oO = take(nt * pl.ors);
-  if (any({K::SliceBwdN, K::DesliceBwdN})) pl.oP = take(nt * pl.prs);
+  // slice's point-owning backward stores its dfx rows before it forms dx, so
+  // the dx rows reuse them when they fit (a second resident CTA at DV = 64)
+  if (k == K::SliceBwdN && pl.prs <= pl.ors)
+    pl.oP = pl.oO;
+  else if (any({K::SliceBwdN, K::DesliceBwdN}))
+    pl.oP = take(nt * pl.prs);
   if (any({K::FusedSliceFwd, K::FusedDesliceBwd, K::SliceFwdG, K::DesliceBwdG}))
     pl.oA = take(nt * pl.ars);
   if (any({K::FusedSliceBwd, K::FusedDesliceBwd, K::SliceBwdG, K::DesliceBwdG}))
