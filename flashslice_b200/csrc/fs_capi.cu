@@ -62,7 +62,24 @@ int check_problem(const fs_problem* p) {
   if (p->flags < 0 || p->flags > 3) return fail(FS_ERR_ARGUMENT, "bad flags %d", p->flags);
   if (p->engine != FS_ENGINE_AUTO && p->engine != FS_ENGINE_FMA)
     return fail(FS_ERR_ARGUMENT, "bad engine %d", p->engine);
+  if (p->row_splits) {
+    const int64_t* r = p->row_splits;
+    if (r[0] != 0 || r[p->B] != p->N)
+      return fail(FS_ERR_SHAPE, "row_splits must run from 0 to N=%lld (got %lld .. %lld)",
+                  (long long)p->N, (long long)r[0], (long long)r[p->B]);
+    for (int64_t b = 0; b < p->B; ++b)
+      if (r[b + 1] < r[b]) return fail(FS_ERR_SHAPE, "row_splits decrease at sample %lld",
+                                       (long long)b);
+  }
   return FS_OK;
+}
+
+// The calls below serve row splits on the tensor-core engine only.
+int ragged_unsupported(const char* op) {
+  return fail(FS_ERR_UNSUPPORTED,
+              "%s with row_splits needs the tensor-core engine: fp32 single-tile problems "
+              "with D = DV = G = 32, TMA-addressable point tensors, at most %d samples", op,
+              FS_MAX_SPLITS);
 }
 
 // ---------------------------------------------------------------- tensor-core path
@@ -109,14 +126,25 @@ bool tc_shape(const fs_problem& p) {
 
 // Fill the tensor-core parameters; false when a tensor map cannot be made
 // (the FMA kernels then serve the call).
+// TMA map of a point tensor of problem p: (B, N) rows, or with row splits
+// one batch entry of N rows.
+bool point_map(CUtensorMap* map, const fs_problem& p, const fs_tensor4* t) {
+  return tcx::make_point_map(map, t->data, p.row_splits ? 1 : p.B, p.N, p.H, t->stride);
+}
+
 bool tc_params(const fs_problem& p, tcx::TcKind k, const fs_tensor4* x, const fs_tensor4* v,
                const float* W, const float* bias, const float* tau, tcx::TcParams& q) {
   q = tcx::TcParams();
-  if (!tcx::make_point_map(&q.mx, x->data, p.B, p.N, p.H, x->stride)) {
+  if (p.row_splits) {
+    if (p.B > tcx::kMaxSplits) return false;
+    q.nsplit = (int)p.B;
+    for (int64_t b = 0; b <= p.B; ++b) q.split[b] = p.row_splits[b];
+  }
+  if (!point_map(&q.mx, p, x)) {
     if (debug_routes()) fprintf(stderr, "[flashslice_b200] tensor map of x_mid refused\n");
     return false;
   }
-  if (v && !tcx::make_point_map(&q.mv, v->data, p.B, p.N, p.H, v->stride)) {
+  if (v && !point_map(&q.mv, p, v)) {
     if (debug_routes()) fprintf(stderr, "[flashslice_b200] tensor map of the value tensor refused\n");
     return false;
   }
@@ -329,6 +357,7 @@ int fs_slice_fwd_noalloc(const fs_problem* p, const fs_tensor4* x_mid, const fs_
   FS_CHECK(need(z_num, "z_num"));
   FS_CHECK(need(s_out, "s"));
   if (p->flags != 0) return fail(FS_ERR_ARGUMENT, "fs_slice_fwd_noalloc takes no statistics");
+  if (p->row_splits) return ragged_unsupported("fs_slice_fwd_noalloc");
   const Setup s = setup(FS_OP_SLICE_FWD, *p);
   if (!s.fused)
     return fail(FS_ERR_UNSUPPORTED,
@@ -388,6 +417,7 @@ int fs_compute_stats(const fs_problem* p, const fs_tensor4* x_mid, const float* 
   FS_CHECK(need(bias, "bias"));
   FS_CHECK(need(tau, "tau"));
   FS_CHECK(need(stats, "stats"));
+  if (p->row_splits) return ragged_unsupported("statistics");
   const Setup s = setup(FS_OP_STATS, *p);
   return run_stats(*p, s, x_mid, weight, bias, tau, stats, (cudaStream_t)stream);
 }
@@ -434,6 +464,8 @@ int fs_slice_fwd(const fs_problem* p, const fs_tensor4* x_mid, const fs_tensor4*
     P = tq.P;
     route_note("slice_fwd", "tensor-core", *p, x_mid, fx_mid);
     FS_TRY(tcx::run_tc(tcx::TcKind::SliceFwd, tq, st));
+  } else if (p->row_splits) {
+    return ragged_unsupported("slice forward");
   } else if (s.fused) {
     P = s.Pn;
     route_note("slice_fwd", "fma-fused", *p, x_mid, fx_mid);
@@ -486,6 +518,7 @@ int fs_deslice_fwd(const fs_problem* p, const fs_tensor4* x_mid, const float* we
     FS_TRY(tcx::run_tc(tcx::TcKind::DesliceFwd, tq, st));
     return FS_OK;
   }
+  if (p->row_splits) return ragged_unsupported("deslice forward");
   route_note("deslice_fwd", s.fused ? "fma-fused" : "fma-blocked", *p, x_mid, out);
   if (s.fused) return launch_kind(Kind::FusedDesliceFwd, *p, s, q, s.Pn, st);
   if (stats_in) {
@@ -565,6 +598,8 @@ static int bwd_common(bool slice, const fs_problem* p, const fs_tensor4* x_mid,
     Pw = Pdt = tq.P;
     route_note(slice ? "slice_bwd" : "deslice_bwd", "tensor-core", *p, x_mid, vals);
     FS_TRY(tcx::run_tc(slice ? tcx::TcKind::SliceBwd : tcx::TcKind::DesliceBwd, tq, st));
+  } else if (p->row_splits) {
+    return ragged_unsupported(slice ? "slice backward" : "deslice backward");
   } else if (s.fused) {
     Pw = s.Pn;
     if (debug_routes())
@@ -614,7 +649,10 @@ int fs_deslice_bwd(const fs_problem* p, const fs_tensor4* x_mid, const float* we
 
 int fs_coupled_supported(const fs_problem* p) {
   if (check_problem(p) != FS_OK) return 0;
-  return setup(FS_OP_SLICE_BWD, *p).fused && tc_shape(*p) && !p->flags ? 1 : 0;
+  return setup(FS_OP_SLICE_BWD, *p).fused && tc_shape(*p) && !p->flags &&
+                 (!p->row_splits || p->B <= FS_MAX_SPLITS)
+             ? 1
+             : 0;
 }
 
 int fs_coupled_bwd(const fs_problem* p, const fs_tensor4* x_mid, const fs_tensor4* fx_mid,
@@ -648,7 +686,7 @@ int fs_coupled_bwd(const fs_problem* p, const fs_tensor4* x_mid, const fs_tensor
                 "strides");
   tcx::TcParams tq;
   if (!tc_params(*p, tcx::TcKind::CoupledBwd, x_mid, fx_mid, weight, bias, tau, tq) ||
-      !tcx::make_point_map(&tq.mo, d_out->data, p->B, p->N, p->H, d_out->stride))
+      !point_map(&tq.mo, *p, d_out))
     return fail(FS_ERR_UNSUPPORTED, "no TMA tensor map for the point tensors");
   cudaStream_t st = (cudaStream_t)stream;
   tq.M = tokens;

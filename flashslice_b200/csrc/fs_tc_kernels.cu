@@ -779,12 +779,28 @@ __device__ __forceinline__ void epilogue(Ctl& c) {
   if ((threadIdx.x >> 5) == 0) tmem_dealloc(c.tmem, NCOLS);
 }
 
+// The points of one b: all N rows of batch entry b, or, with row splits
+// (ragged samples packed along n), rows [split[b], split[b + 1]) of the one
+// batch entry. Tile t covers its rows [128 t, 128 t + 128); rows at or past N
+// are masked (they may be the next sample's, or past the tensor: zeros).
+struct Span {
+  int64_t n0;  // first row in the tensors' n axis
+  int bc;      // b coordinate in the point tensors
+  int N, ntiles;
+  __device__ __forceinline__ int row(int tile) const { return (int)(n0 + (int64_t)tile * kTile); }
+};
+__device__ __forceinline__ Span span_of(const TcParams& p, int b) {
+  if (p.nsplit == 0) return Span{0, b, p.N, p.ntiles};
+  const int64_t a = p.split[b], n = p.split[b + 1] - a;
+  return Span{a, 0, (int)n, (int)((n + kTile - 1) / kTile)};
+}
+
 // issue the TMA loads of one tile (one or two point tensors) on bar
 __device__ __forceinline__ void tma_tile(const TcParams& p, uint8_t* st0, uint8_t* st1, int h,
-                                         int tile, int b, uint64_t* bar) {
+                                         const Span& sp, int tile, uint64_t* bar) {
   mbar_arrive_expect_tx(bar, st1 ? 2 * kStage : kStage);
-  tma_load_4d(st0, &p.mx, 0, h, tile * kTile, b, bar);
-  if (st1) tma_load_4d(st1, &p.mv, 0, h, tile * kTile, b, bar);
+  tma_load_4d(st0, &p.mx, 0, h, sp.row(tile), sp.bc, bar);
+  if (st1) tma_load_4d(st1, &p.mv, 0, h, sp.row(tile), sp.bc, bar);
 }
 
 // Prefetch the tile after `tile` into the staging buffers. Called by one
@@ -795,8 +811,8 @@ __device__ __forceinline__ void tma_tile(const TcParams& p, uint8_t* st0, uint8_
 // writes, and with two CTAs per SM such loads were seen returning the next
 // tile's bytes.
 __device__ __forceinline__ void prefetch(const TcParams& p, uint8_t* st0, uint8_t* st1, int h,
-                                         int tile, int b, uint64_t* bar) {
-  if (tile + p.P < p.ntiles) tma_tile(p, st0, st1, h, tile + p.P, b, bar);
+                                         const Span& sp, int tile, uint64_t* bar) {
+  if (tile + p.P < sp.ntiles) tma_tile(p, st0, st1, h, sp, tile + p.P, bar);
 }
 
 // Per-kernel threads per point row, co-resident CTAs per SM (shared memory,
@@ -856,6 +872,7 @@ __global__ void __launch_bounds__(128 * kTSliceFwd, kCtasSliceFwd)
   uint8_t* sm = align_smem(sm_raw);
   const Th<T> th;
   const int bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
+  const Span sp = span_of(p, b);
   Ctl c = prologue_begin<256>(sm, kSfBar);
   float* red = (float*)(sm + kSfRed);
   put_small<NT>(sm + kSfWs, p.W + (int64_t)b * p.swb + (int64_t)h * p.swh);
@@ -881,23 +898,27 @@ __global__ void __launch_bounds__(128 * kTSliceFwd, kCtasSliceFwd)
     tst_wait();
   };
   int tile = blockIdx.x, buf = 0;
-  if (threadIdx.x == 0) tma_tile(p, stX, fbuf(0), h, tile, b, c.bar);
-  split_tile(0);
-  to_async_barrier();
-  if (threadIdx.x == 0) {
-    prefetch(p, stX, fbuf(1), h, tile, b, c.bar);  // F[1] is unused yet
-    wide_ts<96, false>(tL, tX, dWs);  // logits = x W^T
-    commit(c, kG1);
+  // (a CTA of a sample with fewer tiles than CTAs has none: it writes zero
+  // partials; the condition is the same for every thread)
+  if (tile < sp.ntiles) {
+    if (threadIdx.x == 0) tma_tile(p, stX, fbuf(0), h, sp, tile, c.bar);
+    split_tile(0);
+    to_async_barrier();
+    if (threadIdx.x == 0) {
+      prefetch(p, stX, fbuf(1), h, sp, tile, c.bar);  // F[1] is unused yet
+      wide_ts<96, false>(tL, tX, dWs);  // logits = x W^T
+      commit(c, kG1);
+    }
   }
-  for (; tile < p.ntiles; tile += p.P, buf ^= 1) {
+  for (; tile < sp.ntiles; tile += p.P, buf ^= 1) {
     const int n0 = tile * kTile;
-    const bool more = tile + p.P < p.ntiles;
-    const bool more2 = tile + 2 * p.P < p.ntiles;
+    const bool more = tile + p.P < sp.ntiles;
+    const bool more2 = tile + 2 * p.P < sp.ntiles;
     wait_bar(c, kG1, p.status);
     {
       float lg[C];
       ld_wide<96, C>(tL + th.lane_off, th.cs, lg);
-      softmax_fwd<T, C>(lg, rc, n0 + th.row < p.N, red, th);
+      softmax_fwd<T, C>(lg, rc, n0 + th.row < sp.N, red, th);
       Split<C>(lg).to_smem(sm + kSfWS, th.row, th.cs);
 #pragma unroll
       for (int k = 0; k < C / 2; ++k) put2(accs, k, __fadd2_rn(f2(accs, k), f2(lg, k)));
@@ -913,7 +934,7 @@ __global__ void __launch_bounds__(128 * kTSliceFwd, kCtasSliceFwd)
       if (threadIdx.x == 0) {
         if (more2) {  // tile i+2: its x now, its fx once tile i's pool is done with F[buf]
           mbar_arrive_expect_tx(c.bar + kBarTma, 2 * kStage);
-          tma_load_4d(stX, &p.mx, 0, h, (tile + 2 * p.P) * kTile, b, c.bar + kBarTma);
+          tma_load_4d(stX, &p.mx, 0, h, sp.row(tile + 2 * p.P), sp.bc, c.bar + kBarTma);
         }
         wide_ts<96, false>(tL, tX, dWs);
         commit(c, kG1);
@@ -921,7 +942,7 @@ __global__ void __launch_bounds__(128 * kTSliceFwd, kCtasSliceFwd)
     }
     wait_bar(c, kG2, p.status);
     if (threadIdx.x == 0 && more2)
-      tma_load_4d(fbuf(buf), &p.mv, 0, h, (tile + 2 * p.P) * kTile, b, c.bar + kBarTma);
+      tma_load_4d(fbuf(buf), &p.mv, 0, h, sp.row(tile + 2 * p.P), sp.bc, c.bar + kBarTma);
     if (th.q < 3) drain_pool<C>(tP + th.lane_off, th.cs, accz);
   }
   const int64_t slot = (int64_t)bh * p.P + blockIdx.x;
@@ -948,6 +969,7 @@ __global__ void __launch_bounds__(128 * kTDesliceFwd, kCtasDesliceFwd)
   uint8_t* sm = align_smem(sm_raw);
   const Th<T> th;
   const int bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
+  const Span sp = span_of(p, b);
   Ctl c = prologue_begin<kDfCols>(sm, kDfBar);
   float* red = (float*)(sm + kDfRed);
   put_small<NT>(sm + kDfWs, p.W + (int64_t)b * p.swb + (int64_t)h * p.swh);
@@ -962,8 +984,8 @@ __global__ void __launch_bounds__(128 * kTDesliceFwd, kCtasDesliceFwd)
   const uint64_t dWs = desc_smallK(sm + kDfWs);
   const uint64_t dTs = kNwDf == 32 ? desc_smallM(sm + kDfTs) : desc_stacked(sm + kDfTs);
   int tile = blockIdx.x;
-  if (threadIdx.x == 0) tma_tile(p, sm + kDfStageX, nullptr, h, tile, b, c.bar);
-  for (; tile < p.ntiles; tile += p.P) {
+  if (threadIdx.x == 0 && tile < sp.ntiles) tma_tile(p, sm + kDfStageX, nullptr, h, sp, tile, c.bar);
+  for (; tile < sp.ntiles; tile += p.P) {
     const int n0 = tile * kTile;
     wait_bar(c, kBarTma, p.status);
     {
@@ -974,7 +996,7 @@ __global__ void __launch_bounds__(128 * kTDesliceFwd, kCtasDesliceFwd)
     }
     to_async_barrier();
     if (threadIdx.x == 0) {
-      prefetch(p, sm + kDfStageX, nullptr, h, tile, b, c.bar);
+      prefetch(p, sm + kDfStageX, nullptr, h, sp, tile, c.bar);
       wide_ts<kNwDf, false>(tL, tA, dWs);  // logits = x W^T
       commit(c, kG1);
     }
@@ -993,9 +1015,9 @@ __global__ void __launch_bounds__(128 * kTDesliceFwd, kCtasDesliceFwd)
     }
     wait_bar(c, kG2, p.status);
     store_result<kNwDf, C>(tL, th.q, th.cs,
-                           p.out + (int64_t)b * p.so[0] + (int64_t)n0 * p.so[1] +
+                           p.out + (int64_t)sp.bc * p.so[0] + (sp.n0 + n0) * p.so[1] +
                                (int64_t)h * p.so[2],
-                           p.so[1], p.N - n0);
+                           p.so[1], sp.N - n0);
   }
   epilogue<kDfCols>(c);
 }
@@ -1020,6 +1042,7 @@ __global__ void __launch_bounds__(128 * kTSliceBwd, kCtasSliceBwd)
   uint8_t* sm = align_smem(sm_raw);
   const Th<T> th;
   const int bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
+  const Span sp = span_of(p, b);
   Ctl c = prologue_begin<256>(sm, kSbBar);
   float* ds_s = (float*)(sm + kSbDs);
   float* red = (float*)(sm + kSbRed);
@@ -1040,10 +1063,11 @@ __global__ void __launch_bounds__(128 * kTSliceBwd, kCtasSliceBwd)
 #pragma unroll
   for (int i = 0; i < C; ++i) accw[i] = accb[i] = 0.f;
   int tile = blockIdx.x;
-  if (threadIdx.x == 0) tma_tile(p, sm + kSbStageX, sm + kSbStageF, h, tile, b, c.bar);
-  for (; tile < p.ntiles; tile += p.P) {
+  if (threadIdx.x == 0 && tile < sp.ntiles)
+    tma_tile(p, sm + kSbStageX, sm + kSbStageF, h, sp, tile, c.bar);
+  for (; tile < sp.ntiles; tile += p.P) {
     const int n0 = tile * kTile;
-    const bool valid = n0 + th.row < p.N;
+    const bool valid = n0 + th.row < sp.N;
     wait_bar(c, kBarTma, p.status);
     {
       float x[C], f[C];
@@ -1057,7 +1081,7 @@ __global__ void __launch_bounds__(128 * kTSliceBwd, kCtasSliceBwd)
     }
     to_async_barrier();
     if (threadIdx.x == 0) {
-      prefetch(p, sm + kSbStageX, sm + kSbStageF, h, tile, b, c.bar);
+      prefetch(p, sm + kSbStageX, sm + kSbStageF, h, sp, tile, c.bar);
       wide_ts<96, false>(tL, tX, dWk);  // logits = x W^T
       commit(c, kG1);
       wide_ts<64, false>(tDw, tF, dZk);  // dw = fx dz_num^T
@@ -1092,13 +1116,13 @@ __global__ void __launch_bounds__(128 * kTSliceBwd, kCtasSliceBwd)
     }
     wait_bar(c, kG3, p.status);
     store_result<32, C>(tDfx, th.q, th.cs,
-                        p.out2 + (int64_t)b * p.so2[0] + (int64_t)n0 * p.so2[1] +
+                        p.out2 + (int64_t)sp.bc * p.so2[0] + (sp.n0 + n0) * p.so2[1] +
                             (int64_t)h * p.so2[2],
-                        p.so2[1], p.N - n0);
+                        p.so2[1], sp.N - n0);
     store_result<32, C>(tDx, th.q, th.cs,
-                        p.out + (int64_t)b * p.so[0] + (int64_t)n0 * p.so[1] +
+                        p.out + (int64_t)sp.bc * p.so[0] + (sp.n0 + n0) * p.so[1] +
                             (int64_t)h * p.so[2],
-                        p.so[1], p.N - n0);
+                        p.so[1], sp.N - n0);
     wait_bar(c, kG4, p.status);
     if (th.q < 3) drain_pool<C>(tP + th.lane_off, th.cs, accw);
   }
@@ -1134,6 +1158,7 @@ __global__ void __launch_bounds__(128 * kTDesliceBwd, kCtasDesliceBwd)
   uint8_t* sm = align_smem(sm_raw);
   const Th<T> th;
   const int bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
+  const Span sp = span_of(p, b);
   Ctl c = prologue_begin<256>(sm, kDbBar);
   float* red = (float*)(sm + kDbRed);
   put_small<NT>(sm + kDbWs, p.W + (int64_t)b * p.swb + (int64_t)h * p.swh);
@@ -1154,11 +1179,11 @@ __global__ void __launch_bounds__(128 * kTDesliceBwd, kCtasDesliceBwd)
 #pragma unroll
   for (int i = 0; i < C; ++i) acct[i] = accw[i] = accb[i] = 0.f;
   int tile = blockIdx.x;
-  if (threadIdx.x == 0) tma_tile(p, stX, stO, h, tile, b, c.bar);
-  for (; tile < p.ntiles; tile += p.P) {
+  if (threadIdx.x == 0 && tile < sp.ntiles) tma_tile(p, stX, stO, h, sp, tile, c.bar);
+  for (; tile < sp.ntiles; tile += p.P) {
     const int n0 = tile * kTile;
-    const bool valid = n0 + th.row < p.N;
-    const bool more = tile + p.P < p.ntiles;
+    const bool valid = n0 + th.row < sp.N;
+    const bool more = tile + p.P < sp.ntiles;
     wait_bar(c, kBarTma, p.status);
     {
       float x[C], o[C];
@@ -1204,9 +1229,9 @@ __global__ void __launch_bounds__(128 * kTDesliceBwd, kCtasDesliceBwd)
     }
     wait_bar(c, kG3, p.status);
     store_result<32, C>(tDx, th.q, th.cs,
-                        p.out + (int64_t)b * p.so[0] + (int64_t)n0 * p.so[1] +
+                        p.out + (int64_t)sp.bc * p.so[0] + (sp.n0 + n0) * p.so[1] +
                             (int64_t)h * p.so[2],
-                        p.so[1], p.N - n0);
+                        p.so[1], sp.N - n0);
     wait_bar(c, kG4, p.status);
     if (th.q < 3) drain_pool<C>(tP + th.lane_off, th.cs, acct);
     tc_fence_before();
@@ -1215,14 +1240,14 @@ __global__ void __launch_bounds__(128 * kTDesliceBwd, kCtasDesliceBwd)
     if (threadIdx.x == 0) {
       if (more) {
         mbar_arrive_expect_tx(c.bar + kBarTma, 2 * kStage);
-        tma_load_4d(stX, &p.mx, 0, h, (tile + p.P) * kTile, b, c.bar + kBarTma);
+        tma_load_4d(stX, &p.mx, 0, h, sp.row(tile + p.P), sp.bc, c.bar + kBarTma);
       }
       mma_pool(tP, dUp, dXb);  // dW += (dl/tau)^T x
       commit(c, kG5);
     }
     wait_bar(c, kG5, p.status);
     if (threadIdx.x == 0 && more)  // UP is free once the dW pool is done
-      tma_load_4d(stO, &p.mv, 0, h, (tile + p.P) * kTile, b, c.bar + kBarTma);
+      tma_load_4d(stO, &p.mv, 0, h, sp.row(tile + p.P), sp.bc, c.bar + kBarTma);
     if (th.q < 3) drain_pool<C>(tP + th.lane_off, th.cs, accw);
   }
   const int64_t slot = (int64_t)bh * p.P + blockIdx.x;
@@ -1274,6 +1299,7 @@ __global__ void __launch_bounds__(128 * kTCoupledBwd, kCtasCoupledBwd)
   uint8_t* sm = align_smem(sm_raw);
   const Th<T> th;
   const int bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
+  const Span sp = span_of(p, b);
   Ctl c = prologue_begin<256>(sm, kCbBar);
   float* ds_s = (float*)(sm + kCbDs);
   float* red = (float*)(sm + kCbRed);
@@ -1300,16 +1326,16 @@ __global__ void __launch_bounds__(128 * kTCoupledBwd, kCtasCoupledBwd)
 #pragma unroll
   for (int i = 0; i < C; ++i) accw[i] = accb[i] = 0.f;
   int tile = blockIdx.x;
-  if (threadIdx.x == 0) {
+  if (threadIdx.x == 0 && tile < sp.ntiles) {
     mbar_arrive_expect_tx(c.bar + kBarTma, 3 * kStage);
-    tma_load_4d(stX, &p.mx, 0, h, tile * kTile, b, c.bar + kBarTma);
-    tma_load_4d(stF, &p.mv, 0, h, tile * kTile, b, c.bar + kBarTma);
-    tma_load_4d(stO, &p.mo, 0, h, tile * kTile, b, c.bar + kBarTma);
+    tma_load_4d(stX, &p.mx, 0, h, sp.row(tile), sp.bc, c.bar + kBarTma);
+    tma_load_4d(stF, &p.mv, 0, h, sp.row(tile), sp.bc, c.bar + kBarTma);
+    tma_load_4d(stO, &p.mo, 0, h, sp.row(tile), sp.bc, c.bar + kBarTma);
   }
-  for (; tile < p.ntiles; tile += p.P) {
+  for (; tile < sp.ntiles; tile += p.P) {
     const int n0 = tile * kTile;
-    const bool valid = n0 + th.row < p.N;
-    const bool more = tile + p.P < p.ntiles;
+    const bool valid = n0 + th.row < sp.N;
+    const bool more = tile + p.P < sp.ntiles;
     wait_bar(c, kBarTma, p.status);
     {
       float x[C], f[C], o[C];
@@ -1325,8 +1351,8 @@ __global__ void __launch_bounds__(128 * kTCoupledBwd, kCtasCoupledBwd)
     if (threadIdx.x == 0) {
       if (more) {  // x and fx of the next tile; its d_out once UP is free
         mbar_arrive_expect_tx(c.bar + kBarTma, 3 * kStage);
-        tma_load_4d(stX, &p.mx, 0, h, (tile + p.P) * kTile, b, c.bar + kBarTma);
-        tma_load_4d(stF, &p.mv, 0, h, (tile + p.P) * kTile, b, c.bar + kBarTma);
+        tma_load_4d(stX, &p.mx, 0, h, sp.row(tile + p.P), sp.bc, c.bar + kBarTma);
+        tma_load_4d(stF, &p.mv, 0, h, sp.row(tile + p.P), sp.bc, c.bar + kBarTma);
       }
       wide_ss96(tL, dXa, dWk);  // logits = x W^T
       commit(c, kG1);
@@ -1362,17 +1388,17 @@ __global__ void __launch_bounds__(128 * kTCoupledBwd, kCtasCoupledBwd)
     }
     wait_bar(c, kG3, p.status);
     if (threadIdx.x == 0 && more)  // UP is free once the dW pool is done
-      tma_load_4d(stO, &p.mo, 0, h, (tile + p.P) * kTile, b, c.bar + kBarTma);
+      tma_load_4d(stO, &p.mo, 0, h, sp.row(tile + p.P), sp.bc, c.bar + kBarTma);
     if (th.q < 3) drain_pool<C>(tP + th.lane_off, th.cs, accw);
     wait_bar(c, kG4, p.status);
     store_result<32, C>(tDfx, th.q, th.cs,
-                        p.out2 + (int64_t)b * p.so2[0] + (int64_t)n0 * p.so2[1] +
+                        p.out2 + (int64_t)sp.bc * p.so2[0] + (sp.n0 + n0) * p.so2[1] +
                             (int64_t)h * p.so2[2],
-                        p.so2[1], p.N - n0);
+                        p.so2[1], sp.N - n0);
     store_result<32, C>(tDx, th.q, th.cs,
-                        p.out + (int64_t)b * p.so[0] + (int64_t)n0 * p.so[1] +
+                        p.out + (int64_t)sp.bc * p.so[0] + (sp.n0 + n0) * p.so[1] +
                             (int64_t)h * p.so[2],
-                        p.so[1], p.N - n0);
+                        p.so[1], sp.N - n0);
   }
   const int64_t slot = (int64_t)bh * p.P + blockIdx.x;
   float* xch = (float*)(sm + kCbX);

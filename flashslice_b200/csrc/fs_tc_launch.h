@@ -13,6 +13,8 @@ namespace tcx {
 
 enum class TcKind { SliceFwd, DesliceFwd, SliceBwd, DesliceBwd, CoupledBwd };
 
+constexpr int kMaxSplits = 128;  // FS_MAX_SPLITS
+
 struct TcParams {
   CUtensorMap mx;  // x_mid: (32, H, N, B) fp32 tiles of 128 points
   CUtensorMap mv;  // fx_mid or d_out, same shape
@@ -34,6 +36,10 @@ struct TcParams {
   float* partS;
   float* partDt;
   int* status;      // device word: set to a non-zero code when a bounded wait gives up
+  // ragged samples: nsplit = B > 0 and split[0 .. B] the row offsets of the
+  // samples in the point tensors' single batch entry; 0 = dense
+  int nsplit;
+  int64_t split[kMaxSplits + 1];
 };
 
 cudaError_t run_tc(TcKind k, const TcParams& p, cudaStream_t s);

@@ -8,7 +8,9 @@ run in hand-written sm_100a kernels reached through the C ABI of
 
 Exports mirror the reference (``flashslice/kernels/__init__.py:44-59``);
 ``fused_coupling`` (a whole slice -> tokens -> deslice round with a tied
-backward) has no reference counterpart.
+backward) and the ragged-batch forms ``ragged_slice``, ``ragged_deslice``,
+``ragged_coupling`` (samples of different N in one launch per op) have no
+reference counterpart.
 """
 
 from .slice_ops import (fused_slice, fused_deslice, fused_coupling, unsupported_dims,
@@ -17,8 +19,10 @@ from .slice_ops import (fused_slice, fused_deslice, fused_coupling, unsupported_
 from . import blocked  # noqa: F401  -- registers the flashslice::*_blk ops
 from .blocked import set_block_g, set_stats_mode, stats_mode
 from ._state import set_engine
+from .ragged import ragged_slice, ragged_deslice, ragged_coupling
 
 __all__ = ["fused_slice", "fused_deslice", "fused_coupling", "unsupported_dims",
            "single_tile_dims",
            "set_dot_mode", "set_kernel_mode", "set_block_g", "set_stats_mode",
-           "stats_mode", "set_tile_table", "tile_table", "set_engine"]
+           "stats_mode", "set_tile_table", "tile_table", "set_engine", "ragged_slice",
+           "ragged_deslice", "ragged_coupling"]

@@ -14,7 +14,7 @@ import torch
 _PKG = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 LIBPATH = os.path.join(_PKG, "_native", "libflashslice_b200.so")
 
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 FS_OK, FS_ERR_SHAPE, FS_ERR_ARGUMENT, FS_ERR_WORKSPACE, FS_ERR_CUDA, FS_ERR_TIMEOUT, \
     FS_ERR_UNSUPPORTED = range(7)
@@ -34,7 +34,7 @@ class Problem(ctypes.Structure):
     _fields_ = [("B", _I64), ("N", _I64), ("H", _I64), ("D", _I64), ("DV", _I64), ("G", _I64),
                 ("act_dtype", _I32), ("dot", _I32), ("family", _I32), ("stats_mode", _I32),
                 ("w_batch", _I32), ("w_heads", _I32), ("b_batch", _I32), ("b_heads", _I32),
-                ("flags", _I32), ("engine", _I32)]
+                ("flags", _I32), ("engine", _I32), ("row_splits", _P)]
 
 
 class Tensor4(ctypes.Structure):

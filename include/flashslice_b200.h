@@ -49,7 +49,7 @@
 extern "C" {
 #endif
 
-#define FS_ABI_VERSION 1
+#define FS_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define FS_API __attribute__((visibility("default")))
@@ -95,7 +95,18 @@ typedef struct fs_problem {
   int32_t flags;       /* FS_FLAG_* : which optional statistics buffers the
                           call passes; part of the workspace size contract    */
   int32_t engine;      /* FS_ENGINE_*: 0 lets the library choose */
+  /* Ragged samples (NULL: B dense samples of N points each). Otherwise a
+   * HOST array of B + 1 non-decreasing row offsets, row_splits[0] = 0 and
+   * row_splits[B] = N: the point tensors hold one batch entry of N rows and
+   * sample b owns rows [row_splits[b], row_splits[b + 1]); weight, bias,
+   * tokens, z_num, s and the parameter gradients keep their per-sample
+   * (B, ...) layouts. Served by the tensor-core engine (FS_MAX_SPLITS samples
+   * at most a call); other problems return FS_ERR_UNSUPPORTED. The reference
+   * plans this in ROADMAP.md:66-68 ("Ragged batching"). */
+  const int64_t* row_splits;
 } fs_problem;
+
+#define FS_MAX_SPLITS 128
 
 /* Engine selection. FS_ENGINE_AUTO runs the tensor-core kernels where they
  * serve the problem (single-tile family, fp32, D = DV = G = 32, TMA-friendly

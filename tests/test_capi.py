@@ -34,8 +34,9 @@ def test_library_exports_every_declared_symbol():
 
 
 def test_struct_layout_matches_header():
-    # int64 x6 + int32 x10
-    assert ctypes.sizeof(nat.Problem) == 6 * 8 + 10 * 4
+    # int64 x6 + int32 x10 + the row_splits pointer
+    assert ctypes.sizeof(nat.Problem) == 6 * 8 + 10 * 4 + 8
+    assert nat.Problem.row_splits.offset == 6 * 8 + 10 * 4
     assert ctypes.sizeof(nat.Tensor4) == 8 + 4 * 8
 
 
@@ -108,3 +109,17 @@ def test_stats_flags_must_match_pointers():
     rc = lib.fs_slice_fwd(ctypes.byref(p), ctypes.byref(t), ctypes.byref(t), one, one, one, None,
                           None, one, one, None, 0, None)
     assert rc == nat.FS_ERR_ARGUMENT
+
+
+def test_row_splits_validated_without_gpu():
+    """Row splits must run from 0 to N without decreasing; the check needs no
+    GPU (fs_coupled_supported reports 0 for a problem that fails it)."""
+    import ctypes
+    lib = nat.load()
+    for splits, ok in (([0, 40, 100], 1), ([0, 60, 40, 100], 0), ([0, 50, 99], 0),
+                       ([1, 50, 100], 0)):
+        arr = (ctypes.c_int64 * len(splits))(*splits)
+        p = prob(B=len(splits) - 1, N=100)
+        p.row_splits = ctypes.cast(arr, ctypes.c_void_p)
+        assert lib.fs_coupled_supported(ctypes.byref(p)) == ok, splits
+
