@@ -404,6 +404,14 @@ int fs_device_status(int reset) {
   return v;
 }
 
+int fs_selftest_wait_timeout(uint64_t limit_ns, void* stream) {
+  if (limit_ns == 0 || limit_ns > 2000000000ull)
+    return fail(FS_ERR_ARGUMENT, "limit_ns must be in (0, 2e9], got %llu",
+                (unsigned long long)limit_ns);
+  FS_TRY(tcx::run_wait_selftest(limit_ns, (cudaStream_t)stream));
+  return FS_OK;
+}
+
 size_t fs_workspace_bytes(int op, const fs_problem* p) {
   if (check_problem(p) != FS_OK) return 0;
   return setup(op, *p).total;

@@ -63,13 +63,14 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 }
 
 // Wait for the phase with the given parity to complete; false (and *status
-// set) if it does not within kWaitNs.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status) {
+// set) if it does not within limit_ns (kWaitNs in the kernels).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status,
+                                          uint64_t limit_ns = kWaitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 0; i < (1u << 30); ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (globaltimer_ns() - t0 > kWaitNs) break;
+    if (globaltimer_ns() - t0 > limit_ns) break;
   }
   if (status) atomicExch(status, kErrTimeout);
   return false;

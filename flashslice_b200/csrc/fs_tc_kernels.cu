@@ -1410,6 +1410,19 @@ __global__ void __launch_bounds__(128 * kTCoupledBwd, kCtasCoupledBwd)
   epilogue<256>(c);
 }
 
+// ------------------------------------------------------------ wait self-test
+// One thread waits, with a limit of limit_ns, on an mbarrier that nothing
+// arrives at: the bounded-wait path of the kernels (status word set, the
+// kernel returns, the context stays usable), exercised without a fault.
+__global__ void k_tc_wait_selftest(int* status, uint64_t limit_ns) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+    mbar_wait(&bar, 0, status, limit_ns);
+  }
+}
+
 // ------------------------------------------------------------ host side
 
 static __device__ int fs_tc_status_word;
@@ -1503,6 +1516,14 @@ cudaError_t run_tc(TcKind k, const TcParams& p, cudaStream_t s) {
   if (e != cudaSuccess) return e;
   g_launches.fetch_add(1, std::memory_order_relaxed);
   g_tc_launches.fetch_add(1, std::memory_order_relaxed);
+  return cudaGetLastError();
+}
+
+cudaError_t run_wait_selftest(uint64_t limit_ns, cudaStream_t s) {
+  int* word = device_status();
+  if (!word) return cudaErrorInvalidValue;
+  k_tc_wait_selftest<<<1, 32, 0, s>>>(word, limit_ns);
+  g_launches.fetch_add(1, std::memory_order_relaxed);
   return cudaGetLastError();
 }
 

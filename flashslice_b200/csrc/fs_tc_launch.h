@@ -44,6 +44,9 @@ struct TcParams {
 
 cudaError_t run_tc(TcKind k, const TcParams& p, cudaStream_t s);
 
+// one bounded wait that runs out (limit_ns), on `s`: sets the status word
+cudaError_t run_wait_selftest(uint64_t limit_ns, cudaStream_t s);
+
 // tensor-core kernels launched (also counted in fs::g_launches)
 extern std::atomic<uint64_t> g_tc_launches;
 int tc_ctas_per_sm(TcKind k);

@@ -65,6 +65,7 @@ SIGNATURES = {
                                       _P, _P, _P, ctypes.c_size_t, _P]),
     "fs_coupled_supported": (ctypes.c_int, [_PP]),
     "fs_rank_sum": (ctypes.c_int, [_P, _P, ctypes.c_int, ctypes.c_int64, _P]),
+    "fs_selftest_wait_timeout": (ctypes.c_int, [ctypes.c_uint64, _P]),
 }
 
 ENGINE_AUTO, ENGINE_FMA = 0, 1

@@ -146,6 +146,13 @@ FS_API uint64_t fs_tc_launch_count(void);
  * counterpart. */
 FS_API int fs_device_status(int reset);
 
+/* Self-test of the bounded-wait path: launches on `stream` one kernel whose
+ * single wait (on an mbarrier nothing arrives at) gives up after limit_ns
+ * (at most 2e9) and sets the status word to 1, as a kernel's timed-out wait
+ * does; the kernel then returns and the context stays usable. No reference
+ * counterpart. */
+FS_API int fs_selftest_wait_timeout(uint64_t limit_ns, void* stream);
+
 /* Bytes of workspace `op` needs for problem `p` (0 when it needs none). */
 FS_API size_t fs_workspace_bytes(int op, const fs_problem* p);
 

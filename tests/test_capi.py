@@ -123,3 +123,9 @@ def test_row_splits_validated_without_gpu():
         p.row_splits = ctypes.cast(arr, ctypes.c_void_p)
         assert lib.fs_coupled_supported(ctypes.byref(p)) == ok, splits
 
+
+def test_wait_selftest_argument_checked_without_gpu():
+    lib = nat.load()
+    assert lib.fs_selftest_wait_timeout(0, None) == nat.FS_ERR_ARGUMENT
+    assert lib.fs_selftest_wait_timeout(3_000_000_000, None) == nat.FS_ERR_ARGUMENT
+

@@ -141,3 +141,24 @@ def test_round_deterministic(env):
     c = _round(K, st, "auto", (x, fx, W, b, tau), r)
     for k in a:
         assert torch.equal(a[k], c[k]), k
+
+
+def test_bounded_wait_reports_and_context_survives(env):
+    """A device-side wait that runs out (an mbarrier nothing arrives at, 5 ms
+    limit) sets the status word, its kernel returns, and the same context
+    then runs the tensor-core kernels correctly: failure detection without a
+    GPU fault."""
+    import ctypes
+    K, st, lib = env
+    from flashslice_b200.kernels import _native as nat
+    assert lib.fs_device_status(1) == 0
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    nat.check(lib.fs_selftest_wait_timeout(5_000_000, stream))
+    assert lib.fs_device_status(1) == 1
+    assert lib.fs_device_status(0) == 0
+    x, fx, W, b, tau, tok = _inputs(4097, "hgd")
+    tc = _run(K, st, "auto", x, fx, W, b, tau, tok)
+    ex = _run(K, st, "fma", x, fx, W, b, tau, tok)
+    for a, e in zip(tc, ex):
+        assert relerr(a, e) <= 1e-5
+    assert lib.fs_device_status(1) == 0
