@@ -70,9 +70,12 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--config", choices=sorted(CONFIGS), default="cfg2")
+    ap.add_argument("--config", choices=sorted(CONFIGS) + ["cfg4"], default="cfg2")
     ap.add_argument("--n", type=int, default=None, help="override the point count")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--tf32-gemms", action="store_true",
+                    help="config 4: let the model's torch GEMMs use TF32 (the coupling ops "
+                         "stay exact fp32 either way)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-sample", type=int, default=131072,
                     help="points per CPU-baseline step")
@@ -373,10 +376,82 @@ def run_reference(args, cfg):
     print(json.dumps(line), flush=True)
 
 
+# --------------------------------------------------------------------------- config 4
+
+MODEL4 = dict(space_dim=3, fun_dim=1, out_dim=4, n_hidden=256, n_heads=8, n_layers=8,
+              slice_num=32)
+
+
+def run_model(args):
+    """Config 4: one training step (forward, MSE backward, Adam) of the
+    Transolver with the fused ops, on one GPU, next to the same model on its
+    eager slice/deslice path (identical weights and data)."""
+    from flashslice_b200 import Transolver
+    torch.backends.cuda.matmul.allow_tf32 = bool(args.tf32_gemms)
+    device = torch.device("cuda", 0)
+    n = args.n or 200_000
+    g = torch.Generator(device="cpu").manual_seed(0)
+    xs = torch.rand(1, n, 3, generator=g).to(device)
+    fs = torch.randn(1, n, 1, generator=g).to(device)
+    ys = torch.randn(1, n, 4, generator=g).to(device)
+    torch.manual_seed(0)
+    fused = Transolver(**MODEL4, use_fused_slice=True).to(device)
+    eager = Transolver(**MODEL4, use_fused_slice=False).to(device)
+    eager.load_state_dict(fused.state_dict())
+    lib = __import__("flashslice_b200.kernels._native", fromlist=["load"]).load()
+
+    def timed(model):
+        opt = torch.optim.Adam(model.parameters(), lr=1e-4)
+
+        def step():
+            opt.zero_grad(set_to_none=True)
+            loss = torch.nn.functional.mse_loss(model(xs, fs), ys)
+            loss.backward()
+            opt.step()
+
+        for _ in range(max(args.warmup, 1)):
+            step()
+        torch.cuda.synchronize()
+        launches0 = lib.fs_launch_count()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            step()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / args.steps, lib.fs_launch_count() - launches0
+
+    clocks = ClockSampler(0)
+    clocks.start()
+    ms, launches = timed(fused)
+    clk = clocks.stop()
+    ms_eager, _ = timed(eager)
+    line = {"metric": METRIC, "value": round(n / (ms * 1e-3) / 1e6, 3), "unit": UNIT,
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, U[0,1]^3 points)",
+            "config": {"workload": "cfg4", "model": "Transolver", **MODEL4, "N": n,
+                       "step": "forward + MSE backward + Adam", "l2": "activations larger "
+                       "than L2, no flush", "gemms": "tf32" if args.tf32_gemms else "fp32",
+                       "eager_ms_per_step": round(ms_eager, 4),
+                       "speedup_vs_eager": round(ms_eager / ms, 3)},
+            "gpu_launches": launches,
+            "roofline": None, "roofline_note": "a whole model step: projection GEMMs and "
+            "MLPs (cuBLAS) dominate; the coupling ops are measured by the default workload",
+            "cpu_baseline": None, "e2e": None, "clocks": clk}
+    print(json.dumps(line), flush=True)
+
+
 # --------------------------------------------------------------------------- main
 
 def main():
     args = parse()
+    if args.config == "cfg4":
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "config 4 is a model step; "
+                              "the reference arm times the coupling round (default config)"}))
+            return None
+        return run_model(args)
     cfg = dict(CONFIGS[args.config])
     if args.n is not None:
         cfg["N"] = args.n
