@@ -120,7 +120,8 @@ void route_note(const char* op, const char* engine, const fs_problem& p, const f
 }
 
 bool tc_shape(const fs_problem& p) {
-  return p.engine == FS_ENGINE_AUTO && p.family == FS_FAMILY_SINGLE && p.act_dtype == FS_F32 &&
+  return p.engine == FS_ENGINE_AUTO && p.family == FS_FAMILY_SINGLE &&
+         (p.act_dtype == FS_F32 || p.act_dtype == FS_BF16) &&
          p.D == 32 && p.DV == 32 && p.G == 32 && p.N >= 1;
 }
 
@@ -129,12 +130,14 @@ bool tc_shape(const fs_problem& p) {
 // TMA map of a point tensor of problem p: (B, N) rows, or with row splits
 // one batch entry of N rows.
 bool point_map(CUtensorMap* map, const fs_problem& p, const fs_tensor4* t) {
-  return tcx::make_point_map(map, t->data, p.row_splits ? 1 : p.B, p.N, p.H, t->stride);
+  return tcx::make_point_map(map, t->data, p.row_splits ? 1 : p.B, p.N, p.H, t->stride,
+                             p.act_dtype == FS_BF16 ? 1 : 0);
 }
 
 bool tc_params(const fs_problem& p, tcx::TcKind k, const fs_tensor4* x, const fs_tensor4* v,
                const float* W, const float* bias, const float* tau, tcx::TcParams& q) {
   q = tcx::TcParams();
+  q.pdt = p.act_dtype == FS_BF16 ? 1 : 0;
   if (p.row_splits) {
     if (p.B > tcx::kMaxSplits) return false;
     q.nsplit = (int)p.B;

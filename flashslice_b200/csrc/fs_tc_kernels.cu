@@ -284,6 +284,14 @@ struct Split {
 #pragma unroll
     for (int k = 0; k < C / 2; ++k) split_pair(f2(v, k), hw[k], mw[k], lw[k]);
   }
+  // values that are bf16 already: they are their own hi part, mid = lo = 0
+  __device__ __forceinline__ explicit Split(const uint32_t (&bf16_pairs)[C / 2]) {
+#pragma unroll
+    for (int k = 0; k < C / 2; ++k) {
+      hw[k] = bf16_pairs[k];
+      mw[k] = lw[k] = 0u;
+    }
+  }
   // into a stacked buffer as row `row`, columns [C cs, C cs + C)
   __device__ __forceinline__ void to_smem(uint8_t* buf, int row, int cs) const {
     uint8_t* base = buf + (row >> 3) * kRS + (row & 7) * 16;
@@ -307,6 +315,52 @@ struct Split {
     tst<C / 2>(a + 32, hw);
   }
 };
+
+// This thread's C columns of one row of a point tile staged by TMA, in the
+// tile's type: fp32 (128-byte rows, 128B swizzle: chunk j at j ^ (r % 8)),
+// split three ways, or bf16 (64-byte rows, 64B swizzle: chunk j at
+// j ^ ((r / 2) % 4)), exact as its own hi part. Read into registers first
+// (load), split where the caller consumes them.
+template <int C, typename PT>
+struct RowVals;
+template <int C>
+struct RowVals<C, float> {
+  float v[C];
+  __device__ __forceinline__ void load(const uint8_t* tile, int row, int cs) {
+    read_cols<C>(tile, row, cs, v);
+  }
+  __device__ __forceinline__ Split<C> split() const { return Split<C>(v); }
+};
+template <int C>
+struct RowVals<C, __nv_bfloat16> {
+  uint32_t w[C / 2];
+  __device__ __forceinline__ void load(const uint8_t* tile, int row, int cs) {
+    const uint8_t* r = tile + row * 64;
+#pragma unroll
+    for (int i = 0; i < C / 8; ++i) {
+      const int j = cs * (C / 8) + i;
+      const uint4 q = *(const uint4*)(r + ((j ^ ((row >> 1) & 3)) << 4));
+      w[4 * i] = q.x;
+      w[4 * i + 1] = q.y;
+      w[4 * i + 2] = q.z;
+      w[4 * i + 3] = q.w;
+    }
+  }
+  __device__ __forceinline__ Split<C> split() const { return Split<C>(w); }
+};
+
+// bytes of one staged point tile of type PT (128 points x 32 values)
+template <typename PT>
+__host__ __device__ constexpr int stage_bytes() {
+  return kTile * 32 * (int)sizeof(PT);
+}
+
+// two result values of a row stored in the point tensor's type
+__device__ __forceinline__ void store2(float* p, float2 v) { *(float2*)p = v; }
+__device__ __forceinline__ void store2(__nv_bfloat16* p, float2 v) {
+  *(__nv_bfloat162*)p = __float22bfloat162_rn(v);
+}
+
 
 // A 32 x 32 fp32 matrix M (row-major) split into the three-part small
 // operand at dst: part p (0 lo, 1 mid, 2 hi) at +2048 p, K-major with rows r
@@ -349,8 +403,8 @@ __device__ __forceinline__ void put_small_stacked(uint8_t* dst, const float* M) 
 // 32-column accumulator (NW = 32) or an N-stacked one whose column groups
 // are added small first (NW = 64, 96). Rows at or past `nvalid` are not
 // written.
-template <int NW, int C>
-__device__ __forceinline__ void store_result(uint32_t tcol, int q, int cs, float* row0,
+template <int NW, int C, typename PT>
+__device__ __forceinline__ void store_result(uint32_t tcol, int q, int cs, PT* row0,
                                              int64_t row_stride, int nvalid) {
   const int t = threadIdx.x & 31;
   constexpr int J = C / 8;
@@ -376,7 +430,7 @@ __device__ __forceinline__ void store_result(uint32_t tcol, int q, int cs, float
     for (int sub = 0; sub < 2; ++sub) {
       const int row = 32 * q + 16 * hf + 8 * sub + (t >> 2);
       if (row < nvalid) {
-        float* rp = row0 + (int64_t)row * row_stride + cs * C + 2 * (t & 3);
+        PT* rp = row0 + (int64_t)row * row_stride + cs * C + 2 * (t & 3);
 #pragma unroll
         for (int j = 0; j < J; ++j) {
           float2 v = make_float2(__uint_as_float(r[hf][j][0][2 * sub]),
@@ -385,7 +439,7 @@ __device__ __forceinline__ void store_result(uint32_t tcol, int q, int cs, float
           for (int g = 1; g < NG; ++g)
             v = __fadd2_rn(v, make_float2(__uint_as_float(r[hf][j][g][2 * sub]),
                                           __uint_as_float(r[hf][j][g][2 * sub + 1])));
-          *(float2*)(rp + 8 * j) = v;
+          store2(rp + 8 * j, v);
         }
       }
     }
@@ -795,10 +849,11 @@ __device__ __forceinline__ Span span_of(const TcParams& p, int b) {
   return Span{a, 0, (int)n, (int)((n + kTile - 1) / kTile)};
 }
 
-// issue the TMA loads of one tile (one or two point tensors) on bar
+// issue the TMA loads of one tile (one or two point tensors of type PT) on bar
+template <typename PT>
 __device__ __forceinline__ void tma_tile(const TcParams& p, uint8_t* st0, uint8_t* st1, int h,
                                          const Span& sp, int tile, uint64_t* bar) {
-  mbar_arrive_expect_tx(bar, st1 ? 2 * kStage : kStage);
+  mbar_arrive_expect_tx(bar, st1 ? 2 * stage_bytes<PT>() : stage_bytes<PT>());
   tma_load_4d(st0, &p.mx, 0, h, sp.row(tile), sp.bc, bar);
   if (st1) tma_load_4d(st1, &p.mv, 0, h, sp.row(tile), sp.bc, bar);
 }
@@ -810,9 +865,10 @@ __device__ __forceinline__ void tma_tile(const TcParams& p, uint8_t* st0, uint8_
 // generic-proxy shared loads still in flight before the TMA's async-proxy
 // writes, and with two CTAs per SM such loads were seen returning the next
 // tile's bytes.
+template <typename PT>
 __device__ __forceinline__ void prefetch(const TcParams& p, uint8_t* st0, uint8_t* st1, int h,
                                          const Span& sp, int tile, uint64_t* bar) {
-  if (tile + p.P < sp.ntiles) tma_tile(p, st0, st1, h, sp, tile + p.P, bar);
+  if (tile + p.P < sp.ntiles) tma_tile<PT>(p, st0, st1, h, sp, tile + p.P, bar);
 }
 
 // Per-kernel threads per point row, co-resident CTAs per SM (shared memory,
@@ -865,6 +921,7 @@ constexpr int kSfStageX = 0, kSfWS = kStage, kSfF = kSfWS + kSplit, kSfWs = kSfF
               kSfBar = kSfRed + red_bytes(kTSliceFwd, 2), kSfBytes = kSfBar + kBarBytes;
 static_assert(kSfF % 1024 == 0 && kSplit % 1024 == 0, "fx staging tiles need 1 KB alignment");
 
+template <typename PT>
 __global__ void __launch_bounds__(128 * kTSliceFwd, kCtasSliceFwd)
     k_tc_slice_fwd(const __grid_constant__ TcParams p) {
   constexpr int T = kTSliceFwd, NT = Th<T>::NT, C = Th<T>::C;
@@ -889,23 +946,23 @@ __global__ void __launch_bounds__(128 * kTSliceFwd, kCtasSliceFwd)
   // split one tile's rows (x into TMEM, fx from its staging in F[buf] into F[buf])
   auto split_tile = [&](int buf) {
     wait_bar(c, kBarTma, p.status);
-    float x[C], f[C];
-    read_cols<C>(stX, th.row, th.cs, x);
-    read_cols<C>(fbuf(buf), th.row, th.cs, f);
+    RowVals<C, PT> x, f;
+    x.load(stX, th.row, th.cs);
+    f.load(fbuf(buf), th.row, th.cs);
     __syncthreads();  // every staged fx row is in registers before F[buf] is overwritten
-    Split<C>(x).to_tmem(tX + th.lane_off, th.cs);
-    Split<C>(f).to_smem(fbuf(buf), th.row, th.cs);
+    x.split().to_tmem(tX + th.lane_off, th.cs);
+    f.split().to_smem(fbuf(buf), th.row, th.cs);
     tst_wait();
   };
   int tile = blockIdx.x, buf = 0;
   // (a CTA of a sample with fewer tiles than CTAs has none: it writes zero
   // partials; the condition is the same for every thread)
   if (tile < sp.ntiles) {
-    if (threadIdx.x == 0) tma_tile(p, stX, fbuf(0), h, sp, tile, c.bar);
+    if (threadIdx.x == 0) tma_tile<PT>(p, stX, fbuf(0), h, sp, tile, c.bar);
     split_tile(0);
     to_async_barrier();
     if (threadIdx.x == 0) {
-      prefetch(p, stX, fbuf(1), h, sp, tile, c.bar);  // F[1] is unused yet
+      prefetch<PT>(p, stX, fbuf(1), h, sp, tile, c.bar);  // F[1] is unused yet
       wide_ts<96, false>(tL, tX, dWs);  // logits = x W^T
       commit(c, kG1);
     }
@@ -933,7 +990,7 @@ __global__ void __launch_bounds__(128 * kTSliceFwd, kCtasSliceFwd)
       to_async_barrier();
       if (threadIdx.x == 0) {
         if (more2) {  // tile i+2: its x now, its fx once tile i's pool is done with F[buf]
-          mbar_arrive_expect_tx(c.bar + kBarTma, 2 * kStage);
+          mbar_arrive_expect_tx(c.bar + kBarTma, 2 * stage_bytes<PT>());
           tma_load_4d(stX, &p.mx, 0, h, sp.row(tile + 2 * p.P), sp.bc, c.bar + kBarTma);
         }
         wide_ts<96, false>(tL, tX, dWs);
@@ -962,6 +1019,7 @@ constexpr int kDfStageX = 0, kDfWs = kStage, kDfTs = kDfWs + kSmall,
               kDfBias = kDfTs + kSmall, kDfRed = kDfBias + 128,
               kDfBar = kDfRed + red_bytes(kTDesliceFwd, 2), kDfBytes = kDfBar + kBarBytes;
 
+template <typename PT>
 __global__ void __launch_bounds__(128 * kTDesliceFwd, kCtasDesliceFwd)
     k_tc_deslice_fwd(const __grid_constant__ TcParams p) {
   constexpr int T = kTDesliceFwd, NT = Th<T>::NT, C = Th<T>::C;
@@ -984,19 +1042,19 @@ __global__ void __launch_bounds__(128 * kTDesliceFwd, kCtasDesliceFwd)
   const uint64_t dWs = desc_smallK(sm + kDfWs);
   const uint64_t dTs = kNwDf == 32 ? desc_smallM(sm + kDfTs) : desc_stacked(sm + kDfTs);
   int tile = blockIdx.x;
-  if (threadIdx.x == 0 && tile < sp.ntiles) tma_tile(p, sm + kDfStageX, nullptr, h, sp, tile, c.bar);
+  if (threadIdx.x == 0 && tile < sp.ntiles) tma_tile<PT>(p, sm + kDfStageX, nullptr, h, sp, tile, c.bar);
   for (; tile < sp.ntiles; tile += p.P) {
     const int n0 = tile * kTile;
     wait_bar(c, kBarTma, p.status);
     {
-      float x[C];
-      read_cols<C>(sm + kDfStageX, th.row, th.cs, x);
-      Split<C>(x).to_tmem(tA + th.lane_off, th.cs);
+      RowVals<C, PT> x;
+      x.load(sm + kDfStageX, th.row, th.cs);
+      x.split().to_tmem(tA + th.lane_off, th.cs);
       tst_wait();
     }
     to_async_barrier();
     if (threadIdx.x == 0) {
-      prefetch(p, sm + kDfStageX, nullptr, h, sp, tile, c.bar);
+      prefetch<PT>(p, sm + kDfStageX, nullptr, h, sp, tile, c.bar);
       wide_ts<kNwDf, false>(tL, tA, dWs);  // logits = x W^T
       commit(c, kG1);
     }
@@ -1015,7 +1073,7 @@ __global__ void __launch_bounds__(128 * kTDesliceFwd, kCtasDesliceFwd)
     }
     wait_bar(c, kG2, p.status);
     store_result<kNwDf, C>(tL, th.q, th.cs,
-                           p.out + (int64_t)sp.bc * p.so[0] + (sp.n0 + n0) * p.so[1] +
+                           (PT*)p.out + (int64_t)sp.bc * p.so[0] + (sp.n0 + n0) * p.so[1] +
                                (int64_t)h * p.so[2],
                            p.so[1], sp.N - n0);
   }
@@ -1035,6 +1093,7 @@ constexpr int kSbStageX = 0, kSbStageF = kStage, kSbX = 2 * kStage, kSbUp = kSbX
               kSbDs = kSbBias + 128, kSbRed = kSbDs + 128,
               kSbBar = kSbRed + red_bytes(kTSliceBwd, 3), kSbBytes = kSbBar + kBarBytes;
 
+template <typename PT>
 __global__ void __launch_bounds__(128 * kTSliceBwd, kCtasSliceBwd)
     k_tc_slice_bwd(const __grid_constant__ TcParams p) {
   constexpr int T = kTSliceBwd, NT = Th<T>::NT, C = Th<T>::C;
@@ -1064,24 +1123,24 @@ __global__ void __launch_bounds__(128 * kTSliceBwd, kCtasSliceBwd)
   for (int i = 0; i < C; ++i) accw[i] = accb[i] = 0.f;
   int tile = blockIdx.x;
   if (threadIdx.x == 0 && tile < sp.ntiles)
-    tma_tile(p, sm + kSbStageX, sm + kSbStageF, h, sp, tile, c.bar);
+    tma_tile<PT>(p, sm + kSbStageX, sm + kSbStageF, h, sp, tile, c.bar);
   for (; tile < sp.ntiles; tile += p.P) {
     const int n0 = tile * kTile;
     const bool valid = n0 + th.row < sp.N;
     wait_bar(c, kBarTma, p.status);
     {
-      float x[C], f[C];
-      read_cols<C>(sm + kSbStageX, th.row, th.cs, x);
-      read_cols<C>(sm + kSbStageF, th.row, th.cs, f);
-      const Split<C> xs(x);
+      RowVals<C, PT> x, f;
+      x.load(sm + kSbStageX, th.row, th.cs);
+      f.load(sm + kSbStageF, th.row, th.cs);
+      const Split<C> xs = x.split();
       xs.to_smem(sm + kSbX, th.row, th.cs);
       xs.to_tmem(tX + th.lane_off, th.cs);
-      Split<C>(f).to_tmem(tF + th.lane_off, th.cs);
+      f.split().to_tmem(tF + th.lane_off, th.cs);
       tst_wait();
     }
     to_async_barrier();
     if (threadIdx.x == 0) {
-      prefetch(p, sm + kSbStageX, sm + kSbStageF, h, sp, tile, c.bar);
+      prefetch<PT>(p, sm + kSbStageX, sm + kSbStageF, h, sp, tile, c.bar);
       wide_ts<96, false>(tL, tX, dWk);  // logits = x W^T
       commit(c, kG1);
       wide_ts<64, false>(tDw, tF, dZk);  // dw = fx dz_num^T
@@ -1116,11 +1175,11 @@ __global__ void __launch_bounds__(128 * kTSliceBwd, kCtasSliceBwd)
     }
     wait_bar(c, kG3, p.status);
     store_result<32, C>(tDfx, th.q, th.cs,
-                        p.out2 + (int64_t)sp.bc * p.so2[0] + (sp.n0 + n0) * p.so2[1] +
+                        (PT*)p.out2 + (int64_t)sp.bc * p.so2[0] + (sp.n0 + n0) * p.so2[1] +
                             (int64_t)h * p.so2[2],
                         p.so2[1], sp.N - n0);
     store_result<32, C>(tDx, th.q, th.cs,
-                        p.out + (int64_t)sp.bc * p.so[0] + (sp.n0 + n0) * p.so[1] +
+                        (PT*)p.out + (int64_t)sp.bc * p.so[0] + (sp.n0 + n0) * p.so[1] +
                             (int64_t)h * p.so[2],
                         p.so[1], sp.N - n0);
     wait_bar(c, kG4, p.status);
@@ -1151,6 +1210,7 @@ constexpr int kDbX = 0, kDbO = kSplit, kDbWp = 2 * kSplit, kDbUp = 3 * kSplit,
               kDbBytes = kDbBar + kBarBytes;
 static_assert(kDbWp % 1024 == 0 && kDbUp % 1024 == 0, "staging tiles need 1 KB alignment");
 
+template <typename PT>
 __global__ void __launch_bounds__(128 * kTDesliceBwd, kCtasDesliceBwd)
     k_tc_deslice_bwd(const __grid_constant__ TcParams p) {
   constexpr int T = kTDesliceBwd, NT = Th<T>::NT, C = Th<T>::C;
@@ -1179,20 +1239,20 @@ __global__ void __launch_bounds__(128 * kTDesliceBwd, kCtasDesliceBwd)
 #pragma unroll
   for (int i = 0; i < C; ++i) acct[i] = accw[i] = accb[i] = 0.f;
   int tile = blockIdx.x;
-  if (threadIdx.x == 0 && tile < sp.ntiles) tma_tile(p, stX, stO, h, sp, tile, c.bar);
+  if (threadIdx.x == 0 && tile < sp.ntiles) tma_tile<PT>(p, stX, stO, h, sp, tile, c.bar);
   for (; tile < sp.ntiles; tile += p.P) {
     const int n0 = tile * kTile;
     const bool valid = n0 + th.row < sp.N;
     const bool more = tile + p.P < sp.ntiles;
     wait_bar(c, kBarTma, p.status);
     {
-      float x[C], o[C];
-      read_cols<C>(stX, th.row, th.cs, x);
-      read_cols<C>(stO, th.row, th.cs, o);
-      const Split<C> xs(x);
+      RowVals<C, PT> x, o;
+      x.load(stX, th.row, th.cs);
+      o.load(stO, th.row, th.cs);
+      const Split<C> xs = x.split();
       xs.to_smem(sm + kDbX, th.row, th.cs);
       xs.to_tmem(tX + th.lane_off, th.cs);
-      const Split<C> os(o);
+      const Split<C> os = o.split();
       os.to_smem(sm + kDbO, th.row, th.cs);
       os.to_tmem(tO + th.lane_off, th.cs);
       tst_wait();
@@ -1229,7 +1289,7 @@ __global__ void __launch_bounds__(128 * kTDesliceBwd, kCtasDesliceBwd)
     }
     wait_bar(c, kG3, p.status);
     store_result<32, C>(tDx, th.q, th.cs,
-                        p.out + (int64_t)sp.bc * p.so[0] + (sp.n0 + n0) * p.so[1] +
+                        (PT*)p.out + (int64_t)sp.bc * p.so[0] + (sp.n0 + n0) * p.so[1] +
                             (int64_t)h * p.so[2],
                         p.so[1], sp.N - n0);
     wait_bar(c, kG4, p.status);
@@ -1239,7 +1299,7 @@ __global__ void __launch_bounds__(128 * kTDesliceBwd, kCtasDesliceBwd)
     tc_fence_after();
     if (threadIdx.x == 0) {
       if (more) {
-        mbar_arrive_expect_tx(c.bar + kBarTma, 2 * kStage);
+        mbar_arrive_expect_tx(c.bar + kBarTma, 2 * stage_bytes<PT>());
         tma_load_4d(stX, &p.mx, 0, h, sp.row(tile + p.P), sp.bc, c.bar + kBarTma);
       }
       mma_pool(tP, dUp, dXb);  // dW += (dl/tau)^T x
@@ -1292,6 +1352,7 @@ constexpr int kCbStageX = 0, kCbStageF = kStage, kCbX = 2 * kStage, kCbUp = kCbX
               kCbBar = kCbRed + red_bytes(kTCoupledBwd, 3), kCbBytes = kCbBar + kBarBytes;
 static_assert(kCbUp % 1024 == 0, "the d_out staging tile needs 1 KB alignment");
 
+template <typename PT>
 __global__ void __launch_bounds__(128 * kTCoupledBwd, kCtasCoupledBwd)
     k_tc_coupled_bwd(const __grid_constant__ TcParams p) {
   constexpr int T = kTCoupledBwd, NT = Th<T>::NT, C = Th<T>::C;
@@ -1327,7 +1388,7 @@ __global__ void __launch_bounds__(128 * kTCoupledBwd, kCtasCoupledBwd)
   for (int i = 0; i < C; ++i) accw[i] = accb[i] = 0.f;
   int tile = blockIdx.x;
   if (threadIdx.x == 0 && tile < sp.ntiles) {
-    mbar_arrive_expect_tx(c.bar + kBarTma, 3 * kStage);
+    mbar_arrive_expect_tx(c.bar + kBarTma, 3 * stage_bytes<PT>());
     tma_load_4d(stX, &p.mx, 0, h, sp.row(tile), sp.bc, c.bar + kBarTma);
     tma_load_4d(stF, &p.mv, 0, h, sp.row(tile), sp.bc, c.bar + kBarTma);
     tma_load_4d(stO, &p.mo, 0, h, sp.row(tile), sp.bc, c.bar + kBarTma);
@@ -1338,19 +1399,19 @@ __global__ void __launch_bounds__(128 * kTCoupledBwd, kCtasCoupledBwd)
     const bool more = tile + p.P < sp.ntiles;
     wait_bar(c, kBarTma, p.status);
     {
-      float x[C], f[C], o[C];
-      read_cols<C>(stX, th.row, th.cs, x);
-      read_cols<C>(stF, th.row, th.cs, f);
-      read_cols<C>(stO, th.row, th.cs, o);
-      Split<C>(x).to_smem(sm + kCbX, th.row, th.cs);
-      Split<C>(f).to_tmem(tF + th.lane_off, th.cs);
-      Split<C>(o).to_tmem(tO + th.lane_off, th.cs);
+      RowVals<C, PT> x, f, o;
+      x.load(stX, th.row, th.cs);
+      f.load(stF, th.row, th.cs);
+      o.load(stO, th.row, th.cs);
+      x.split().to_smem(sm + kCbX, th.row, th.cs);
+      f.split().to_tmem(tF + th.lane_off, th.cs);
+      o.split().to_tmem(tO + th.lane_off, th.cs);
       tst_wait();
     }
     to_async_barrier();
     if (threadIdx.x == 0) {
       if (more) {  // x and fx of the next tile; its d_out once UP is free
-        mbar_arrive_expect_tx(c.bar + kBarTma, 3 * kStage);
+        mbar_arrive_expect_tx(c.bar + kBarTma, 3 * stage_bytes<PT>());
         tma_load_4d(stX, &p.mx, 0, h, sp.row(tile + p.P), sp.bc, c.bar + kBarTma);
         tma_load_4d(stF, &p.mv, 0, h, sp.row(tile + p.P), sp.bc, c.bar + kBarTma);
       }
@@ -1392,11 +1453,11 @@ __global__ void __launch_bounds__(128 * kTCoupledBwd, kCtasCoupledBwd)
     if (th.q < 3) drain_pool<C>(tP + th.lane_off, th.cs, accw);
     wait_bar(c, kG4, p.status);
     store_result<32, C>(tDfx, th.q, th.cs,
-                        p.out2 + (int64_t)sp.bc * p.so2[0] + (sp.n0 + n0) * p.so2[1] +
+                        (PT*)p.out2 + (int64_t)sp.bc * p.so2[0] + (sp.n0 + n0) * p.so2[1] +
                             (int64_t)h * p.so2[2],
                         p.so2[1], sp.N - n0);
     store_result<32, C>(tDx, th.q, th.cs,
-                        p.out + (int64_t)sp.bc * p.so[0] + (sp.n0 + n0) * p.so[1] +
+                        (PT*)p.out + (int64_t)sp.bc * p.so[0] + (sp.n0 + n0) * p.so[1] +
                             (int64_t)h * p.so[2],
                         p.so[1], sp.N - n0);
   }
@@ -1440,7 +1501,7 @@ int* device_status() {
 }
 
 bool make_point_map(CUtensorMap* map, const void* data, int64_t B, int64_t N, int64_t H,
-                    const int64_t stride[4]) {
+                    const int64_t stride[4], int pdt) {
   static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
   if (!encode) {
     void* fn = nullptr;
@@ -1451,9 +1512,10 @@ bool make_point_map(CUtensorMap* map, const void* data, int64_t B, int64_t N, in
       return false;
     encode = (PFN_cuTensorMapEncodeTiled_v12000)fn;
   }
+  const int64_t es = pdt == 1 ? 2 : 4;
   if (stride[3] != 1 || ((uintptr_t)data & 15)) return false;
   for (int i = 0; i < 3; ++i)
-    if (stride[i] <= 0 || (stride[i] * 4) % 16 || stride[i] * 4 >= ((int64_t)1 << 40))
+    if (stride[i] <= 0 || (stride[i] * es) % 16 || stride[i] * es >= ((int64_t)1 << 40))
       return false;
   // The encoder is a driver call and needs a current context on this thread;
   // a thread that has made no runtime call yet (an autograd worker on its
@@ -1462,17 +1524,21 @@ bool make_point_map(CUtensorMap* map, const void* data, int64_t B, int64_t N, in
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || cudaSetDevice(dev) != cudaSuccess) return false;
   cuuint64_t dims[4] = {32, (cuuint64_t)H, (cuuint64_t)N, (cuuint64_t)B};
-  cuuint64_t gstr[3] = {(cuuint64_t)(stride[2] * 4), (cuuint64_t)(stride[1] * 4),
-                        (cuuint64_t)(stride[0] * 4)};
+  cuuint64_t gstr[3] = {(cuuint64_t)(stride[2] * es), (cuuint64_t)(stride[1] * es),
+                        (cuuint64_t)(stride[0] * es)};
   cuuint32_t box[4] = {32, 1, kTile, 1};
-  cuuint32_t es[4] = {1, 1, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
   // the encoder wants a 64-byte aligned map; do not rely on the caller's stack
   unsigned char raw[sizeof(CUtensorMap) + 64];
   CUtensorMap* aligned = (CUtensorMap*)(((uintptr_t)raw + 63) & ~(uintptr_t)63);
-  const CUresult r = encode(aligned, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<void*>(data),
-                            dims, gstr, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  // fp32 rows are 128 bytes (128B swizzle), bf16 rows 64 bytes (64B swizzle)
+  const CUresult r = encode(aligned,
+                            pdt == 1 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                     : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                            4, const_cast<void*>(data), dims, gstr, box, estr,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE,
+                            pdt == 1 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return false;
   std::memcpy(map, aligned, sizeof(CUtensorMap));
   return true;
@@ -1497,22 +1563,23 @@ static cudaError_t launch_tc(K kernel, int T, int bytes, const TcParams& p, cuda
   return cudaSuccess;
 }
 
-cudaError_t run_tc(TcKind k, const TcParams& p, cudaStream_t s) {
-  cudaError_t e = cudaSuccess;
+template <typename PT>
+static cudaError_t run_tc_t(TcKind k, const TcParams& p, cudaStream_t s) {
   switch (k) {
-    case TcKind::SliceFwd: e = launch_tc(k_tc_slice_fwd, kTSliceFwd, kSfBytes, p, s); break;
+    case TcKind::SliceFwd: return launch_tc(k_tc_slice_fwd<PT>, kTSliceFwd, kSfBytes, p, s);
     case TcKind::DesliceFwd:
-      e = launch_tc(k_tc_deslice_fwd, kTDesliceFwd, kDfBytes, p, s);
-      break;
-    case TcKind::SliceBwd: e = launch_tc(k_tc_slice_bwd, kTSliceBwd, kSbBytes, p, s); break;
+      return launch_tc(k_tc_deslice_fwd<PT>, kTDesliceFwd, kDfBytes, p, s);
+    case TcKind::SliceBwd: return launch_tc(k_tc_slice_bwd<PT>, kTSliceBwd, kSbBytes, p, s);
     case TcKind::DesliceBwd:
-      e = launch_tc(k_tc_deslice_bwd, kTDesliceBwd, kDbBytes, p, s);
-      break;
+      return launch_tc(k_tc_deslice_bwd<PT>, kTDesliceBwd, kDbBytes, p, s);
     case TcKind::CoupledBwd:
-      e = launch_tc(k_tc_coupled_bwd, kTCoupledBwd, kCbBytes, p, s);
-      break;
-    default: return cudaErrorInvalidValue;
+      return launch_tc(k_tc_coupled_bwd<PT>, kTCoupledBwd, kCbBytes, p, s);
   }
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t run_tc(TcKind k, const TcParams& p, cudaStream_t s) {
+  const cudaError_t e = p.pdt == 1 ? run_tc_t<__nv_bfloat16>(k, p, s) : run_tc_t<float>(k, p, s);
   if (e != cudaSuccess) return e;
   g_launches.fetch_add(1, std::memory_order_relaxed);
   g_tc_launches.fetch_add(1, std::memory_order_relaxed);

@@ -20,6 +20,7 @@ struct TcParams {
   CUtensorMap mv;  // fx_mid or d_out, same shape
   CUtensorMap mo;  // d_out of the coupled backward (mv is fx_mid there)
   int B, N, H, P, ntiles;
+  int pdt;  // point tensors' type: 0 fp32, 1 bf16 (tiles, outputs)
   const float* W;
   const float* bias;
   const float* tau;
@@ -27,9 +28,9 @@ struct TcParams {
   const float* M;   // tokens or dz_num (B, H, 32, 32)
   const float* M2;  // dz_num of the coupled backward (M is tokens there)
   const float* ds;  // (B, H, 32)
-  float* out;       // deslice out / dx_mid (B, N, H, 32), element strides so
+  void* out;        // deslice out / dx_mid (B, N, H, 32), element strides so
   int64_t so[4];
-  float* out2;      // dfx_mid
+  void* out2;       // dfx_mid
   int64_t so2[4];
   float* partA;
   float* partB;
@@ -56,7 +57,7 @@ int tc_ctas_per_sm(TcKind k);
 // (width stride != 1, unaligned base or strides) or the driver entry point is
 // missing.
 bool make_point_map(CUtensorMap* map, const void* data, int64_t B, int64_t N, int64_t H,
-                    const int64_t stride[4]);
+                    const int64_t stride[4], int pdt = 0);
 
 // Address of this library's device status word on the current device.
 int* device_status();

@@ -394,11 +394,11 @@ def native_deslice_bwd(x_mid, weight, bias, tau, tokens, stats, d_out, dot, fami
 def _coupled_call(x_mid, fx_mid, weight, bias, tau, dot):
     """The native problem of a coupled backward, or None when the coupled
     kernel does not serve these inputs (shape, dtype, engine, layout)."""
-    if fx_mid.shape[3] != x_mid.shape[3] or x_mid.dtype != torch.float32 or \
-            fx_mid.dtype != torch.float32 or not x_mid.is_cuda:
+    if fx_mid.shape[3] != x_mid.shape[3] or x_mid.dtype not in (torch.float32, torch.bfloat16) \
+            or fx_mid.dtype != x_mid.dtype or not x_mid.is_cuda:
         return None
     c = _Call(x_mid, fx_mid.shape[3], weight, bias, tau, dot, nat.FAMILY_SINGLE, 0,
-              torch.float32)
+              x_mid.dtype)
     return c if nat.load().fs_coupled_supported(ctypes.byref(c.prob)) else None
 
 
@@ -411,7 +411,7 @@ def native_coupled_bwd(x_mid, fx_mid, d_out, weight, bias, tau, tokens, dz_num, 
     if N == 0:
         return None
     c = _coupled_call(x_mid, fx_mid, weight, bias, tau, dot)
-    if c is None or d_out.dtype != torch.float32:
+    if c is None or d_out.dtype != x_mid.dtype:
         return None
     dev = x_mid.device
     dxm = torch.empty_like(x_mid)
@@ -593,7 +593,8 @@ torch.library.register_autograd("flashslice::flash_deslice", _deslice_grad,
 def _tc_strides(t):
     """t, or a contiguous copy when its layout is not one the tensor-core
     kernels read (unit width stride, 16-byte aligned strides and base)."""
-    ok = t.stride(3) == 1 and all(st % 4 == 0 for st in t.stride()[:3]) and \
+    per16 = 16 // t.element_size()
+    ok = t.stride(3) == 1 and all(st % per16 == 0 for st in t.stride()[:3]) and \
         t.data_ptr() % 16 == 0
     return t if ok else t.contiguous()
 
