@@ -46,6 +46,9 @@ CONFIGS = {
     # configs[1] of the baseline: per-GPU shard of 2^20 points (weak scaling)
     "cfg2": dict(B=1, N=1 << 20, H=8, D=32, DV=32, G=32, weight="hgd", tau="uniform",
                  dtype=torch.float32, dot="ieee", split=False),
+    # config 2's shape with bf16 point tensors (a bf16 layer's x_mid / fx_mid)
+    "cfg2-bf16": dict(B=1, N=1 << 20, H=8, D=32, DV=32, G=32, weight="hgd", tau="uniform",
+                      dtype=torch.bfloat16, dot="bf16", split=False),
     "cfg1": dict(B=1, N=16384, H=8, D=32, DV=32, G=32, weight="gd", tau="half",
                  dtype=torch.float32, dot="ieee", split=False),
     "cfg3": dict(B=2, N=262144, H=8, D=32, DV=64, G=1024, weight="bhgd", tau="half",
