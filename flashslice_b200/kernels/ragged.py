@@ -13,8 +13,8 @@ contract per sample:
   ``z_num`` ``(S, H, G, DV)`` and ``s`` ``(S, H, G)`` are per sample;
 * every result equals the dense op applied to each sample alone.
 
-The tensor-core engine serves them in one launch per op (fp32, D = DV = G =
-32, at most ``FS_MAX_SPLITS`` samples): each (sample, head) gets its CTAs and
+The tensor-core engine serves them in one launch per op (fp32 or bf16 point
+tensors, D = DV = G = 32, at most ``FS_MAX_SPLITS`` samples): each (sample, head) gets its CTAs and
 masks the rows past its sample. Other problems run the dense ops sample by
 sample (still native, one launch per sample)."""
 
@@ -81,7 +81,7 @@ class _Native:
         Bw, Hw, Bb, Hb = _extents(weight, bias, S, H)
         self.w, self.b, self.tau = _f32(weight), _f32(bias), _f32(tau)
         self.splits = splits  # the ABI reads the host array during the call
-        self.prob = nat.Problem(S, N, H, D, dv, self.G, nat.DTYPE_CODE[torch.float32], int(dot),
+        self.prob = nat.Problem(S, N, H, D, dv, self.G, nat.DTYPE_CODE[x_mid.dtype], int(dot),
                                 nat.FAMILY_SINGLE, 0, Bw, Hw, Bb, Hb, 0,
                                 nat.ENGINES[_state.engine], ctypes.c_void_p(splits.data_ptr()))
         self.device = x_mid.device
@@ -89,7 +89,8 @@ class _Native:
     @staticmethod
     def make(x_mid, dv, weight, bias, tau, dot, splits):
         S = splits.numel() - 1
-        if (x_mid.dtype != torch.float32 or S > MAX_SPLITS or x_mid.shape[1] == 0 or
+        if (x_mid.dtype not in (torch.float32, torch.bfloat16) or S > MAX_SPLITS or
+                x_mid.shape[1] == 0 or
                 x_mid.shape[3] != 32 or dv != 32 or weight.shape[-2] != 32 or not x_mid.is_cuda):
             return None
         c = _Native(x_mid, dv, weight, bias, tau, dot, splits)
@@ -102,7 +103,7 @@ class _Native:
 def native_slice(x_mid, fx_mid, weight, bias, tau, splits, dot=0):
     """(z_num (S, H, G, DV), s (S, H, G)) in one launch, or None."""
     c = _Native.make(x_mid, fx_mid.shape[3], weight, bias, tau, dot, splits)
-    if c is None or fx_mid.dtype != torch.float32:
+    if c is None or fx_mid.dtype != x_mid.dtype:
         return None
     x_mid, fx_mid = _tc_strides(x_mid), _tc_strides(fx_mid)
     z = torch.empty(c.S, c.H, c.G, c.DV, device=c.device, dtype=torch.float32)
@@ -121,7 +122,7 @@ def native_deslice(x_mid, weight, bias, tau, tokens, splits, dot=0):
     if c is None:
         return None
     x_mid = _tc_strides(x_mid)
-    out = torch.empty(1, c.N, c.H, c.DV, device=c.device, dtype=torch.float32)
+    out = torch.empty(1, c.N, c.H, c.DV, device=c.device, dtype=x_mid.dtype)
     tok = _f32(tokens)
     ws, nws = c.workspace(nat.OP_DESLICE_FWD)
     with torch.cuda.device(c.device):
@@ -156,7 +157,7 @@ def native_slice_bwd(x_mid, fx_mid, weight, bias, tau, dz_num, ds, splits, dot=0
 
 def native_deslice_bwd(x_mid, weight, bias, tau, tokens, d_out, splits, dot=0):
     c = _Native.make(x_mid, tokens.shape[3], weight, bias, tau, dot, splits)
-    x_mid, d_out = _tc_strides(x_mid), _tc_strides(d_out.float())
+    x_mid, d_out = _tc_strides(x_mid), _tc_strides(d_out.to(x_mid.dtype))
     dx = torch.empty_like(x_mid)
     dtok = torch.empty(c.S, c.H, c.G, c.DV, device=c.device, dtype=torch.float32)
     dW, db, dt = _param_bufs(c, weight, bias)
@@ -172,7 +173,8 @@ def native_deslice_bwd(x_mid, weight, bias, tau, tokens, d_out, splits, dot=0):
 def native_coupled_bwd(x_mid, fx_mid, d_out, weight, bias, tau, tokens, dz_num, ds, splits,
                        dot=0):
     c = _Native.make(x_mid, fx_mid.shape[3], weight, bias, tau, dot, splits)
-    x_mid, fx_mid, d_out = _tc_strides(x_mid), _tc_strides(fx_mid), _tc_strides(d_out.float())
+    x_mid, fx_mid = _tc_strides(x_mid), _tc_strides(fx_mid)
+    d_out = _tc_strides(d_out.to(x_mid.dtype))
     dx, dfx = torch.empty_like(x_mid), torch.empty_like(fx_mid)
     dW, db, dt = _param_bufs(c, weight, bias)
     ws, nws = c.workspace(nat.OP_SLICE_BWD)
@@ -248,7 +250,7 @@ def ragged_slice(x_mid, fx_mid, weight, bias, tau, row_splits):
     splits = _splits(row_splits, x_mid.shape[1])
     weight, bias, G = _prep(x_mid, weight, bias, splits)
     if _Native.make(x_mid, fx_mid.shape[3], weight, bias, tau, 0, splits) is not None and \
-            fx_mid.dtype == torch.float32:
+            fx_mid.dtype == x_mid.dtype:
         return _RaggedSlice.apply(x_mid, fx_mid, weight, bias, tau, splits)
     S = splits.numel() - 1
     parts = [fused_slice(_rows(x_mid, splits, b), _rows(fx_mid, splits, b),
@@ -284,7 +286,7 @@ def ragged_coupling(x_mid, fx_mid, weight, bias, tau, row_splits, mix=None, mix_
         mix_params = [q for q in mix.parameters()] if isinstance(mix, torch.nn.Module) else []
     params = tuple(q for q in mix_params if q.requires_grad)
     if _Native.make(x_mid, fx_mid.shape[3], weight, bias, tau, 0, splits) is not None and \
-            fx_mid.dtype == torch.float32:
+            fx_mid.dtype == x_mid.dtype:
         return _CouplingRound.apply(x_mid, fx_mid, weight, bias, tau, eps, 0, mix, None,
                                     _RaggedOps(splits), *params)
     S = splits.numel() - 1

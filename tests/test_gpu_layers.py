@@ -52,6 +52,37 @@ def test_layer_fused_matches_eager(cuda_device, kw):
         assert ef <= max(2.0 * ee, 1e-5), (k, ef, ee)
 
 
+def test_layer_bf16_autocast_on_tensor_cores(cuda_device):
+    """The layer under bf16 autocast: its projections hand bf16 x_mid / fx_mid
+    to the coupling round, which runs on the tensor cores; output and
+    gradients against the float64 layer within the reference's bf16 gate
+    (2e-2), as close as the eager path under the same autocast."""
+    torch.backends.cuda.matmul.allow_tf32 = False
+    from flashslice_b200 import Physics_Attention_Irregular_Mesh
+    from flashslice_b200.kernels import _native as nat
+    torch.manual_seed(5)
+    kw = dict(heads=8, dim_head=32, slice_num=32)
+    eager = Physics_Attention_Irregular_Mesh(256, **kw)
+    fused = Physics_Attention_Irregular_Mesh(256, use_fused_slice=True, **kw)
+    fused.load_state_dict(eager.state_dict())
+    truth = Physics_Attention_Irregular_Mesh(256, **kw)
+    truth.load_state_dict(eager.state_dict())
+    g = torch.Generator().manual_seed(6)
+    x = torch.randn(1, 8000, 256, generator=g)
+    up = torch.randn(1, 8000, 256, generator=g)
+    lib = nat.load()
+    n0 = lib.fs_tc_launch_count()
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        rf = _layer_run(fused.cuda(), x.cuda(), up.cuda())
+    assert lib.fs_tc_launch_count() - n0 == 4
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        re = _layer_run(eager.cuda(), x.cuda(), up.cuda())
+    rt = _layer_run(truth.double().cuda(), x.double().cuda(), up.double().cuda())
+    for k in rt:
+        ef, ee = relerr(rf[k].double(), rt[k]), relerr(re[k].double(), rt[k])
+        assert ef <= max(1.25 * ee, 2e-2), (k, ef, ee)
+
+
 def test_transolver_fused_trains(cuda_device):
     """A few optimiser steps of a small Transolver on the fused path track the
     eager model step for step."""

@@ -127,3 +127,25 @@ def test_ragged_with_mix_and_fallback(env):
         assert relerr(out, ref) <= 1e-5, (D, relerr(out, ref))
         for a, e in zip(leaves + [M], ref_leaves + [Md]):
             assert relerr(a.grad, e.grad) <= 5e-5, (D, relerr(a.grad, e.grad))
+
+
+def test_ragged_coupling_bf16(env):
+    """bf16 samples in one launch per op: against the dense bf16 rounds run
+    sample by sample (the same kernels per sample)."""
+    K, R, lib = env
+    (x, fx, W, b, tau, up), splits = _inputs([333, 4000, 1], "hgd", seed=31)
+    x, fx, up = x.bfloat16(), fx.bfloat16(), up.bfloat16()
+    W, b, tau = W.float(), b.float(), tau.float()
+    L = [t.clone().requires_grad_(True) for t in (x, fx, W, b, tau)]
+    n0 = lib.fs_tc_launch_count()
+    out = R.ragged_coupling(*L, splits)
+    (out.float() * up.float()).sum().backward()
+    assert lib.fs_tc_launch_count() - n0 == 4 and out.dtype == torch.bfloat16
+    D = [t.clone().requires_grad_(True) for t in (x, fx, W, b, tau)]
+    outs = [K.fused_coupling(D[0][:, a:e], D[1][:, a:e], D[2], D[3], D[4])
+            for a, e in zip(splits[:-1], splits[1:])]
+    od = torch.cat(outs, dim=1)
+    (od.float() * up.float()).sum().backward()
+    assert relerr(out, od) <= 1e-2
+    for a, e in zip(L, D):
+        assert relerr(a.grad, e.grad) <= (1e-2 if a.dtype == torch.bfloat16 else 1e-4)
