@@ -76,6 +76,9 @@ def parse():
     ap.add_argument("--config", choices=sorted(CONFIGS) + ["cfg4"], default="cfg2")
     ap.add_argument("--n", type=int, default=None, help="override the point count")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--bf16-autocast", action="store_true",
+                    help="config 4: train under torch.autocast(bfloat16) (bf16 activations, "
+                         "the coupling ops on bf16 point tensors)")
     ap.add_argument("--tf32-gemms", action="store_true",
                     help="config 4: let the model's torch GEMMs use TF32 (the coupling ops "
                          "stay exact fp32 either way)")
@@ -408,7 +411,8 @@ def run_model(args):
 
         def step():
             opt.zero_grad(set_to_none=True)
-            loss = torch.nn.functional.mse_loss(model(xs, fs), ys)
+            with torch.autocast("cuda", dtype=torch.bfloat16, enabled=bool(args.bf16_autocast)):
+                loss = torch.nn.functional.mse_loss(model(xs, fs).float(), ys)
             loss.backward()
             opt.step()
 
@@ -432,7 +436,8 @@ def run_model(args):
     line = {"metric": METRIC, "value": round(n / (ms * 1e-3) / 1e6, 3), "unit": UNIT,
             "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, U[0,1]^3 points)",
+            "vs_baseline": None, "dtype": "bf16" if args.bf16_autocast else "f32",
+            "data": "synthetic (seeded, U[0,1]^3 points)",
             "config": {"workload": "cfg4", "model": "Transolver", **MODEL4, "N": n,
                        "step": "forward + MSE backward + Adam", "l2": "activations larger "
                        "than L2, no flush", "gemms": "tf32" if args.tf32_gemms else "fp32",
