@@ -292,9 +292,20 @@ int need(const void* ptr, const char* what) {
     if (rc_ != FS_OK) return rc_; \
   } while (0)
 
-int launch_kind(Kind k, const fs_problem& p, const Setup& s, Params q, int P, cudaStream_t st) {
-  q.P = P;
+// Launch kind k with at most P programs per (b, h) (per slot block for the
+// slot-owning kinds): as many as fill the SMs' resident slots in one wave
+// (a second, partial wave would leave most SMs idle while it runs). P comes
+// back as the count used; the partials' reduction takes that count.
+int launch_kind(Kind k, const fs_problem& p, const Setup& s, Params q, int& P, cudaStream_t st) {
   q.pl = make_plan(k, (int)p.D, (int)p.DV, s.nt);
+  const bool slot_owning = k == Kind::SliceFwdG || k == Kind::SliceBwdG || k == Kind::DesliceBwdG;
+  const int64_t per = (int64_t)s.BH * (slot_owning ? s.ngb : 1);
+  const int fit = engine_resident(k, p.act_dtype, s.nt, q);
+  if (fit > 0) {
+    const int64_t want = (int64_t)fit * kSmCount / per;
+    if (want >= 1 && want < P) P = (int)want;
+  }
+  q.P = P;
   FS_TRY(run_engine(k, p.act_dtype, s.nt, q, s.ngb, st));
   return FS_OK;
 }
@@ -304,8 +315,8 @@ int run_stats(const fs_problem& p, const Setup& s, const fs_tensor4* x, const fl
   Params q = base_params(p, s, W, bias, tau);
   q.x = pt(x);
   q.stats_out = dst;
-  return launch_kind(p.stats_mode == 1 ? Kind::StatsTwoPass : Kind::StatsOnline, p, s, q, s.Pn,
-                     st);
+  int P = s.Pn;  // no partials: any count serves
+  return launch_kind(p.stats_mode == 1 ? Kind::StatsTwoPass : Kind::StatsOnline, p, s, q, P, st);
 }
 
 }  // namespace
@@ -380,9 +391,10 @@ int fs_slice_fwd_noalloc(const fs_problem* p, const fs_tensor4* x_mid, const fs_
   q.v = pt(fx_mid);
   q.partA = at(base, s.partA);
   q.partS = at(base, s.partS);
-  FS_CHECK(launch_kind(Kind::FusedSliceFwd, *p, s, q, s.Pn, st));
-  FS_TRY(run_reduce(q.partA, z_num, s.BH, 1, s.Pn, p->G * p->DV, s.BH, 1, st));
-  FS_TRY(run_reduce(q.partS, s_out, s.BH, 1, s.Pn, p->G, s.BH, 1, st));
+  int P = s.Pn;
+  FS_CHECK(launch_kind(Kind::FusedSliceFwd, *p, s, q, P, st));
+  FS_TRY(run_reduce(q.partA, z_num, s.BH, 1, P, p->G * p->DV, s.BH, 1, st));
+  FS_TRY(run_reduce(q.partS, s_out, s.BH, 1, P, p->G, s.BH, 1, st));
   return FS_OK;
 }
 
@@ -531,19 +543,20 @@ int fs_deslice_fwd(const fs_problem* p, const fs_tensor4* x_mid, const float* we
   }
   if (p->row_splits) return ragged_unsupported("deslice forward");
   route_note("deslice_fwd", s.fused ? "fma-fused" : "fma-blocked", *p, x_mid, out);
-  if (s.fused) return launch_kind(Kind::FusedDesliceFwd, *p, s, q, s.Pn, st);
+  int P = s.Pn;  // no partials: any count serves
+  if (s.fused) return launch_kind(Kind::FusedDesliceFwd, *p, s, q, P, st);
   if (stats_in) {
     q.stats_in = stats_in;
-    return launch_kind(Kind::DesliceFwdStats, *p, s, q, s.Pn, st);
+    return launch_kind(Kind::DesliceFwdStats, *p, s, q, P, st);
   }
   float* dst = s.internal_stats ? at(workspace, s.stats) : stats_out;
   if (p->stats_mode == 0) {
     q.stats_out = dst;
-    return launch_kind(Kind::DesliceFwdOnline, *p, s, q, s.Pn, st);
+    return launch_kind(Kind::DesliceFwdOnline, *p, s, q, P, st);
   }
   FS_CHECK(run_stats(*p, s, x_mid, weight, bias, tau, dst, st));
   q.stats_in = dst;
-  return launch_kind(Kind::DesliceFwdStats, *p, s, q, s.Pn, st);
+  return launch_kind(Kind::DesliceFwdStats, *p, s, q, P, st);
 }
 
 static int bwd_common(bool slice, const fs_problem* p, const fs_tensor4* x_mid,
@@ -619,6 +632,7 @@ static int bwd_common(bool slice, const fs_problem* p, const fs_tensor4* x_mid,
               (int)(!slice || tc_tensor_ok(dfx)));
     route_note(slice ? "slice_bwd" : "deslice_bwd", "fma-fused", *p, x_mid, dx);
     FS_CHECK(launch_kind(slice ? Kind::FusedSliceBwd : Kind::FusedDesliceBwd, *p, s, q, Pw, st));
+    Pdt = Pw;
   } else {
     const float* stats = stats_in;
     if (!stats) {
@@ -628,7 +642,7 @@ static int bwd_common(bool slice, const fs_problem* p, const fs_tensor4* x_mid,
     }
     q.stats_in = stats;
     q.delta = at(workspace, s.delta);
-    FS_CHECK(launch_kind(slice ? Kind::SliceBwdN : Kind::DesliceBwdN, *p, s, q, s.Pn, st));
+    FS_CHECK(launch_kind(slice ? Kind::SliceBwdN : Kind::DesliceBwdN, *p, s, q, Pdt, st));
     Pw = s.Pg;
     FS_CHECK(launch_kind(slice ? Kind::SliceBwdG : Kind::DesliceBwdG, *p, s, q, Pw, st));
   }

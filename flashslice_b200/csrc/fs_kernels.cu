@@ -621,6 +621,54 @@ static cudaError_t run_kind(Kind k, const Params& p, int nblk, cudaStream_t s) {
   return cudaErrorInvalidValue;
 }
 
+// CTAs of kind k that fit one SM at once (its shared memory, registers and
+// threads), 0 if the query fails.
+template <typename K>
+static int resident(K kernel, int nt, const Params& p) {
+  const size_t bytes = (size_t)p.pl.total * sizeof(float);
+  if (bytes > kMaxSmem ||
+      cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) !=
+          cudaSuccess ||
+      cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                           cudaSharedmemCarveoutMaxShared) != cudaSuccess)
+    return 0;
+  int n = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, nt, bytes) != cudaSuccess)
+    return 0;
+  return n;
+}
+
+template <typename T, int NT>
+static int resident_kind(Kind k, const Params& p) {
+  switch (k) {
+    case Kind::FusedSliceFwd: return resident(k_fused_slice_fwd<T, NT>, NT, p);
+    case Kind::FusedDesliceFwd: return resident(k_fused_deslice_fwd<T, NT>, NT, p);
+    case Kind::FusedSliceBwd: return resident(k_fused_slice_bwd<T, NT>, NT, p);
+    case Kind::FusedDesliceBwd: return resident(k_fused_deslice_bwd<T, NT>, NT, p);
+    case Kind::StatsOnline: return resident(k_blk_stats<T, NT, false>, NT, p);
+    case Kind::StatsTwoPass: return resident(k_blk_stats<T, NT, true>, NT, p);
+    case Kind::DesliceFwdStats: return resident(k_blk_deslice_fwd<T, NT, false>, NT, p);
+    case Kind::DesliceFwdOnline: return resident(k_blk_deslice_fwd<T, NT, true>, NT, p);
+    case Kind::SliceFwdG: return resident(k_blk_slice_fwd_g<T, NT>, NT, p);
+    case Kind::SliceBwdN: return resident(k_blk_bwd_n<T, NT, true>, NT, p);
+    case Kind::DesliceBwdN: return resident(k_blk_bwd_n<T, NT, false>, NT, p);
+    case Kind::SliceBwdG: return resident(k_blk_bwd_g<T, NT, true>, NT, p);
+    case Kind::DesliceBwdG: return resident(k_blk_bwd_g<T, NT, false>, NT, p);
+  }
+  return 0;
+}
+
+int engine_resident(Kind k, int dtype, int nt, const Params& p) {
+  if (nt == 128) {
+    if (dtype == 0) return resident_kind<float, 128>(k, p);
+    if (dtype == 1) return resident_kind<__nv_bfloat16, 128>(k, p);
+    return resident_kind<__half, 128>(k, p);
+  }
+  if (dtype == 0) return resident_kind<float, 32>(k, p);
+  if (dtype == 1) return resident_kind<__nv_bfloat16, 32>(k, p);
+  return resident_kind<__half, 32>(k, p);
+}
+
 cudaError_t run_engine(Kind k, int dtype, int nt, const Params& p, int nblk, cudaStream_t s) {
   const bool fused = k == Kind::FusedSliceFwd || k == Kind::FusedDesliceFwd ||
                      k == Kind::FusedSliceBwd || k == Kind::FusedDesliceBwd;

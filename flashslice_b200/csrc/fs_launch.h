@@ -92,6 +92,10 @@ extern std::atomic<uint64_t> g_launches;
 // nblk = slot blocks for the slot-owning kinds.
 cudaError_t run_engine(Kind k, int dtype, int nt, const Params& p, int nblk, cudaStream_t s);
 
+// CTAs of kind k (dtype, nt, p's shared-memory plan) resident per SM, 0 if
+// unknown.
+int engine_resident(Kind k, int dtype, int nt, const Params& p);
+
 // Fixed-order sum of per-program partials (see k_reduce).
 cudaError_t run_reduce(const float* part, float* out, int B, int H, int P, int64_t E, int ob_ext,
                        int oh_ext, cudaStream_t s);
