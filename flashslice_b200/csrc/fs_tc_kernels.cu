@@ -1,5 +1,6 @@
 // flashslice_b200 -- tensor-core (tcgen05) kernels of the single-tile family
-// for the hot shape: fp32 point tensors, D = DV = G = 32.
+// for the hot shape: D = DV = G = 32, fp32 or bf16 point tensors (the kernels
+// are templated on the point type; a bf16 value is its own exact hi part).
 //
 // Every product is formed on the tensor cores from an exact three-way bf16
 // split of each fp32 operand, x = hi + mid + lo (8 + 8 + 8 significant bits);
