@@ -125,6 +125,49 @@ bool tc_shape(const fs_problem& p) {
          p.D == 32 && p.DV == 32 && p.G == 32 && p.N >= 1;
 }
 
+// The slot-owning slice forward on the tensor cores (shapes past the single
+// tile, either family): bf16 point tensors in the bf16 dot mode (the value
+// dot rounds the weights w to bf16, blocked.py), D = 32, DV = 32 or 64, G a
+// multiple of 128, dense points.
+bool blk_tc_shape(const fs_problem& p) {
+  return p.engine == FS_ENGINE_AUTO && p.act_dtype == FS_BF16 &&
+         p.dot == 3 && p.D == 32 && (p.DV == 32 || p.DV == 64) && p.G % 128 == 0 &&
+         p.N >= 1 && !p.row_splits;
+}
+
+bool blk_tc_params(const fs_problem& p, const fs_tensor4* x, const fs_tensor4* v,
+                   const float* W, const float* bias, const float* tau, const float* stats,
+                   int max_p, tcx::TcParams& q) {
+  q = tcx::TcParams();
+  q.pdt = 1;
+  if (!tcx::make_point_map(&q.mx, x->data, p.B, p.N, p.H, x->stride, 2, (int)p.D) ||
+      !tcx::make_point_map(&q.mv, v->data, p.B, p.N, p.H, v->stride, 2, (int)p.DV))
+    return false;
+  q.status = tcx::device_status();
+  if (!q.status) return false;
+  q.B = (int)p.B;
+  q.N = (int)p.N;
+  q.H = (int)p.H;
+  q.G = (int)p.G;
+  q.dv = (int)p.DV;
+  q.ntiles = (int)((p.N + 127) / 128);
+  // two CTAs per SM over (slot blocks x b x h), one wave, within the partial
+  // buffers (sized for max_p programs per slot block of the FMA kernels)
+  int64_t P = 2 * kSmCount / (p.B * p.H * (p.G / 128));
+  if (P > max_p) P = max_p;
+  if (P > q.ntiles) P = q.ntiles;
+  q.P = (int)(P < 1 ? 1 : P);
+  q.W = W;
+  q.bias = bias;
+  q.tau = tau;
+  q.stats_in = stats;
+  q.swb = p.w_batch > 1 ? (int64_t)p.w_heads * p.G * p.D : 0;
+  q.swh = p.w_heads > 1 ? p.G * p.D : 0;
+  q.sbb = p.b_batch > 1 ? (int64_t)p.b_heads * p.G : 0;
+  q.sbh = p.b_heads > 1 ? p.G : 0;
+  return true;
+}
+
 // Fill the tensor-core parameters; false when a tensor map cannot be made
 // (the FMA kernels then serve the call).
 // TMA map of a point tensor of problem p: (B, N) rows, or with row splits
@@ -501,8 +544,19 @@ int fs_slice_fwd(const fs_problem* p, const fs_tensor4* x_mid, const fs_tensor4*
       stats = dst;
     }
     q.stats_in = stats;
-    P = s.Pg;
-    FS_CHECK(launch_kind(Kind::SliceFwdG, *p, s, q, P, st));
+    tcx::TcParams tb;
+    if (blk_tc_shape(*p) && tc_tensor_ok(x_mid) && tc_tensor_ok(fx_mid) &&
+        blk_tc_params(*p, x_mid, fx_mid, weight, bias, tau, stats, s.Pg, tb)) {
+      // the partial buffers sized for the FMA kernels hold the (fewer) CTAs'
+      tb.partA = q.partA;
+      tb.partS = q.partS;
+      P = tb.P;
+      route_note("slice_fwd", "tensor-core-blocked", *p, x_mid, fx_mid);
+      FS_TRY(tcx::run_tc(tcx::TcKind::BlkSliceFwd, tb, st));
+    } else {
+      P = s.Pg;
+      FS_CHECK(launch_kind(Kind::SliceFwdG, *p, s, q, P, st));
+    }
   }
   const int BH = s.BH;
   FS_TRY(run_reduce(q.partA, z_num, BH, 1, P, p->G * p->DV, BH, 1, st));

@@ -1472,6 +1472,154 @@ __global__ void __launch_bounds__(128 * kTCoupledBwd, kCtasCoupledBwd)
   epilogue<256>(c);
 }
 
+// ------------------------------------------------------------ blocked slice forward, bf16 dots
+// The slot-owning slice forward of the blocked family (blocked.py:404-462)
+// for bf16 point tensors in the bf16 dot mode, D = 32, DV in {32, 64}, G a
+// multiple of 128, with the per-point statistics (m, l) given. One CTA owns
+// 128 slots of one (b, h) and streams the points:
+//  * logits = x W^T on the tensor cores, exact: the bf16 x times W's three
+//    bf16 parts (six MMAs, N = 128), so that they match the statistics'
+//    fp32 logits;
+//  * w = exp(logit - m) / l per point, rounded to bf16 (the bf16 dot mode's
+//    value dot, blocked.py), written as the pool's slot-major operand;
+//  * z_num += w^T fx and s += w^T 1 (MMAs with N = DV and N = 16) accumulate
+//    in TMEM over the CTA's tiles.
+// Point tiles arrive by TMA as 16-byte column boxes, which lays them out as
+// the MMAs' operands directly (x K-major, fx point-major), double-buffered.
+// smem: [W parts x 3 (24 KB)][bias][x stage x 2][fx stage x 2][w tile][ones][bars]
+// TMEM: logits at 0 (128 columns), z_num at 128 (DV), s at 192 (16).
+constexpr int kBgSlots = 128;
+constexpr int kBgWs = 0, kBgBias = 3 * 8192, kBgX = kBgBias + 1024, kBgF = kBgX + 2 * 8192,
+              kBgW = kBgF + 2 * 16384, kBgOnes = kBgW + 32768, kBgBar = kBgOnes + 4096,
+              kBgBytes = kBgBar + kBarBytes;
+static_assert(kBgX % 1024 == 0 && kBgF % 1024 == 0 && kBgW % 1024 == 0, "blocked slice layout");
+
+__global__ void __launch_bounds__(128, 2) k_tc_blk_slice_fwd_bf16(const __grid_constant__ TcParams p) {
+  extern __shared__ __align__(16) uint8_t sm_raw[];
+  uint8_t* sm = align_smem(sm_raw);
+  const int gb = blockIdx.y, bh = blockIdx.z, b = bh / p.H, h = bh - b * p.H;
+  const int g0 = gb * kBgSlots, DV = p.dv;
+  const Span sp = span_of(p, b);
+  Ctl c = prologue_begin<256>(sm, kBgBar);
+  // W rows g0 .. g0 + 127, three bf16 parts, K-major (rows g, k = d) at +8 KB p
+  {
+    const float* Wb = p.W + (int64_t)b * p.swb + (int64_t)h * p.swh + (int64_t)g0 * 32;
+    for (int i = threadIdx.x; i < kBgSlots * 32; i += 128) {
+      const int r = i >> 5, k = i & 31;
+      __nv_bfloat16 hi, mi, lo;
+      split3(Wb[i], hi, mi, lo);
+      const uint32_t o = kmajor_off(r, k, 32);
+      *(__nv_bfloat16*)(sm + kBgWs + o) = lo;
+      *(__nv_bfloat16*)(sm + kBgWs + 8192 + o) = mi;
+      *(__nv_bfloat16*)(sm + kBgWs + 16384 + o) = hi;
+    }
+    const float inv_tau = __frcp_rn(p.tau[h]);
+    float* bias2 = (float*)(sm + kBgBias);
+    bias2[threadIdx.x] = p.bias[(int64_t)b * p.sbb + (int64_t)h * p.sbh + g0 + threadIdx.x] *
+                         inv_tau * kLog2e;
+    uint32_t* ones = (uint32_t*)(sm + kBgOnes);
+    for (int i = threadIdx.x; i < 1024; i += 128) ones[i] = 0x3F803F80u;  // bf16 1.0 pairs
+  }
+  prologue_end(c);
+  const float scale = __frcp_rn(p.tau[h]) * kLog2e;
+  const float* bias2 = (const float*)(sm + kBgBias);
+  const uint32_t tL = c.tmem, tZ = c.tmem + 128, tS = c.tmem + 192;
+  const int row = threadIdx.x;                                       // point row / slot
+  const uint32_t tlane = (uint32_t)((threadIdx.x >> 5) * 32) << 16;  // its TMEM lane
+  const uint32_t stage_b = (uint32_t)(4 + DV / 8) * 2048;  // bytes of one tile's boxes
+  auto xs = [&](int k) { return sm + kBgX + (k & 1) * 8192; };
+  auto fs = [&](int k) { return sm + kBgF + (k & 1) * 16384; };
+  auto load = [&](int k, int tile) {  // tile's x (4 boxes) and fx (DV / 8 boxes), one thread
+    mbar_arrive_expect_tx(c.bar + kBarTma, stage_b);
+    for (int q = 0; q < 4; ++q)
+      tma_load_4d(xs(k) + q * 2048, &p.mx, 8 * q, h, sp.row(tile), sp.bc, c.bar + kBarTma);
+    for (int q = 0; q < DV / 8; ++q)
+      tma_load_4d(fs(k) + q * 2048, &p.mv, 8 * q, h, sp.row(tile), sp.bc, c.bar + kBarTma);
+  };
+  const uint32_t id_l = idesc_bf16(128, 128, 0, 0), id_z = idesc_bf16(128, DV == 64 ? 64 : 32, 1, 1),
+                 id_s = idesc_bf16(128, 16, 1, 1);
+  const int n_my = sp.ntiles > (int)blockIdx.x ? (sp.ntiles - 1 - (int)blockIdx.x) / p.P + 1 : 0;
+  if (threadIdx.x == 0 && n_my > 0) load(0, blockIdx.x);
+  for (int k = 0; k < n_my; ++k) {
+    const int tile = blockIdx.x + k * p.P, n0 = tile * kTile;
+    wait_bar(c, kBarTma, p.status);
+    if (threadIdx.x == 0) {  // logits: x times W lo, mid, hi (small first)
+      for (int part = 0; part < 3; ++part)
+        for (int ks = 0; ks < 2; ++ks)
+          mma_bf16(tL, smem_desc(smem_u32(xs(k)) + ks * 4096, 2048, 128),
+                   smem_desc(smem_u32(sm + kBgWs + part * 8192) + ks * 256, 128, 512), id_l,
+                   (part | ks) != 0);
+      commit(c, kG1);
+    }
+    if (k > 0) wait_bar(c, kG2, p.status);  // tile k - 1's pool: its buffers and the w tile free
+    if (threadIdx.x == 0 && k + 1 < n_my) load(k + 1, tile + p.P);
+    wait_bar(c, kG1, p.status);
+    {
+      const int n = n0 + row;
+      const bool valid = n < sp.N;
+      float m2 = 0.f, inv_l = 0.f;
+      if (valid) {
+        const float* st = p.stats_in + (int64_t)bh * 2 * p.N;
+        const int64_t ni = sp.n0 + n;
+        m2 = st[ni] * kLog2e;
+        inv_l = __frcp_rn(st[p.N + ni]);
+      }
+      uint8_t* wrow = sm + kBgW + (row >> 3) * (kBgSlots * 16) + (row & 7) * 16;
+#pragma unroll
+      for (int ch = 0; ch < 4; ++ch) {
+        uint32_t r[32];
+        tld<32>(tL + tlane + ch * 32, r);
+        tld_wait();
+        uint32_t wv[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int g = ch * 32 + 2 * j;
+          const float a =
+              valid ? ex2(__uint_as_float(r[2 * j]) * scale + bias2[g] - m2) * inv_l : 0.f;
+          const float e =
+              valid ? ex2(__uint_as_float(r[2 * j + 1]) * scale + bias2[g + 1] - m2) * inv_l : 0.f;
+          wv[j] = bf2_bits(__floats2bfloat162_rn(a, e));
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q)  // slots ch*32 + 8q .. +7: one 16-byte chunk
+          *(uint4*)(wrow + (ch * 4 + q) * 128) =
+              make_uint4(wv[4 * q], wv[4 * q + 1], wv[4 * q + 2], wv[4 * q + 3]);
+      }
+    }
+    to_async_barrier();
+    if (threadIdx.x == 0) {  // z_num += w^T fx, s += w^T 1, 16 points a step
+      for (int ks = 0; ks < 8; ++ks) {
+        const uint64_t ad = smem_desc(smem_u32(sm + kBgW) + ks * 2 * (kBgSlots * 16), kBgSlots * 16, 128);
+        mma_bf16(tZ, ad, smem_desc(smem_u32(fs(k)) + ks * 256, 128, 2048), id_z, (k | ks) != 0);
+        mma_bf16(tS, ad, smem_desc(smem_u32(sm + kBgOnes) + ks * 256, 128, 2048), id_s,
+                 (k | ks) != 0);
+      }
+      commit(c, kG2);
+    }
+  }
+  if (n_my > 0) wait_bar(c, kG2, p.status);
+  tc_fence_after();
+  // this CTA's partial sums: row = slot g0 + row
+  const int64_t slot = (int64_t)bh * p.P + blockIdx.x;
+  float* pz = p.partA + (slot * p.G + g0 + row) * DV;
+  float* ps = p.partS + slot * p.G + g0 + row;
+  if (n_my > 0) {
+    uint32_t r[32];
+    for (int ch = 0; ch < DV / 32; ++ch) {
+      tld<32>(tZ + tlane + ch * 32, r);
+      tld_wait();
+      for (int j = 0; j < 32; ++j) pz[ch * 32 + j] = __uint_as_float(r[j]);
+    }
+    tld<32>(tS + tlane, r);  // 16 columns read, the first holds s
+    tld_wait();
+    *ps = __uint_as_float(r[0]);
+  } else {
+    for (int j = 0; j < DV; ++j) pz[j] = 0.f;
+    *ps = 0.f;
+  }
+  epilogue<256>(c);
+}
+
 // ------------------------------------------------------------ wait self-test
 // One thread waits, with a limit of limit_ns, on an mbarrier that nothing
 // arrives at: the bounded-wait path of the kernels (status word set, the
@@ -1502,7 +1650,7 @@ int* device_status() {
 }
 
 bool make_point_map(CUtensorMap* map, const void* data, int64_t B, int64_t N, int64_t H,
-                    const int64_t stride[4], int pdt) {
+                    const int64_t stride[4], int pdt, int width) {
   static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
   if (!encode) {
     void* fn = nullptr;
@@ -1513,7 +1661,7 @@ bool make_point_map(CUtensorMap* map, const void* data, int64_t B, int64_t N, in
       return false;
     encode = (PFN_cuTensorMapEncodeTiled_v12000)fn;
   }
-  const int64_t es = pdt == 1 ? 2 : 4;
+  const int64_t es = pdt == 0 ? 4 : 2;
   if (stride[3] != 1 || ((uintptr_t)data & 15)) return false;
   for (int i = 0; i < 3; ++i)
     if (stride[i] <= 0 || (stride[i] * es) % 16 || stride[i] * es >= ((int64_t)1 << 40))
@@ -1524,21 +1672,25 @@ bool make_point_map(CUtensorMap* map, const void* data, int64_t B, int64_t N, in
   // context, which cudaSetDevice does.
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || cudaSetDevice(dev) != cudaSuccess) return false;
-  cuuint64_t dims[4] = {32, (cuuint64_t)H, (cuuint64_t)N, (cuuint64_t)B};
+  cuuint64_t dims[4] = {(cuuint64_t)width, (cuuint64_t)H, (cuuint64_t)N, (cuuint64_t)B};
   cuuint64_t gstr[3] = {(cuuint64_t)(stride[2] * es), (cuuint64_t)(stride[1] * es),
                         (cuuint64_t)(stride[0] * es)};
-  cuuint32_t box[4] = {32, 1, kTile, 1};
+  cuuint32_t box[4] = {pdt == 2 ? 8u : 32u, 1, kTile, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   // the encoder wants a 64-byte aligned map; do not rely on the caller's stack
   unsigned char raw[sizeof(CUtensorMap) + 64];
   CUtensorMap* aligned = (CUtensorMap*)(((uintptr_t)raw + 63) & ~(uintptr_t)63);
-  // fp32 rows are 128 bytes (128B swizzle), bf16 rows 64 bytes (64B swizzle)
+  // fp32 rows are 128 bytes (128B swizzle), bf16 rows 64 bytes (64B swizzle);
+  // mode 2: bf16, 16-byte column boxes of 128 rows, no swizzle (one box lands
+  // as 16 contiguous 8 x 16-byte core matrices)
   const CUresult r = encode(aligned,
-                            pdt == 1 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
-                                     : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                            pdt == 0 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                     : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
                             4, const_cast<void*>(data), dims, gstr, box, estr,
                             CU_TENSOR_MAP_INTERLEAVE_NONE,
-                            pdt == 1 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
+                            pdt == 0   ? CU_TENSOR_MAP_SWIZZLE_128B
+                            : pdt == 1 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                       : CU_TENSOR_MAP_SWIZZLE_NONE,
                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return false;
   std::memcpy(map, aligned, sizeof(CUtensorMap));
@@ -1580,7 +1732,15 @@ static cudaError_t run_tc_t(TcKind k, const TcParams& p, cudaStream_t s) {
 }
 
 cudaError_t run_tc(TcKind k, const TcParams& p, cudaStream_t s) {
-  const cudaError_t e = p.pdt == 1 ? run_tc_t<__nv_bfloat16>(k, p, s) : run_tc_t<float>(k, p, s);
+  cudaError_t e;
+  if (k == TcKind::BlkSliceFwd) {
+    e = set_smem((const void*)k_tc_blk_slice_fwd_bf16, kBgBytes + kSmemPad);
+    if (e == cudaSuccess)
+      k_tc_blk_slice_fwd_bf16<<<dim3(p.P, p.G / kBgSlots, p.B * p.H), 128, kBgBytes + kSmemPad,
+                                s>>>(p);
+  } else {
+    e = p.pdt == 1 ? run_tc_t<__nv_bfloat16>(k, p, s) : run_tc_t<float>(k, p, s);
+  }
   if (e != cudaSuccess) return e;
   g_launches.fetch_add(1, std::memory_order_relaxed);
   g_tc_launches.fetch_add(1, std::memory_order_relaxed);
@@ -1604,6 +1764,7 @@ int tc_ctas_per_sm(TcKind k) {
     case TcKind::SliceBwd: return kCtasSliceBwd;
     case TcKind::DesliceBwd: return kCtasDesliceBwd;
     case TcKind::CoupledBwd: return kCtasCoupledBwd;
+    case TcKind::BlkSliceFwd: return 2;
   }
   return 1;
 }
@@ -1611,6 +1772,7 @@ int tc_ctas_per_sm(TcKind k) {
 // shared memory per SM (228 KB) holds the co-resident CTAs, each with its
 // alignment pad and the 1 KB the runtime reserves per CTA
 static_assert((kSfBytes + kSmemPad + 1024) * kCtasSliceFwd <= 228 * 1024, "slice fwd smem");
+static_assert((kBgBytes + kSmemPad + 1024) * 2 <= 228 * 1024, "blocked slice fwd smem");
 static_assert((kDfBytes + kSmemPad + 1024) * kCtasDesliceFwd <= 228 * 1024, "deslice fwd smem");
 static_assert((kSbBytes + kSmemPad + 1024) * kCtasSliceBwd <= 228 * 1024, "slice bwd smem");
 static_assert((kDbBytes + kSmemPad + 1024) * kCtasDesliceBwd <= 228 * 1024, "deslice bwd smem");

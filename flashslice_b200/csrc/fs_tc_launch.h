@@ -11,7 +11,7 @@
 namespace fs {
 namespace tcx {
 
-enum class TcKind { SliceFwd, DesliceFwd, SliceBwd, DesliceBwd, CoupledBwd };
+enum class TcKind { SliceFwd, DesliceFwd, SliceBwd, DesliceBwd, CoupledBwd, BlkSliceFwd };
 
 constexpr int kMaxSplits = 128;  // FS_MAX_SPLITS
 
@@ -21,6 +21,8 @@ struct TcParams {
   CUtensorMap mo;  // d_out of the coupled backward (mv is fx_mid there)
   int B, N, H, P, ntiles;
   int pdt;  // point tensors' type: 0 fp32, 1 bf16 (tiles, outputs)
+  int dv, G;              // the blocked slice forward's value width and slot count
+  const float* stats_in;  // its per-point statistics (B, H, 2, N)
   const float* W;
   const float* bias;
   const float* tau;
@@ -57,7 +59,7 @@ int tc_ctas_per_sm(TcKind k);
 // (width stride != 1, unaligned base or strides) or the driver entry point is
 // missing.
 bool make_point_map(CUtensorMap* map, const void* data, int64_t B, int64_t N, int64_t H,
-                    const int64_t stride[4], int pdt = 0);
+                    const int64_t stride[4], int pdt = 0, int width = 32);
 
 // Address of this library's device status word on the current device.
 int* device_status();
