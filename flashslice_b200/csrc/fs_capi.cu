@@ -137,7 +137,7 @@ bool blk_tc_shape(const fs_problem& p) {
 
 bool blk_tc_params(const fs_problem& p, const fs_tensor4* x, const fs_tensor4* v,
                    const float* W, const float* bias, const float* tau, const float* stats,
-                   int max_p, tcx::TcParams& q) {
+                   int max_p, tcx::TcParams& q, int ctas_per_sm = 2) {
   q = tcx::TcParams();
   q.pdt = 1;
   if (!tcx::make_point_map(&q.mx, x->data, p.B, p.N, p.H, x->stride, 2, (int)p.D) ||
@@ -151,9 +151,9 @@ bool blk_tc_params(const fs_problem& p, const fs_tensor4* x, const fs_tensor4* v
   q.G = (int)p.G;
   q.dv = (int)p.DV;
   q.ntiles = (int)((p.N + 127) / 128);
-  // two CTAs per SM over (slot blocks x b x h), one wave, within the partial
+  // ctas_per_sm CTAs per SM over (slot blocks x b x h), one wave, within the partial
   // buffers (sized for max_p programs per slot block of the FMA kernels)
-  int64_t P = 2 * kSmCount / (p.B * p.H * (p.G / 128));
+  int64_t P = ctas_per_sm * kSmCount / (p.B * p.H * (p.G / 128));
   if (P > max_p) P = max_p;
   if (P > q.ntiles) P = q.ntiles;
   q.P = (int)(P < 1 ? 1 : P);
@@ -697,8 +697,23 @@ static int bwd_common(bool slice, const fs_problem* p, const fs_tensor4* x_mid,
     q.stats_in = stats;
     q.delta = at(workspace, s.delta);
     FS_CHECK(launch_kind(slice ? Kind::SliceBwdN : Kind::DesliceBwdN, *p, s, q, Pdt, st));
-    Pw = s.Pg;
-    FS_CHECK(launch_kind(slice ? Kind::SliceBwdG : Kind::DesliceBwdG, *p, s, q, Pw, st));
+    tcx::TcParams tb;
+    if (blk_tc_shape(*p) && tc_tensor_ok(x_mid) && tc_tensor_ok(vals) &&
+        blk_tc_params(*p, x_mid, vals, weight, bias, tau, stats, s.Pg, tb, 1)) {
+      tb.M = mat;
+      tb.ds = ds;
+      tb.delta = q.delta;
+      tb.partA = q.partA;
+      tb.partB = q.partB;
+      tb.partS = q.partS;
+      Pw = tb.P;
+      route_note(slice ? "slice_bwd (slot-owning)" : "deslice_bwd (slot-owning)",
+                 "tensor-core-blocked", *p, x_mid, vals);
+      FS_TRY(tcx::run_tc(slice ? tcx::TcKind::BlkSliceBwdG : tcx::TcKind::BlkDesliceBwdG, tb, st));
+    } else {
+      Pw = s.Pg;
+      FS_CHECK(launch_kind(slice ? Kind::SliceBwdG : Kind::DesliceBwdG, *p, s, q, Pw, st));
+    }
   }
   const int B = (int)p->B, H = (int)p->H, BH = s.BH;
   FS_TRY(run_reduce(q.partA, dW, B, H, Pw, p->G * p->D, p->w_batch, p->w_heads, st));

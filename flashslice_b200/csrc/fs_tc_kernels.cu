@@ -1620,6 +1620,204 @@ __global__ void __launch_bounds__(128, 2) k_tc_blk_slice_fwd_bf16(const __grid_c
   epilogue<256>(c);
 }
 
+// ------------------------------------------------------------ blocked backward, slot-owning, bf16 dots
+// The slot-owning half of the blocked backward (slice: dW, db, blocked.py:
+// 677-741; deslice: dW, db, dtokens, :819-888) for bf16 point tensors in the
+// bf16 dot mode, D = 32, DV in {32, 64}, G a multiple of 128, given the
+// statistics and the point-owning pass's delta and row sums. One CTA owns 128
+// slots of one (b, h) and streams the points; per tile:
+//  * logits = x W^T and dw = v M^T (v = d_out with M = tokens, or v = fx with
+//    M = dz_num, plus ds), both exact on the tensor cores (W and M in three
+//    bf16 parts; the bf16 x and v are exact), N = 128;
+//  * w = exp(logit - m) / l, dl = w (dw - delta) / tau, written as bf16
+//    slot-major operands (the bf16 value dots);
+//  * dW += dl^T x, db += dl^T 1 and, deslice, dtokens += w^T d_out,
+//    accumulated in TMEM over the CTA's tiles.
+// Two threads per point row (64 slots each). One CTA per SM (TMEM).
+// smem: [W parts][M parts][bias][ds][x stage x 2][v stage x 2][dl tile][w tile][ones][bars]
+// TMEM: logits 0, dw 128, dW 256 (32), db 288 (16), dtokens 320 (DV).
+constexpr int kBbW = 0, kBbM = 3 * 8192, kBbBias = kBbM + 3 * 16384, kBbDs = kBbBias + 512,
+              kBbX = kBbDs + 512 + 1024 - ((kBbDs + 512) % 1024), kBbV = kBbX + 2 * 8192,
+              kBbDl = kBbV + 2 * 16384, kBbWt = kBbDl + 32768, kBbOnes = kBbWt + 32768,
+              kBbBar = kBbOnes + 4096, kBbBytes = kBbBar + kBarBytes;
+static_assert(kBbX % 1024 == 0 && kBbDl % 1024 == 0, "blocked backward layout");
+
+template <bool SLICE>
+__global__ void __launch_bounds__(256, 1) k_tc_blk_bwd_g_bf16(const __grid_constant__ TcParams p) {
+  extern __shared__ __align__(16) uint8_t sm_raw[];
+  uint8_t* sm = align_smem(sm_raw);
+  const int gb = blockIdx.y, bh = blockIdx.z, b = bh / p.H, h = bh - b * p.H;
+  const int g0 = gb * kBgSlots, DV = p.dv;
+  const Span sp = span_of(p, b);
+  Ctl c = prologue_begin<512>(sm, kBbBar);
+  const float inv_tau = __frcp_rn(p.tau[h]);
+  {
+    // W rows g0 .. g0 + 127 (K = d, 32) and M rows (K = dv) in three bf16 parts
+    const float* Wb = p.W + (int64_t)b * p.swb + (int64_t)h * p.swh + (int64_t)g0 * 32;
+    for (int i = threadIdx.x; i < kBgSlots * 32; i += 256) {
+      const int r = i >> 5, k = i & 31;
+      __nv_bfloat16 hi, mi, lo;
+      split3(Wb[i], hi, mi, lo);
+      const uint32_t o = kmajor_off(r, k, 32);
+      *(__nv_bfloat16*)(sm + kBbW + o) = lo;
+      *(__nv_bfloat16*)(sm + kBbW + 8192 + o) = mi;
+      *(__nv_bfloat16*)(sm + kBbW + 16384 + o) = hi;
+    }
+    const float* Mb = p.M + ((int64_t)bh * p.G + g0) * DV;
+    for (int i = threadIdx.x; i < kBgSlots * DV; i += 256) {
+      const int r = i / DV, k = i - r * DV;
+      __nv_bfloat16 hi, mi, lo;
+      split3(Mb[i], hi, mi, lo);
+      const uint32_t o = kmajor_off(r, k, DV);
+      *(__nv_bfloat16*)(sm + kBbM + o) = lo;
+      *(__nv_bfloat16*)(sm + kBbM + 16384 + o) = mi;
+      *(__nv_bfloat16*)(sm + kBbM + 32768 + o) = hi;
+    }
+    if (threadIdx.x < kBgSlots) {
+      float* bias2 = (float*)(sm + kBbBias);
+      bias2[threadIdx.x] = p.bias[(int64_t)b * p.sbb + (int64_t)h * p.sbh + g0 + threadIdx.x] *
+                           inv_tau * kLog2e;
+      ((float*)(sm + kBbDs))[threadIdx.x] = SLICE ? p.ds[(int64_t)bh * p.G + g0 + threadIdx.x] : 0.f;
+    }
+    uint32_t* ones = (uint32_t*)(sm + kBbOnes);
+    for (int i = threadIdx.x; i < 1024; i += 256) ones[i] = 0x3F803F80u;
+  }
+  prologue_end(c);
+  const float scale = inv_tau * kLog2e;
+  const float* bias2 = (const float*)(sm + kBbBias);
+  const float* dss = (const float*)(sm + kBbDs);
+  const uint32_t tL = c.tmem, tD = c.tmem + 128, tW = c.tmem + 256, tB = c.tmem + 288,
+                 tT = c.tmem + 320;
+  const int warp = threadIdx.x >> 5, row = 32 * (warp & 3) + (threadIdx.x & 31), half = warp >> 2;
+  const uint32_t tlane = (uint32_t)(32 * (warp & 3)) << 16;
+  const uint32_t stage_b = (uint32_t)(4 + DV / 8) * 2048;
+  auto xs = [&](int k) { return sm + kBbX + (k & 1) * 8192; };
+  auto vs = [&](int k) { return sm + kBbV + (k & 1) * 16384; };
+  auto load = [&](int k, int tile) {
+    mbar_arrive_expect_tx(c.bar + kBarTma, stage_b);
+    for (int q = 0; q < 4; ++q)
+      tma_load_4d(xs(k) + q * 2048, &p.mx, 8 * q, h, sp.row(tile), sp.bc, c.bar + kBarTma);
+    for (int q = 0; q < DV / 8; ++q)
+      tma_load_4d(vs(k) + q * 2048, &p.mv, 8 * q, h, sp.row(tile), sp.bc, c.bar + kBarTma);
+  };
+  const uint32_t id_l = idesc_bf16(128, 128, 0, 0);
+  const uint32_t id_w = idesc_bf16(128, 32, 1, 1), id_s = idesc_bf16(128, 16, 1, 1),
+                 id_t = idesc_bf16(128, DV == 64 ? 64 : 32, 1, 1);
+  const int n_my = sp.ntiles > (int)blockIdx.x ? (sp.ntiles - 1 - (int)blockIdx.x) / p.P + 1 : 0;
+  if (threadIdx.x == 0 && n_my > 0) load(0, blockIdx.x);
+  for (int k = 0; k < n_my; ++k) {
+    const int tile = blockIdx.x + k * p.P, n0 = tile * kTile;
+    wait_bar(c, kBarTma, p.status);
+    if (threadIdx.x == 0) {
+      for (int part = 0; part < 3; ++part)  // logits = x W^T (lo, mid, hi of W)
+        for (int ks = 0; ks < 2; ++ks)
+          mma_bf16(tL, smem_desc(smem_u32(xs(k)) + ks * 4096, 2048, 128),
+                   smem_desc(smem_u32(sm + kBbW + part * 8192) + ks * 256, 128, 512), id_l,
+                   (part | ks) != 0);
+      for (int part = 0; part < 3; ++part)  // dw = v M^T
+        for (int ks = 0; ks < DV / 16; ++ks)
+          mma_bf16(tD, smem_desc(smem_u32(vs(k)) + ks * 4096, 2048, 128),
+                   smem_desc(smem_u32(sm + kBbM + part * 16384) + ks * 256, 128, DV * 16), id_l,
+                   (part | ks) != 0);
+      commit(c, kG1);
+    }
+    if (k > 0) wait_bar(c, kG2, p.status);  // tile k - 1's pools: buffers and tiles free
+    if (threadIdx.x == 0 && k + 1 < n_my) load(k + 1, tile + p.P);
+    wait_bar(c, kG1, p.status);
+    {
+      const int n = n0 + row;
+      const bool valid = n < sp.N;
+      float m2 = 0.f, r = 0.f, delta = 0.f;
+      if (valid) {
+        const int64_t ni = sp.n0 + n;
+        m2 = p.stats_in[(int64_t)bh * 2 * p.N + ni] * kLog2e;
+        delta = p.delta[(int64_t)bh * 2 * p.N + ni];
+        r = __frcp_rn(p.delta[(int64_t)bh * 2 * p.N + p.N + ni]);
+      }
+      uint8_t* dlrow = sm + kBbDl + (row >> 3) * (kBgSlots * 16) + (row & 7) * 16;
+      uint8_t* wrow = sm + kBbWt + (row >> 3) * (kBgSlots * 16) + (row & 7) * 16;
+#pragma unroll
+      for (int ch = 0; ch < 2; ++ch) {
+        const int c0 = half * 64 + ch * 32;
+        uint32_t lr[32], dr[32];
+        tld<32>(tL + tlane + c0, lr);
+        tld<32>(tD + tlane + c0, dr);
+        tld_wait();
+        uint32_t dl2[16], w2[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          float wv[2], dv[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int g = c0 + 2 * j + e;
+            const float w = valid ? ex2(__uint_as_float(lr[2 * j + e]) * scale + bias2[g] - m2) * r
+                                  : 0.f;
+            const float dwv = __uint_as_float(dr[2 * j + e]) + dss[g];
+            wv[e] = w;
+            dv[e] = w * (dwv - delta) * inv_tau;
+          }
+          dl2[j] = bf2_bits(__floats2bfloat162_rn(dv[0], dv[1]));
+          w2[j] = bf2_bits(__floats2bfloat162_rn(wv[0], wv[1]));
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int chunk = (c0 >> 3) + q;
+          *(uint4*)(dlrow + chunk * 128) =
+              make_uint4(dl2[4 * q], dl2[4 * q + 1], dl2[4 * q + 2], dl2[4 * q + 3]);
+          if (!SLICE)
+            *(uint4*)(wrow + chunk * 128) =
+                make_uint4(w2[4 * q], w2[4 * q + 1], w2[4 * q + 2], w2[4 * q + 3]);
+        }
+      }
+    }
+    to_async_barrier();
+    if (threadIdx.x == 0) {  // dW += dl^T x, db += dl^T 1, dtokens += w^T d_out
+      for (int ks = 0; ks < 8; ++ks) {
+        const uint64_t ad = smem_desc(smem_u32(sm + kBbDl) + ks * 4096, 2048, 128);
+        mma_bf16(tW, ad, smem_desc(smem_u32(xs(k)) + ks * 256, 128, 2048), id_w, (k | ks) != 0);
+        mma_bf16(tB, ad, smem_desc(smem_u32(sm + kBbOnes) + ks * 256, 128, 2048), id_s,
+                 (k | ks) != 0);
+        if (!SLICE)
+          mma_bf16(tT, smem_desc(smem_u32(sm + kBbWt) + ks * 4096, 2048, 128),
+                   smem_desc(smem_u32(vs(k)) + ks * 256, 128, 2048), id_t, (k | ks) != 0);
+      }
+      commit(c, kG2);
+    }
+  }
+  if (n_my > 0) wait_bar(c, kG2, p.status);
+  tc_fence_after();
+  // partial sums: threads 0-127, one slot each
+  if (threadIdx.x < 128) {
+    const int64_t slot = (int64_t)bh * p.P + blockIdx.x;
+    const int g = g0 + threadIdx.x;
+    float* pw = p.partA + (slot * p.G + g) * 32;
+    float* pb = p.partS + slot * p.G + g;
+    uint32_t rr[32];
+    if (n_my > 0) {
+      tld<32>(tW + tlane, rr);
+      tld_wait();
+      for (int j = 0; j < 32; ++j) pw[j] = __uint_as_float(rr[j]);
+      tld<32>(tB + tlane, rr);
+      tld_wait();
+      *pb = __uint_as_float(rr[0]);
+      if (!SLICE) {
+        float* pt = p.partB + (slot * p.G + g) * DV;
+        for (int ch = 0; ch < DV / 32; ++ch) {
+          tld<32>(tT + tlane + ch * 32, rr);
+          tld_wait();
+          for (int j = 0; j < 32; ++j) pt[ch * 32 + j] = __uint_as_float(rr[j]);
+        }
+      }
+    } else {
+      for (int j = 0; j < 32; ++j) pw[j] = 0.f;
+      *pb = 0.f;
+      if (!SLICE)
+        for (int j = 0; j < DV; ++j) p.partB[(slot * p.G + g) * DV + j] = 0.f;
+    }
+  }
+  epilogue<512>(c);
+}
+
 // ------------------------------------------------------------ wait self-test
 // One thread waits, with a limit of limit_ns, on an mbarrier that nothing
 // arrives at: the bounded-wait path of the kernels (status word set, the
@@ -1733,7 +1931,18 @@ static cudaError_t run_tc_t(TcKind k, const TcParams& p, cudaStream_t s) {
 
 cudaError_t run_tc(TcKind k, const TcParams& p, cudaStream_t s) {
   cudaError_t e;
-  if (k == TcKind::BlkSliceFwd) {
+  if (k == TcKind::BlkSliceBwdG || k == TcKind::BlkDesliceBwdG) {
+    const bool sl = k == TcKind::BlkSliceBwdG;
+    const void* fn = sl ? (const void*)k_tc_blk_bwd_g_bf16<true> : (const void*)k_tc_blk_bwd_g_bf16<false>;
+    e = set_smem(fn, kBbBytes + kSmemPad);
+    if (e == cudaSuccess) {
+      const dim3 grid(p.P, p.G / kBgSlots, p.B * p.H);
+      if (sl)
+        k_tc_blk_bwd_g_bf16<true><<<grid, 256, kBbBytes + kSmemPad, s>>>(p);
+      else
+        k_tc_blk_bwd_g_bf16<false><<<grid, 256, kBbBytes + kSmemPad, s>>>(p);
+    }
+  } else if (k == TcKind::BlkSliceFwd) {
     e = set_smem((const void*)k_tc_blk_slice_fwd_bf16, kBgBytes + kSmemPad);
     if (e == cudaSuccess)
       k_tc_blk_slice_fwd_bf16<<<dim3(p.P, p.G / kBgSlots, p.B * p.H), 128, kBgBytes + kSmemPad,
@@ -1765,6 +1974,8 @@ int tc_ctas_per_sm(TcKind k) {
     case TcKind::DesliceBwd: return kCtasDesliceBwd;
     case TcKind::CoupledBwd: return kCtasCoupledBwd;
     case TcKind::BlkSliceFwd: return 2;
+    case TcKind::BlkSliceBwdG:
+    case TcKind::BlkDesliceBwdG: return 1;
   }
   return 1;
 }
@@ -1773,6 +1984,7 @@ int tc_ctas_per_sm(TcKind k) {
 // alignment pad and the 1 KB the runtime reserves per CTA
 static_assert((kSfBytes + kSmemPad + 1024) * kCtasSliceFwd <= 228 * 1024, "slice fwd smem");
 static_assert((kBgBytes + kSmemPad + 1024) * 2 <= 228 * 1024, "blocked slice fwd smem");
+static_assert(kBbBytes + kSmemPad + 1024 <= 228 * 1024, "blocked backward smem");
 static_assert((kDfBytes + kSmemPad + 1024) * kCtasDesliceFwd <= 228 * 1024, "deslice fwd smem");
 static_assert((kSbBytes + kSmemPad + 1024) * kCtasSliceBwd <= 228 * 1024, "slice bwd smem");
 static_assert((kDbBytes + kSmemPad + 1024) * kCtasDesliceBwd <= 228 * 1024, "deslice bwd smem");

@@ -11,7 +11,16 @@
 namespace fs {
 namespace tcx {
 
-enum class TcKind { SliceFwd, DesliceFwd, SliceBwd, DesliceBwd, CoupledBwd, BlkSliceFwd };
+enum class TcKind {
+  SliceFwd,
+  DesliceFwd,
+  SliceBwd,
+  DesliceBwd,
+  CoupledBwd,
+  BlkSliceFwd,     // blocked slot-owning slice forward, bf16 dots
+  BlkSliceBwdG,    // blocked slot-owning slice backward (dW, db), bf16 dots
+  BlkDesliceBwdG,  // blocked slot-owning deslice backward (dW, db, dtokens), bf16 dots
+};
 
 constexpr int kMaxSplits = 128;  // FS_MAX_SPLITS
 
@@ -23,6 +32,7 @@ struct TcParams {
   int pdt;  // point tensors' type: 0 fp32, 1 bf16 (tiles, outputs)
   int dv, G;              // the blocked slice forward's value width and slot count
   const float* stats_in;  // its per-point statistics (B, H, 2, N)
+  const float* delta;     // the blocked backward's per-point delta and row sum (B, H, 2, N)
   const float* W;
   const float* bias;
   const float* tau;

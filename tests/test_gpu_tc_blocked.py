@@ -64,3 +64,46 @@ def test_blocked_slice_on_tensor_cores(env, case):
     assert lib.fs_tc_launch_count() - n1 == 1
     assert torch.equal(z2, z) and torch.equal(s2, s)
     assert lib.fs_device_status(1) == 0
+
+
+@pytest.mark.parametrize("case", [
+    dict(B=1, N=5000, H=4, DV=64, G=128, mode="hgd", bias=True),
+    dict(B=2, N=20_000, H=8, DV=64, G=1024, mode="bhgd", bias=False),
+    dict(B=1, N=3001, H=2, DV=32, G=256, mode="gd", bias=True),
+], ids=["g128", "g1024-cfg3like", "g256-dv32"])
+def test_blocked_round_backward_on_tensor_cores(env, case):
+    """A whole op-by-op round (slice, normalise, deslice) and its backward:
+    the slot-owning backward kernels (dW, db, dtokens) run on the tensor
+    cores; every gradient against the FMA engine and the float64 math."""
+    K, st, lib = env
+    x, fx, W, b, tau = _inputs(**case)
+    g = torch.Generator().manual_seed(8)
+    up = torch.randn(x.shape[:3] + (case["DV"],), generator=g).bfloat16().cuda()
+    bb = b if b is not None else torch.zeros(W.shape[-2], device="cuda")
+
+    def round_(engine):
+        st.set_engine(engine)
+        try:
+            L = [t.clone().requires_grad_(True) for t in (x, fx, W, bb, tau)]
+            z, s = K.fused_slice(*L)
+            out = K.fused_deslice(L[0], L[2], L[3], L[4], z / (s + 1e-5)[..., None])
+            (out.float() * up.float()).sum().backward()
+            torch.cuda.synchronize()
+            return [out] + [t.grad for t in L]
+        finally:
+            st.set_engine("auto")
+
+    n0 = lib.fs_tc_launch_count()
+    tc = round_("auto")
+    # the slot-owning slice forward, and the slot-owning halves of both backward ops
+    assert lib.fs_tc_launch_count() - n0 == 3
+    ex = round_("fma")
+    from oracle import eager_torch as E
+    ref = E.coupling_round(*[t.detach().double().clone().requires_grad_(True)
+                             for t in (x, fx, W, bb, tau)], up.double())
+    for a, e, k in zip(tc, ex, ("out", "grad:x", "grad:fx", "grad:W", "grad:b", "grad:tau")):
+        # the temperature gradient is a sum that cancels: the bf16 rounding of
+        # the value dots moves it most (the reference's bf16 gate, 2e-2)
+        assert relerr(a, e) <= (2e-2 if k == "grad:tau" else 1e-2), (k, relerr(a, e))
+        assert relerr(a, ref[k]) <= 2e-2, (k, relerr(a, ref[k]))
+    assert lib.fs_device_status(1) == 0
