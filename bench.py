@@ -195,6 +195,50 @@ def op_timings(K, x, fx, W, b, tau, r, dot, reps=3):
     return {k: statistics.median(v) for k, v in times.items()}
 
 
+def op_timings_blocked(x, fx, W, b, tau, r, dot, reps=3):
+    """Per-op device time (ms) of one round on the blocked family, the ops
+    ``fused_coupling`` runs there: slice forward (statistics out), deslice
+    forward (statistics in), and the two backward ops. Median over reps."""
+    from flashslice_b200.kernels import blocked  # noqa: F401  (registers the ops)
+    ops = torch.ops.flashslice
+    bb = b if b is not None else W.new_zeros(W.shape[-2])
+    Wd, bd, td = W.detach(), bb.detach(), tau.detach()
+    xd, fd = x.detach(), fx.detach()
+    times = {k: [] for k in BLK_FLOPS}
+    for _ in range(reps):
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(8)]
+        ev[0].record()
+        z, s, st = ops.slice_blk(xd, fd, Wd, bd, td, None, dot)
+        ev[1].record()
+        den = (s + EPS)[..., None]
+        tok = z / den
+        ev[2].record()
+        ops.deslice_blk(xd, Wd, bd, td, tok, st, dot)
+        ev[3].record()
+        dx1, dtok, _, _, _ = ops.deslice_blk_bwd(xd, Wd, bd, td, tok, st, r, dot)
+        ev[4].record()
+        dz = dtok / den
+        ds = -(dtok * z).sum(-1) / (s + EPS) ** 2
+        ev[5].record()
+        ops.slice_blk_bwd(xd, fd, Wd, bd, td, st, dz, ds, dot)
+        ev[6].record()
+        torch.cuda.synchronize()
+        times["slice_fwd"].append(ev[0].elapsed_time(ev[1]))
+        times["deslice_fwd"].append(ev[2].elapsed_time(ev[3]))
+        times["deslice_bwd"].append(ev[3].elapsed_time(ev[4]))
+        times["slice_bwd"].append(ev[5].elapsed_time(ev[6]))
+    return {k: statistics.median(v) for k, v in times.items()}
+
+
+# Algorithmic flops per point-head of each blocked op, in units of 2 G
+# (multiply-adds of the minimal dots): slice forward logits + pool (D + DV),
+# deslice forward logits + scatter (D + DV), each backward logits, two value
+# dots, dx and dW (3 D + 2 DV): 2 G (8 D + 6 DV) for the round.
+BLK_FLOPS = {"slice_fwd": lambda D, DV: D + DV, "deslice_fwd": lambda D, DV: D + DV,
+             "deslice_bwd": lambda D, DV: 3 * D + 2 * DV,
+             "slice_bwd": lambda D, DV: 3 * D + 2 * DV}
+
+
 # --------------------------------------------------------------------------- clocks
 
 class ClockSampler:
@@ -603,29 +647,47 @@ def main():
 
     # per-op device times of the same round, for the roofline
     dot = K.slice_ops._dot_mode(x)
-    opt = op_timings(K, x, fx, W, b, tau, r, dot)
-    elem = x.element_size()
-    unit_bytes = cfg["B"] * n_local * cfg["H"] * cfg["D"] * elem
-    top = max(opt, key=opt.get)
     peaks = {}
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
             peaks = json.load(f)
     except (OSError, ValueError):
         pass
-    peak = peaks.get("hbm_gbs")
-    peak_src = "measured" if peak else "fallback"
-    peak = peak or 6650.0
-    algo = UNITS[top] * unit_bytes
-    achieved = algo / (opt[top] * 1e-3) / 1e9
-    round_bytes = sum(UNITS.values()) * unit_bytes
-    roofline = {"bound": "hbm", "kernel": top, "achieved": round(achieved, 1),
-                "peak": peak, "peak_source": peak_src, "unit": "GB/s",
-                "frac": round(achieved / peak, 4),
-                "traffic": profile_traffic(KERNEL_OF[top], cfg["B"] * n_local * cfg["H"]),
-                "algorithmic_bytes_per_launch": algo,
-                "op_ms": {k: round(v, 4) for k, v in opt.items()},
-                "round_frac": round(round_bytes / (ms * 1e-3) / 1e9 / peak, 4)}
+    elem = x.element_size()
+    unit_bytes = cfg["B"] * n_local * cfg["H"] * cfg["D"] * elem
+    if K.slice_ops._use_blocked(cfg["D"], cfg["G"], cfg["DV"], dot, x.device):
+        # the blocked family (G > 32): dots of 2 G (8 D + 6 DV) flops a
+        # point-head, bound by the tensor cores (bf16) or the FMA pipes
+        opt = op_timings_blocked(x, fx, W, b, tau, r, dot)
+        top = max(opt, key=opt.get)
+        heads = cfg["B"] * n_local * cfg["H"]
+        flops = {k: 2 * cfg["G"] * f(cfg["D"], cfg["DV"]) * heads for k, f in BLK_FLOPS.items()}
+        peak = peaks.get("bf16_tflops")
+        peak_src = "measured (cuBLAS bf16, burst)" if peak else "fallback"
+        peak = peak or 1590.0
+        achieved = flops[top] / (opt[top] * 1e-3) / 1e12
+        roofline = {"bound": "tensor", "kernel": top, "achieved": round(achieved, 2),
+                    "peak": peak, "peak_source": peak_src, "unit": "TFLOP/s",
+                    "frac": round(achieved / peak, 4), "traffic": None,
+                    "algorithmic_flops_per_launch": flops[top],
+                    "op_ms": {k: round(v, 4) for k, v in opt.items()},
+                    "round_frac": round(sum(flops.values()) / (ms * 1e-3) / 1e12 / peak, 4)}
+    else:
+        opt = op_timings(K, x, fx, W, b, tau, r, dot)
+        top = max(opt, key=opt.get)
+        peak = peaks.get("hbm_gbs")
+        peak_src = "measured" if peak else "fallback"
+        peak = peak or 6650.0
+        algo = UNITS[top] * unit_bytes
+        achieved = algo / (opt[top] * 1e-3) / 1e9
+        round_bytes = sum(UNITS.values()) * unit_bytes
+        roofline = {"bound": "hbm", "kernel": top, "achieved": round(achieved, 1),
+                    "peak": peak, "peak_source": peak_src, "unit": "GB/s",
+                    "frac": round(achieved / peak, 4),
+                    "traffic": profile_traffic(KERNEL_OF[top], cfg["B"] * n_local * cfg["H"]),
+                    "algorithmic_bytes_per_launch": algo,
+                    "op_ms": {k: round(v, 4) for k, v in opt.items()},
+                    "round_frac": round(round_bytes / (ms * 1e-3) / 1e9 / peak, 4)}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:

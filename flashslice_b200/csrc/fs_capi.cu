@@ -141,7 +141,7 @@ bool blk_tc_params(const fs_problem& p, const fs_tensor4* x, const fs_tensor4* v
   q = tcx::TcParams();
   q.pdt = 1;
   if (!tcx::make_point_map(&q.mx, x->data, p.B, p.N, p.H, x->stride, 2, (int)p.D) ||
-      !tcx::make_point_map(&q.mv, v->data, p.B, p.N, p.H, v->stride, 2, (int)p.DV))
+      (v && !tcx::make_point_map(&q.mv, v->data, p.B, p.N, p.H, v->stride, 2, (int)p.DV)))
     return false;
   q.status = tcx::device_status();
   if (!q.status) return false;
@@ -167,6 +167,11 @@ bool blk_tc_params(const fs_problem& p, const fs_tensor4* x, const fs_tensor4* v
   q.sbh = p.b_heads > 1 ? p.G : 0;
   return true;
 }
+
+// CTAs per (b, h) of the blocked point-owning tensor-core kernels: one per
+// SM over all (b, h), within the dtau partial buffer (s.Pn per (b, h)).
+struct Setup;
+int pown_P(const fs_problem& p, const Setup& s);
 
 // Fill the tensor-core parameters; false when a tensor map cannot be made
 // (the FMA kernels then serve the call).
@@ -224,7 +229,16 @@ struct Setup {
   int nt, ntiles, ngb, Pn, Pg, BH;
   bool internal_stats;
   size_t stats, delta, partA, partB, partS, partDt, total;
+  bool has_img;  // operand images of the blocked point-owning tensor-core kernels
+  size_t img;
 };
+
+int pown_P(const fs_problem& p, const Setup& s) {
+  int64_t P = kSmCount / ((int64_t)p.B * p.H);
+  if (P > s.Pn) P = s.Pn;
+  if (P > s.ntiles) P = s.ntiles;
+  return (int)(P < 1 ? 1 : P);
+}
 
 Setup setup(int op, const fs_problem& p) {
   Setup s = {};
@@ -285,6 +299,12 @@ Setup setup(int op, const fs_problem& p) {
       break;
   }
   if (s.internal_stats) s.stats = take(BH * 2 * p.N);
+  if (!s.fused && blk_tc_shape(p) &&
+      (op == FS_OP_SLICE_FWD || op == FS_OP_DESLICE_FWD || op == FS_OP_SLICE_BWD ||
+       op == FS_OP_DESLICE_BWD)) {
+    s.has_img = true;
+    s.img = take(BH * (G / 128) * (int64_t)tcx::blk_image_bytes(DV) / 4);
+  }
   s.total = off;
   return s;
 }
@@ -353,8 +373,24 @@ int launch_kind(Kind k, const fs_problem& p, const Setup& s, Params q, int& P, c
   return FS_OK;
 }
 
+// The per-point statistics: on the tensor cores when the shape allows and
+// the op's workspace holds operand images, else on the FMA engine.
 int run_stats(const fs_problem& p, const Setup& s, const fs_tensor4* x, const float* W,
-              const float* bias, const float* tau, float* dst, cudaStream_t st) {
+              const float* bias, const float* tau, float* dst, cudaStream_t st,
+              void* workspace = nullptr) {
+  tcx::TcParams tn;
+  if (workspace && s.has_img && tc_tensor_ok(x) &&
+      blk_tc_params(p, x, nullptr, W, bias, tau, nullptr, s.Pn, tn)) {
+    tn.M = nullptr;
+    tn.ds = nullptr;
+    tn.img = (uint8_t*)at(workspace, s.img);
+    tn.stats_out = dst;
+    tn.P = pown_P(p, s);
+    route_note("stats", "tensor-core-blocked", p, x, x);
+    FS_TRY(tcx::run_tc(tcx::TcKind::BlkImage, tn, st));
+    FS_TRY(tcx::run_tc(tcx::TcKind::BlkStats, tn, st));
+    return FS_OK;
+  }
   Params q = base_params(p, s, W, bias, tau);
   q.x = pt(x);
   q.stats_out = dst;
@@ -540,7 +576,7 @@ int fs_slice_fwd(const fs_problem* p, const fs_tensor4* x_mid, const fs_tensor4*
     const float* stats = stats_in;
     if (!stats) {
       float* dst = s.internal_stats ? at(workspace, s.stats) : stats_out;
-      FS_CHECK(run_stats(*p, s, x_mid, weight, bias, tau, dst, st));
+      FS_CHECK(run_stats(*p, s, x_mid, weight, bias, tau, dst, st, workspace));
       stats = dst;
     }
     q.stats_in = stats;
@@ -596,21 +632,41 @@ int fs_deslice_fwd(const fs_problem* p, const fs_tensor4* x_mid, const float* we
     return FS_OK;
   }
   if (p->row_splits) return ragged_unsupported("deslice forward");
-  route_note("deslice_fwd", s.fused ? "fma-fused" : "fma-blocked", *p, x_mid, out);
   int P = s.Pn;  // no partials: any count serves
-  if (s.fused) return launch_kind(Kind::FusedDesliceFwd, *p, s, q, P, st);
-  if (stats_in) {
-    q.stats_in = stats_in;
+  // the blocked deslice with statistics: point-owning tensor-core kernel when
+  // the shape allows, else the FMA kernel
+  auto with_stats = [&](const float* stats) -> int {
+    tcx::TcParams tn;
+    if (s.has_img && tc_tensor_ok(x_mid) && tc_tensor_ok(out) &&
+        blk_tc_params(*p, x_mid, out, weight, bias, tau, stats, s.Pn, tn)) {
+      tn.M = tokens;
+      tn.ds = nullptr;
+      tn.img = (uint8_t*)at(workspace, s.img);
+      tn.out = out->data;
+      for (int i = 0; i < 4; ++i) tn.so[i] = out->stride[i];
+      tn.P = pown_P(*p, s);
+      route_note("deslice_fwd", "tensor-core-blocked", *p, x_mid, out);
+      FS_TRY(tcx::run_tc(tcx::TcKind::BlkImage, tn, st));
+      FS_TRY(tcx::run_tc(tcx::TcKind::BlkDesliceFwd, tn, st));
+      return FS_OK;
+    }
+    route_note("deslice_fwd", "fma-blocked", *p, x_mid, out);
+    q.stats_in = stats;
     return launch_kind(Kind::DesliceFwdStats, *p, s, q, P, st);
+  };
+  if (s.fused) {
+    route_note("deslice_fwd", "fma-fused", *p, x_mid, out);
+    return launch_kind(Kind::FusedDesliceFwd, *p, s, q, P, st);
   }
+  if (stats_in) return with_stats(stats_in);
   float* dst = s.internal_stats ? at(workspace, s.stats) : stats_out;
   if (p->stats_mode == 0) {
+    route_note("deslice_fwd", "fma-blocked", *p, x_mid, out);
     q.stats_out = dst;
     return launch_kind(Kind::DesliceFwdOnline, *p, s, q, P, st);
   }
-  FS_CHECK(run_stats(*p, s, x_mid, weight, bias, tau, dst, st));
-  q.stats_in = dst;
-  return launch_kind(Kind::DesliceFwdStats, *p, s, q, P, st);
+  FS_CHECK(run_stats(*p, s, x_mid, weight, bias, tau, dst, st, workspace));
+  return with_stats(dst);
 }
 
 static int bwd_common(bool slice, const fs_problem* p, const fs_tensor4* x_mid,
@@ -691,15 +747,36 @@ static int bwd_common(bool slice, const fs_problem* p, const fs_tensor4* x_mid,
     const float* stats = stats_in;
     if (!stats) {
       float* dst = at(workspace, s.stats);
-      FS_CHECK(run_stats(*p, s, x_mid, weight, bias, tau, dst, st));
+      FS_CHECK(run_stats(*p, s, x_mid, weight, bias, tau, dst, st, workspace));
       stats = dst;
     }
     q.stats_in = stats;
     q.delta = at(workspace, s.delta);
-    FS_CHECK(launch_kind(slice ? Kind::SliceBwdN : Kind::DesliceBwdN, *p, s, q, Pdt, st));
     tcx::TcParams tb;
-    if (blk_tc_shape(*p) && tc_tensor_ok(x_mid) && tc_tensor_ok(vals) &&
-        blk_tc_params(*p, x_mid, vals, weight, bias, tau, stats, s.Pg, tb, 1)) {
+    const bool blk_tc = blk_tc_shape(*p) && tc_tensor_ok(x_mid) && tc_tensor_ok(vals) &&
+                        blk_tc_params(*p, x_mid, vals, weight, bias, tau, stats, s.Pg, tb, 1);
+    if (blk_tc && s.has_img && tc_tensor_ok(dx) && (!slice || tc_tensor_ok(dfx))) {
+      tcx::TcParams tn = tb;
+      tn.M = mat;
+      tn.ds = slice ? ds : nullptr;
+      tn.delta = q.delta;
+      tn.img = (uint8_t*)at(workspace, s.img);
+      tn.out = dx->data;
+      for (int i = 0; i < 4; ++i) tn.so[i] = dx->stride[i];
+      if (slice) {
+        tn.out2 = dfx->data;
+        for (int i = 0; i < 4; ++i) tn.so2[i] = dfx->stride[i];
+      }
+      tn.partDt = q.partDt;
+      tn.P = Pdt = pown_P(*p, s);
+      route_note(slice ? "slice_bwd (point-owning)" : "deslice_bwd (point-owning)",
+                 "tensor-core-blocked", *p, x_mid, vals);
+      FS_TRY(tcx::run_tc(tcx::TcKind::BlkImage, tn, st));
+      FS_TRY(tcx::run_tc(slice ? tcx::TcKind::BlkSliceBwdN : tcx::TcKind::BlkDesliceBwdN, tn, st));
+    } else {
+      FS_CHECK(launch_kind(slice ? Kind::SliceBwdN : Kind::DesliceBwdN, *p, s, q, Pdt, st));
+    }
+    if (blk_tc) {
       tb.M = mat;
       tb.ds = ds;
       tb.delta = q.delta;

@@ -88,6 +88,18 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, i
       : "memory");
 }
 
+// Contiguous global -> shared copy of `bytes` (a multiple of 16; both
+// addresses 16-byte aligned), completing that many bytes of transaction
+// count on `bar`.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_u32(dst)),
+      "l"((uint64_t)src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // generic-proxy shared-memory writes -> visible to the async proxy (MMA, TMA)
 __device__ __forceinline__ void fence_async_shared() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -206,6 +218,12 @@ __device__ __forceinline__ void split3(float x, __nv_bfloat16& h, __nv_bfloat16&
   m = __float2bfloat16_rn(r1);
   const float r2 = r1 - __bfloat162float(m);
   l = __float2bfloat16_rn(r2);
+}
+
+// x = hi + mid + r, |r| <= 2^-17 |x|: two bf16 parts carry 16 significant bits
+__device__ __forceinline__ void split2(float x, __nv_bfloat16& h, __nv_bfloat16& m) {
+  h = __float2bfloat16_rn(x);
+  m = __float2bfloat16_rn(x - __bfloat162float(h));
 }
 
 }  // namespace tc

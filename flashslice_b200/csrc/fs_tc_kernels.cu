@@ -1477,19 +1477,19 @@ __global__ void __launch_bounds__(128 * kTCoupledBwd, kCtasCoupledBwd)
 // for bf16 point tensors in the bf16 dot mode, D = 32, DV in {32, 64}, G a
 // multiple of 128, with the per-point statistics (m, l) given. One CTA owns
 // 128 slots of one (b, h) and streams the points:
-//  * logits = x W^T on the tensor cores, exact: the bf16 x times W's three
-//    bf16 parts (six MMAs, N = 128), so that they match the statistics'
-//    fp32 logits;
+//  * logits = x W^T on the tensor cores: the bf16 x times W's two bf16 parts
+//    (hi, mid: 16 significant bits, four MMAs, N = 128), within 2^-17 of the
+//    fp32 logits the statistics are formed from;
 //  * w = exp(logit - m) / l per point, rounded to bf16 (the bf16 dot mode's
 //    value dot, blocked.py), written as the pool's slot-major operand;
 //  * z_num += w^T fx and s += w^T 1 (MMAs with N = DV and N = 16) accumulate
 //    in TMEM over the CTA's tiles.
 // Point tiles arrive by TMA as 16-byte column boxes, which lays them out as
 // the MMAs' operands directly (x K-major, fx point-major), double-buffered.
-// smem: [W parts x 3 (24 KB)][bias][x stage x 2][fx stage x 2][w tile][ones][bars]
+// smem: [W parts x 2 (16 KB)][bias][x stage x 2][fx stage x 2][w tile][ones][bars]
 // TMEM: logits at 0 (128 columns), z_num at 128 (DV), s at 192 (16).
 constexpr int kBgSlots = 128;
-constexpr int kBgWs = 0, kBgBias = 3 * 8192, kBgX = kBgBias + 1024, kBgF = kBgX + 2 * 8192,
+constexpr int kBgWs = 0, kBgBias = 2 * 8192, kBgX = kBgBias + 1024, kBgF = kBgX + 2 * 8192,
               kBgW = kBgF + 2 * 16384, kBgOnes = kBgW + 32768, kBgBar = kBgOnes + 4096,
               kBgBytes = kBgBar + kBarBytes;
 static_assert(kBgX % 1024 == 0 && kBgF % 1024 == 0 && kBgW % 1024 == 0, "blocked slice layout");
@@ -1501,17 +1501,16 @@ __global__ void __launch_bounds__(128, 2) k_tc_blk_slice_fwd_bf16(const __grid_c
   const int g0 = gb * kBgSlots, DV = p.dv;
   const Span sp = span_of(p, b);
   Ctl c = prologue_begin<256>(sm, kBgBar);
-  // W rows g0 .. g0 + 127, three bf16 parts, K-major (rows g, k = d) at +8 KB p
+  // W rows g0 .. g0 + 127, two bf16 parts (mid, hi), K-major (rows g, k = d)
   {
     const float* Wb = p.W + (int64_t)b * p.swb + (int64_t)h * p.swh + (int64_t)g0 * 32;
     for (int i = threadIdx.x; i < kBgSlots * 32; i += 128) {
       const int r = i >> 5, k = i & 31;
-      __nv_bfloat16 hi, mi, lo;
-      split3(Wb[i], hi, mi, lo);
+      __nv_bfloat16 hi, mi;
+      split2(Wb[i], hi, mi);
       const uint32_t o = kmajor_off(r, k, 32);
-      *(__nv_bfloat16*)(sm + kBgWs + o) = lo;
-      *(__nv_bfloat16*)(sm + kBgWs + 8192 + o) = mi;
-      *(__nv_bfloat16*)(sm + kBgWs + 16384 + o) = hi;
+      *(__nv_bfloat16*)(sm + kBgWs + o) = mi;
+      *(__nv_bfloat16*)(sm + kBgWs + 8192 + o) = hi;
     }
     const float inv_tau = __frcp_rn(p.tau[h]);
     float* bias2 = (float*)(sm + kBgBias);
@@ -1543,8 +1542,8 @@ __global__ void __launch_bounds__(128, 2) k_tc_blk_slice_fwd_bf16(const __grid_c
   for (int k = 0; k < n_my; ++k) {
     const int tile = blockIdx.x + k * p.P, n0 = tile * kTile;
     wait_bar(c, kBarTma, p.status);
-    if (threadIdx.x == 0) {  // logits: x times W lo, mid, hi (small first)
-      for (int part = 0; part < 3; ++part)
+    if (threadIdx.x == 0) {  // logits: x times W mid, hi (small first)
+      for (int part = 0; part < 2; ++part)
         for (int ks = 0; ks < 2; ++ks)
           mma_bf16(tL, smem_desc(smem_u32(xs(k)) + ks * 4096, 2048, 128),
                    smem_desc(smem_u32(sm + kBgWs + part * 8192) + ks * 256, 128, 512), id_l,
@@ -1627,8 +1626,9 @@ __global__ void __launch_bounds__(128, 2) k_tc_blk_slice_fwd_bf16(const __grid_c
 // statistics and the point-owning pass's delta and row sums. One CTA owns 128
 // slots of one (b, h) and streams the points; per tile:
 //  * logits = x W^T and dw = v M^T (v = d_out with M = tokens, or v = fx with
-//    M = dz_num, plus ds), both exact on the tensor cores (W and M in three
-//    bf16 parts; the bf16 x and v are exact), N = 128;
+//    M = dz_num, plus ds) on the tensor cores, W and M in two bf16 parts (16
+//    significant bits; the bf16 x and v are exact), N = 128: the products
+//    the point-owning kernels form;
 //  * w = exp(logit - m) / l, dl = w (dw - delta) / tau, written as bf16
 //    slot-major operands (the bf16 value dots);
 //  * dW += dl^T x, db += dl^T 1 and, deslice, dtokens += w^T d_out,
@@ -1636,7 +1636,7 @@ __global__ void __launch_bounds__(128, 2) k_tc_blk_slice_fwd_bf16(const __grid_c
 // Two threads per point row (64 slots each). One CTA per SM (TMEM).
 // smem: [W parts][M parts][bias][ds][x stage x 2][v stage x 2][dl tile][w tile][ones][bars]
 // TMEM: logits 0, dw 128, dW 256 (32), db 288 (16), dtokens 320 (DV).
-constexpr int kBbW = 0, kBbM = 3 * 8192, kBbBias = kBbM + 3 * 16384, kBbDs = kBbBias + 512,
+constexpr int kBbW = 0, kBbM = 2 * 8192, kBbBias = kBbM + 2 * 16384, kBbDs = kBbBias + 512,
               kBbX = kBbDs + 512 + 1024 - ((kBbDs + 512) % 1024), kBbV = kBbX + 2 * 8192,
               kBbDl = kBbV + 2 * 16384, kBbWt = kBbDl + 32768, kBbOnes = kBbWt + 32768,
               kBbBar = kBbOnes + 4096, kBbBytes = kBbBar + kBarBytes;
@@ -1652,26 +1652,25 @@ __global__ void __launch_bounds__(256, 1) k_tc_blk_bwd_g_bf16(const __grid_const
   Ctl c = prologue_begin<512>(sm, kBbBar);
   const float inv_tau = __frcp_rn(p.tau[h]);
   {
-    // W rows g0 .. g0 + 127 (K = d, 32) and M rows (K = dv) in three bf16 parts
+    // W rows g0 .. g0 + 127 (K = d, 32) and M rows (K = dv) in two bf16 parts
+    // (mid, hi)
     const float* Wb = p.W + (int64_t)b * p.swb + (int64_t)h * p.swh + (int64_t)g0 * 32;
     for (int i = threadIdx.x; i < kBgSlots * 32; i += 256) {
       const int r = i >> 5, k = i & 31;
-      __nv_bfloat16 hi, mi, lo;
-      split3(Wb[i], hi, mi, lo);
+      __nv_bfloat16 hi, mi;
+      split2(Wb[i], hi, mi);
       const uint32_t o = kmajor_off(r, k, 32);
-      *(__nv_bfloat16*)(sm + kBbW + o) = lo;
-      *(__nv_bfloat16*)(sm + kBbW + 8192 + o) = mi;
-      *(__nv_bfloat16*)(sm + kBbW + 16384 + o) = hi;
+      *(__nv_bfloat16*)(sm + kBbW + o) = mi;
+      *(__nv_bfloat16*)(sm + kBbW + 8192 + o) = hi;
     }
     const float* Mb = p.M + ((int64_t)bh * p.G + g0) * DV;
     for (int i = threadIdx.x; i < kBgSlots * DV; i += 256) {
       const int r = i / DV, k = i - r * DV;
-      __nv_bfloat16 hi, mi, lo;
-      split3(Mb[i], hi, mi, lo);
+      __nv_bfloat16 hi, mi;
+      split2(Mb[i], hi, mi);
       const uint32_t o = kmajor_off(r, k, DV);
-      *(__nv_bfloat16*)(sm + kBbM + o) = lo;
-      *(__nv_bfloat16*)(sm + kBbM + 16384 + o) = mi;
-      *(__nv_bfloat16*)(sm + kBbM + 32768 + o) = hi;
+      *(__nv_bfloat16*)(sm + kBbM + o) = mi;
+      *(__nv_bfloat16*)(sm + kBbM + 16384 + o) = hi;
     }
     if (threadIdx.x < kBgSlots) {
       float* bias2 = (float*)(sm + kBbBias);
@@ -1709,12 +1708,12 @@ __global__ void __launch_bounds__(256, 1) k_tc_blk_bwd_g_bf16(const __grid_const
     const int tile = blockIdx.x + k * p.P, n0 = tile * kTile;
     wait_bar(c, kBarTma, p.status);
     if (threadIdx.x == 0) {
-      for (int part = 0; part < 3; ++part)  // logits = x W^T (lo, mid, hi of W)
+      for (int part = 0; part < 2; ++part)  // logits = x W^T (mid, hi of W)
         for (int ks = 0; ks < 2; ++ks)
           mma_bf16(tL, smem_desc(smem_u32(xs(k)) + ks * 4096, 2048, 128),
                    smem_desc(smem_u32(sm + kBbW + part * 8192) + ks * 256, 128, 512), id_l,
                    (part | ks) != 0);
-      for (int part = 0; part < 3; ++part)  // dw = v M^T
+      for (int part = 0; part < 2; ++part)  // dw = v M^T (mid, hi of M)
         for (int ks = 0; ks < DV / 16; ++ks)
           mma_bf16(tD, smem_desc(smem_u32(vs(k)) + ks * 4096, 2048, 128),
                    smem_desc(smem_u32(sm + kBbM + part * 16384) + ks * 256, 128, DV * 16), id_l,
@@ -1814,6 +1813,333 @@ __global__ void __launch_bounds__(256, 1) k_tc_blk_bwd_g_bf16(const __grid_const
       if (!SLICE)
         for (int j = 0; j < DV; ++j) p.partB[(slot * p.G + g) * DV + j] = 0.f;
     }
+  }
+  epilogue<512>(c);
+}
+
+// ------------------------------------------------------------ blocked point-owning kernels, bf16 dots
+// Operand image of one (b, h, 128-slot block) for the point-owning kernels,
+// written once per call by k_tc_blk_image and copied into shared memory by
+// one bulk copy wherever a kernel walks that block:
+//   [bias log2(e) / tau, 128 floats][ds, 128 floats (zeros without ds)]
+//   [W mid][W hi]  128 x 32 bf16 each, K-major rows g (8 KB)
+//   [M hi][M mid]  128 x DV bf16 each, K-major rows g
+// W and M (tokens or dz_num) in two bf16 parts (16 significant bits); the hi
+// parts are also the value dots' bf16 operands, read MN-major. Without M
+// (p.M null, the statistics) the M parts are left unwritten.
+constexpr int kImBias = 0, kImDs = 512, kImW = 1024, kImM = kImW + 2 * 8192;
+__host__ __device__ constexpr int im_mpart(int dv) { return kBgSlots * dv * 2; }
+__host__ __device__ constexpr int im_bytes(int dv) { return kImM + 2 * im_mpart(dv); }
+static_assert(im_bytes(32) % 1024 == 0 && im_bytes(64) % 1024 == 0, "image alignment");
+
+__global__ void __launch_bounds__(256) k_tc_blk_image(const __grid_constant__ TcParams p) {
+  const int gb = blockIdx.x, bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
+  const int g0 = gb * kBgSlots, DV = p.dv, mp = im_mpart(DV);
+  uint8_t* im = p.img + ((int64_t)bh * (p.G / kBgSlots) + gb) * im_bytes(DV);
+  const float* Wb = p.W + (int64_t)b * p.swb + (int64_t)h * p.swh + (int64_t)g0 * 32;
+  for (int i = threadIdx.x; i < kBgSlots * 32; i += 256) {
+    const int r = i >> 5, k = i & 31;
+    __nv_bfloat16 hi, mi;
+    split2(Wb[i], hi, mi);
+    const uint32_t o = kmajor_off(r, k, 32);
+    *(__nv_bfloat16*)(im + kImW + o) = mi;
+    *(__nv_bfloat16*)(im + kImW + 8192 + o) = hi;
+  }
+  const float* Mb = p.M + ((int64_t)bh * p.G + g0) * DV;
+  for (int i = threadIdx.x; p.M && i < kBgSlots * DV; i += 256) {
+    const int r = i / DV, k = i - r * DV;
+    __nv_bfloat16 hi, mi;
+    split2(Mb[i], hi, mi);
+    const uint32_t o = kmajor_off(r, k, DV);
+    *(__nv_bfloat16*)(im + kImM + o) = hi;
+    *(__nv_bfloat16*)(im + kImM + mp + o) = mi;
+  }
+  if (threadIdx.x < kBgSlots) {
+    const float inv_tau = __frcp_rn(p.tau[h]);
+    const int g = g0 + threadIdx.x;
+    ((float*)(im + kImBias))[threadIdx.x] =
+        p.bias[(int64_t)b * p.sbb + (int64_t)h * p.sbh + g] * inv_tau * kLog2e;
+    ((float*)(im + kImDs))[threadIdx.x] = p.ds ? p.ds[(int64_t)bh * p.G + g] : 0.f;
+  }
+}
+
+// The point-owning kernels of the blocked family for bf16 point tensors in
+// the bf16 dot mode, D = 32, DV in {32, 64}, G a multiple of 128, given the
+// statistics (m, l), or forming them. A CTA owns a 128-point tile at a time
+// and walks the slot blocks, their operand images double-buffered:
+//  MODE 3, the statistics, two passes (blocked.py:350-400): m = max_g logit,
+//  then l = sum_g exp(logit - m) with m as its consumers read it;
+//  MODE 2, deslice forward (blocked.py:466-510): out = sum_g e tok / l;
+//  MODE 1, slice backward (blocked.py:577-673), and MODE 0, deslice backward
+//  (blocked.py:745-815): pass 1 forms the row sum l = sum_g e, delta =
+//  sum_g e dw / l (and, slice, dfx = sum_g e dz / l); pass 2 forms dl =
+//  (e dw - e delta) / l, dx = sum_g dl W / tau and the row's temperature
+//  term sum_g dl (logit - m), over all of G before it meets other rows.
+// logits = x W^T and dw = v M^T (+ ds) on the tensor cores with W and M in
+// two bf16 parts (x and v are bf16): within 2^-17 of the fp32 products, and
+// the very products the slot-owning kernels form; the value dots round e,
+// dl, tok, dz and W to bf16 (the bf16 dot mode, blocked.py). delta and l go
+// to the slot-owning kernels through p.delta.
+// Two threads per point row (64 slots each). One CTA per SM (TMEM, smem).
+// smem: [image x 3][x tile][v tile][e / dl tile][row exchange][bars]
+// TMEM: logits 0, dw 128, value accumulator 256 (DV), dx 320 (32).
+constexpr int kPnBufs = 3;  // operand images in flight: the walked one and two ahead
+constexpr int kPnIm = im_bytes(64), kPnX = kPnBufs * kPnIm, kPnV = kPnX + 8192, kPnE = kPnV + 16384,
+              kPnRed = kPnE + 32768, kPnBar = kPnRed + 3072, kPnBytes = kPnBar + kBarBytes;
+static_assert(kPnX % 1024 == 0 && kPnE % 1024 == 0, "point-owning layout");
+
+template <int MODE>
+__global__ void __launch_bounds__(256, 1) k_tc_blk_pown_bf16(const __grid_constant__ TcParams p) {
+  constexpr bool BWD = MODE <= 1, SLICE = MODE == 1, STATS = MODE == 3;
+  constexpr int NPASS = MODE == 2 ? 1 : 2;
+  extern __shared__ __align__(16) uint8_t sm_raw[];
+  uint8_t* sm = align_smem(sm_raw);
+  const int bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H, DV = p.dv, N = p.N;
+  const int nblk = p.G / kBgSlots, mp = im_mpart(DV);
+  const Span sp = span_of(p, b);
+  Ctl c = prologue_begin<512>(sm, kPnBar);
+  prologue_end(c);
+  const float inv_tau = __frcp_rn(p.tau[h]);
+  const float scale = inv_tau * kLog2e;
+  const uint32_t tL = c.tmem, tD = c.tmem + 128, tA = c.tmem + 256, tX = c.tmem + 320;
+  const int warp = threadIdx.x >> 5, row = 32 * (warp & 3) + (threadIdx.x & 31), half = warp >> 2;
+  const uint32_t tlane = (uint32_t)(32 * (warp & 3)) << 16;
+  const uint8_t* img_bh = p.img + (int64_t)bh * nblk * im_bytes(DV);
+  // the deslice forward reads W and M's hi part only, the statistics W only
+  const uint32_t im_copy = BWD ? (uint32_t)im_bytes(DV) : STATS ? (uint32_t)kImM : (uint32_t)(kImM + mp);
+  const uint32_t stage_b = (uint32_t)(BWD ? 4 + DV / 8 : 4) * 2048;
+  uint8_t* const xs = sm + kPnX;
+  uint8_t* const vs = sm + kPnV;
+  uint8_t* const et = sm + kPnE;
+  float* const red = (float*)(sm + kPnRed);
+  uint8_t* const etrow = et + (row >> 3) * 2048 + (row & 7) * 16;
+  auto imb = [&](int qb) { return sm + qb * kPnIm; };  // image buffer qb = q mod kPnBufs
+  auto load_tile = [&](int tile) {  // x (4 boxes) and, backward, v (DV / 8 boxes)
+    mbar_arrive_expect_tx(c.bar + kBarTma, stage_b);
+    for (int i = 0; i < 4; ++i)
+      tma_load_4d(xs + i * 2048, &p.mx, 8 * i, h, sp.row(tile), sp.bc, c.bar + kBarTma);
+    if (BWD)
+      for (int i = 0; i < DV / 8; ++i)
+        tma_load_4d(vs + i * 2048, &p.mv, 8 * i, h, sp.row(tile), sp.bc, c.bar + kBarTma);
+  };
+  auto load_image = [&](int qb, int j) {  // into buffer qb, slot block j's image
+    uint64_t* bar = c.bar + kG3 + qb;
+    mbar_arrive_expect_tx(bar, im_copy);
+    bulk_load(imb(qb), img_bh + (int64_t)j * im_bytes(DV), im_copy, bar);
+  };
+  const uint32_t id_l = idesc_bf16(128, 128, 0, 0);
+  const uint32_t id_a = idesc_bf16(128, DV == 64 ? 64 : 32, 0, 1), id_x = idesc_bf16(128, 32, 0, 1);
+  const int n_my = sp.ntiles > (int)blockIdx.x ? (sp.ntiles - 1 - (int)blockIdx.x) / p.P + 1 : 0;
+  const int nq = n_my * NPASS * nblk;
+  if (threadIdx.x == 0 && nq > 0) {
+    load_tile(blockIdx.x);
+    load_image(0, 0);
+    if (nq > 1) load_image(1, 1 % nblk);
+  }
+  float dt_acc = 0.f;
+  bool v_pending = false;  // value MMAs committed on kG2 and not yet waited for
+  int q = 0, qb = 0;  // block-pass, and its image buffer
+  static_assert(kPnBufs == 3 && kG3 + 2 == kG5, "one barrier per image buffer");
+  for (int k = 0; k < n_my; ++k) {
+    const int tile = blockIdx.x + k * p.P;
+    const int n = tile * kTile + row;
+    const bool valid = n < sp.N;
+    const int64_t ni = sp.n0 + n;
+    const int64_t sbase = (int64_t)bh * 2 * N;
+    float m2 = 0.f, inv_l = 0.f, delta = 0.f;
+    if (valid && !STATS) {
+      m2 = p.stats_in[sbase + ni] * kLog2e;
+      if (!BWD) inv_l = __frcp_rn(p.stats_in[sbase + N + ni]);
+    }
+    wait_bar(c, kBarTma, p.status);
+    for (int pass = 0; pass < NPASS; ++pass) {
+      // backward pass 0: row sum and sum e dw; pass 1: the temperature term;
+      // statistics pass 0: row max (m2 = 0), pass 1: row sum
+      float acc_l = STATS && pass == 0 ? -INFINITY : 0.f, acc_u = 0.f;
+      const bool value_mma = MODE == 2 || SLICE || (BWD && pass == 1);
+      for (int j = 0; j < nblk; ++j, ++q, qb = qb == kPnBufs - 1 ? 0 : qb + 1) {
+        const uint8_t* im = imb(qb);
+        // constant barrier indices keep the phase bits in registers
+        if (qb == 0)
+          wait_bar(c, kG3, p.status);
+        else if (qb == 1)
+          wait_bar(c, kG4, p.status);
+        else
+          wait_bar(c, kG5, p.status);
+        if (threadIdx.x == 0) {
+          // logits = x W^T and dw = v M^T, the small parts first
+          for (int part = 0; part < 2; ++part)  // W mid, hi
+            for (int ks = 0; ks < 2; ++ks)
+              mma_bf16(tL, smem_desc(smem_u32(xs) + ks * 4096, 2048, 128),
+                       smem_desc(smem_u32(im + kImW + part * 8192) + ks * 256, 128, 512), id_l,
+                       (part | ks) != 0);
+          if (BWD)
+            for (int pi = 0; pi < 2; ++pi)  // M mid, hi
+              for (int ks = 0; ks < DV / 16; ++ks)
+                mma_bf16(tD, smem_desc(smem_u32(vs) + ks * 4096, 2048, 128),
+                         smem_desc(smem_u32(im + kImM + (1 - pi) * mp) + ks * 256, 128, DV * 16),
+                         id_l, (pi | ks) != 0);
+          commit(c, kG1);
+        }
+        if (v_pending) {  // block-pass q - 1's value MMAs: the e tile and its image buffer free
+          wait_bar(c, kG2, p.status);
+          v_pending = false;
+        }
+        // two block-passes ahead, into block-pass q - 1's buffer
+        if (threadIdx.x == 0 && q + 2 < nq)
+          load_image(qb == 0 ? kPnBufs - 1 : qb - 1, (j + 2) % nblk);
+        wait_bar(c, kG1, p.status);
+        // The tile's last products have read x and v: fetch the next tile's.
+        // Every thread must have waited for this tile's phase of the TMA
+        // barrier first (else a lagging thread would see it two phases on):
+        // a barrier of an earlier block-pass of the tile guarantees it, and
+        // with one block-pass a tile, the barrier below.
+        const bool next_tile = j == nblk - 1 && pass == NPASS - 1 && k + 1 < n_my;
+        if (threadIdx.x == 0 && next_tile && nblk * NPASS > 1) load_tile(tile + p.P);
+        const float* bias2 = (const float*)(im + kImBias);
+        const float* dss = (const float*)(im + kImDs);
+#pragma unroll
+        for (int ch = 0; ch < 2; ++ch) {
+          const int c0 = half * 64 + ch * 32;
+          uint32_t lr[32], dr[32];
+          tld<32>(tL + tlane + c0, lr);
+          if (BWD) tld<32>(tD + tlane + c0, dr);
+          tld_wait();
+          float va[32], vb[32];
+          uint32_t e2[16];
+#pragma unroll
+          for (int jj = 0; jj < 16; ++jj) {
+            float ov[2];
+#pragma unroll
+            for (int s2 = 0; s2 < 2; ++s2) {
+              const int i = 2 * jj + s2, g = c0 + i;
+              const float t2 = __uint_as_float(lr[i]) * scale + bias2[g] - m2;
+              const float e = valid ? ex2(t2) : 0.f;
+              if (BWD) {
+                float dwg = __uint_as_float(dr[i]);
+                if (SLICE) dwg += dss[g];
+                if (pass == 0) {
+                  va[i] = e;
+                  vb[i] = e * dwg;
+                  ov[s2] = e;
+                } else {
+                  const float dl = (e * dwg - e * delta) * inv_l;
+                  vb[i] = dl * t2;
+                  ov[s2] = dl;
+                }
+              } else if (STATS) {
+                va[i] = pass == 0 ? t2 : e;
+              } else {
+                ov[s2] = e;
+              }
+            }
+            e2[jj] = bf2_bits(__floats2bfloat162_rn(ov[0], ov[1]));
+          }
+          if (BWD) {
+            if (pass == 0) acc_l += tree_sum2(va);
+            acc_u += tree_sum2(vb);
+          }
+          if (STATS) {
+            if (pass == 0) {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) acc_l = fmaxf(acc_l, va[i]);
+            } else {
+              acc_l += tree_sum2(va);
+            }
+          }
+          if (value_mma) {
+#pragma unroll
+            for (int i4 = 0; i4 < 4; ++i4)  // slots c0 + 8 i4 .. + 7: one 16-byte chunk
+              *(uint4*)(etrow + ((c0 >> 3) + i4) * 128) =
+                  make_uint4(e2[4 * i4], e2[4 * i4 + 1], e2[4 * i4 + 2], e2[4 * i4 + 3]);
+          }
+        }
+        to_async_barrier();
+        if (threadIdx.x == 0 && next_tile && nblk * NPASS == 1) load_tile(tile + p.P);
+        if (value_mma) {
+          if (threadIdx.x == 0) {
+            if (BWD && pass == 1) {  // dx += dl W (W hi, MN-major)
+              for (int ks = 0; ks < 8; ++ks)
+                mma_bf16(tX, smem_desc(smem_u32(et) + ks * 256, 128, 2048),
+                         smem_desc(smem_u32(im + kImW + 8192) + ks * 1024, 512, 128), id_x,
+                         (j | ks) != 0);
+            } else {  // dfx += e dz or out += e tok (M hi, MN-major)
+              for (int ks = 0; ks < 8; ++ks)
+                mma_bf16(tA, smem_desc(smem_u32(et) + ks * 256, 128, 2048),
+                         smem_desc(smem_u32(im + kImM) + ks * 2 * DV * 16, DV * 16, 128), id_a,
+                         (j | ks) != 0);
+            }
+            commit(c, kG2);
+          }
+          v_pending = true;
+        }
+      }
+      // ---- end of a pass
+      if (STATS) {
+        red[half * 128 + row] = acc_l;
+        __syncthreads();
+        if (pass == 0) {
+          // m in the logits' units, and on the log2 scale as its readers form it
+          const float m = fmaxf(red[row], red[128 + row]) * kLn2;
+          m2 = m * kLog2e;
+          if (half == 0 && valid) p.stats_out[sbase + ni] = m;
+        } else if (half == 0 && valid) {
+          p.stats_out[sbase + N + ni] = red[row] + red[128 + row];
+        }
+      }
+      if (BWD) {
+        red[(0 + half) * 128 + row] = acc_l;
+        red[(2 + half) * 128 + row] = acc_u;
+        __syncthreads();
+        if (pass == 0) {
+          const float lrow = red[row] + red[128 + row];
+          const float sdw = red[256 + row] + red[384 + row];
+          inv_l = valid ? __frcp_rn(lrow) : 0.f;
+          delta = sdw * inv_l;
+          if (half == 0 && valid) {
+            p.delta[sbase + ni] = delta;
+            p.delta[sbase + N + ni] = lrow;
+          }
+        } else if (half == 0 && valid) {
+          dt_acc += red[256 + row] + red[384 + row];
+        }
+      }
+      const bool store = MODE == 2 || (BWD && (SLICE || pass == 1));
+      if (store) {
+        if (v_pending) {
+          wait_bar(c, kG2, p.status);
+          v_pending = false;
+        }
+        // dx (16 columns a thread), dfx or out (DV / 2), 16 columns a read
+        const bool dxo = BWD && pass == 1;
+        const int w = dxo ? 16 : DV / 2, col = half * w;
+        const float f = dxo ? inv_tau : inv_l;
+        __nv_bfloat16* dst =
+            dxo || !SLICE
+                ? (__nv_bfloat16*)p.out + sp.bc * p.so[0] + ni * p.so[1] + h * p.so[2] + col
+                : (__nv_bfloat16*)p.out2 + sp.bc * p.so2[0] + ni * p.so2[1] + h * p.so2[2] + col;
+        for (int c16 = 0; c16 < w; c16 += 16) {
+          uint32_t r[16];
+          tld<16>((dxo ? tX : tA) + tlane + col + c16, r);
+          tld_wait();
+          uint32_t o[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            o[i] = bf2_bits(__floats2bfloat162_rn(__uint_as_float(r[2 * i]) * f,
+                                                  __uint_as_float(r[2 * i + 1]) * f));
+          if (valid) {
+            *(uint4*)(dst + c16) = make_uint4(o[0], o[1], o[2], o[3]);
+            *(uint4*)(dst + c16 + 8) = make_uint4(o[4], o[5], o[6], o[7]);
+          }
+        }
+        // the next MMAs into these columns follow a barrier after these reads
+      }
+    }
+  }
+  if (v_pending) wait_bar(c, kG2, p.status);
+  if (BWD) {
+    const float tot = cta_sum_nt<256>(dt_acc, red);
+    if (threadIdx.x == 0) p.partDt[(int64_t)bh * p.P + blockIdx.x] = -inv_tau * tot * kLn2;
   }
   epilogue<512>(c);
 }
@@ -1942,6 +2268,29 @@ cudaError_t run_tc(TcKind k, const TcParams& p, cudaStream_t s) {
       else
         k_tc_blk_bwd_g_bf16<false><<<grid, 256, kBbBytes + kSmemPad, s>>>(p);
     }
+  } else if (k == TcKind::BlkImage) {
+    k_tc_blk_image<<<dim3(p.G / kBgSlots, p.B * p.H), 256, 0, s>>>(p);
+    e = cudaSuccess;
+  } else if (k == TcKind::BlkSliceBwdN || k == TcKind::BlkDesliceBwdN ||
+             k == TcKind::BlkDesliceFwd || k == TcKind::BlkStats) {
+    const int mode = k == TcKind::BlkDesliceBwdN ? 0
+                     : k == TcKind::BlkSliceBwdN ? 1
+                     : k == TcKind::BlkDesliceFwd ? 2
+                                                  : 3;
+    const void* fns[4] = {(const void*)k_tc_blk_pown_bf16<0>, (const void*)k_tc_blk_pown_bf16<1>,
+                          (const void*)k_tc_blk_pown_bf16<2>, (const void*)k_tc_blk_pown_bf16<3>};
+    e = set_smem(fns[mode], kPnBytes + kSmemPad);
+    if (e == cudaSuccess) {
+      const dim3 grid(p.P, p.B * p.H);
+      if (mode == 0)
+        k_tc_blk_pown_bf16<0><<<grid, 256, kPnBytes + kSmemPad, s>>>(p);
+      else if (mode == 1)
+        k_tc_blk_pown_bf16<1><<<grid, 256, kPnBytes + kSmemPad, s>>>(p);
+      else if (mode == 2)
+        k_tc_blk_pown_bf16<2><<<grid, 256, kPnBytes + kSmemPad, s>>>(p);
+      else
+        k_tc_blk_pown_bf16<3><<<grid, 256, kPnBytes + kSmemPad, s>>>(p);
+    }
   } else if (k == TcKind::BlkSliceFwd) {
     e = set_smem((const void*)k_tc_blk_slice_fwd_bf16, kBgBytes + kSmemPad);
     if (e == cudaSuccess)
@@ -1975,7 +2324,12 @@ int tc_ctas_per_sm(TcKind k) {
     case TcKind::CoupledBwd: return kCtasCoupledBwd;
     case TcKind::BlkSliceFwd: return 2;
     case TcKind::BlkSliceBwdG:
-    case TcKind::BlkDesliceBwdG: return 1;
+    case TcKind::BlkDesliceBwdG:
+    case TcKind::BlkImage:
+    case TcKind::BlkSliceBwdN:
+    case TcKind::BlkDesliceBwdN:
+    case TcKind::BlkDesliceFwd:
+    case TcKind::BlkStats: return 1;
   }
   return 1;
 }
@@ -1985,6 +2339,9 @@ int tc_ctas_per_sm(TcKind k) {
 static_assert((kSfBytes + kSmemPad + 1024) * kCtasSliceFwd <= 228 * 1024, "slice fwd smem");
 static_assert((kBgBytes + kSmemPad + 1024) * 2 <= 228 * 1024, "blocked slice fwd smem");
 static_assert(kBbBytes + kSmemPad + 1024 <= 228 * 1024, "blocked backward smem");
+static_assert(kPnBytes + kSmemPad + 1024 <= 228 * 1024, "blocked point-owning smem");
+static_assert(im_bytes(32) == blk_image_bytes(32) && im_bytes(64) == blk_image_bytes(64),
+              "operand image size");
 static_assert((kDfBytes + kSmemPad + 1024) * kCtasDesliceFwd <= 228 * 1024, "deslice fwd smem");
 static_assert((kSbBytes + kSmemPad + 1024) * kCtasSliceBwd <= 228 * 1024, "slice bwd smem");
 static_assert((kDbBytes + kSmemPad + 1024) * kCtasDesliceBwd <= 228 * 1024, "deslice bwd smem");

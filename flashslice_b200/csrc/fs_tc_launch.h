@@ -20,6 +20,11 @@ enum class TcKind {
   BlkSliceFwd,     // blocked slot-owning slice forward, bf16 dots
   BlkSliceBwdG,    // blocked slot-owning slice backward (dW, db), bf16 dots
   BlkDesliceBwdG,  // blocked slot-owning deslice backward (dW, db, dtokens), bf16 dots
+  BlkImage,        // per-(b, h, slot block) operand images of W, M, bias, ds (blocked)
+  BlkSliceBwdN,    // blocked point-owning slice backward (dfx, delta, dx, dtau), bf16 dots
+  BlkDesliceBwdN,  // blocked point-owning deslice backward (delta, dx, dtau), bf16 dots
+  BlkDesliceFwd,   // blocked point-owning deslice forward with statistics, bf16 dots
+  BlkStats,        // blocked per-point statistics (m, l), two passes, bf16 points
 };
 
 constexpr int kMaxSplits = 128;  // FS_MAX_SPLITS
@@ -32,7 +37,8 @@ struct TcParams {
   int pdt;  // point tensors' type: 0 fp32, 1 bf16 (tiles, outputs)
   int dv, G;              // the blocked slice forward's value width and slot count
   const float* stats_in;  // its per-point statistics (B, H, 2, N)
-  const float* delta;     // the blocked backward's per-point delta and row sum (B, H, 2, N)
+  float* stats_out;       // the statistics kernel's output, same layout
+  float* delta;           // the blocked backward's per-point delta and row sum (B, H, 2, N)
   const float* W;
   const float* bias;
   const float* tau;
@@ -48,6 +54,7 @@ struct TcParams {
   float* partB;
   float* partS;
   float* partDt;
+  uint8_t* img;     // blocked point-owning kernels: operand images, one per (b, h, slot block)
   int* status;      // device word: set to a non-zero code when a bounded wait gives up
   // ragged samples: nsplit = B > 0 and split[0 .. B] the row offsets of the
   // samples in the point tensors' single batch entry; 0 = dense
@@ -56,6 +63,10 @@ struct TcParams {
 };
 
 cudaError_t run_tc(TcKind k, const TcParams& p, cudaStream_t s);
+
+// Bytes of one operand image of the blocked point-owning kernels (one per
+// b, h and block of 128 slots), value width dv.
+constexpr int blk_image_bytes(int dv) { return 1024 + 2 * 8192 + 2 * 128 * dv * 2; }
 
 // one bounded wait that runs out (limit_ns), on `s`: sets the status word
 cudaError_t run_wait_selftest(uint64_t limit_ns, cudaStream_t s);

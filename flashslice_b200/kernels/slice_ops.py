@@ -698,11 +698,14 @@ def fused_coupling(x_mid, fx_mid, weight, bias, tau, mix=None, mix_params=None, 
         if group is not None:
             from ..sharded import sharded_coupling
             return sharded_coupling(x_mid, fx_mid, weight, bias, tau, mix, eps, group)
-        z, s = fused_slice(x_mid, fx_mid, weight, bias, tau)
+        # the slice's per-point statistics serve the deslice (blocked family;
+        # None on the single-tile path), as physics_attention.py:95-136 hands
+        # them over
+        z, s, st = fused_slice(x_mid, fx_mid, weight, bias, tau, return_stats=True)
         tok = z / (s + eps)[..., None]
         if mix is not None:
             tok = mix(tok)
-        return fused_deslice(x_mid, weight, bias, tau, tok)
+        return fused_deslice(x_mid, weight, bias, tau, tok, stats=st)
     return _CouplingRound.apply(x_mid, fx_mid, weight, bias, tau, eps, dot, mix, group,
                                 _ops if _ops is not None else torch.ops.flashslice, *params)
 

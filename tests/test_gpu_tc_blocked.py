@@ -1,7 +1,8 @@
-"""The blocked family's slot-owning slice forward on the tensor cores (bf16
-point tensors, bf16 dot mode, D = 32, DV = 32 or 64, G a multiple of 128)
-against the exact FMA kernels on the same inputs and statistics and against
-the float64 math (the reference's bf16 gate, 2e-2)."""
+"""The blocked family on the tensor cores (bf16 point tensors, bf16 dot
+mode, D = 32, DV = 32 or 64, G a multiple of 128): the slot-owning slice
+forward and backward halves, the point-owning deslice forward and backward
+halves, against the exact FMA kernels on the same inputs and statistics
+and against the float64 math (the reference's bf16 gate, 2e-2)."""
 
 import pytest
 import torch
@@ -46,7 +47,8 @@ def test_blocked_slice_on_tensor_cores(env, case):
     n0 = lib.fs_tc_launch_count()
     z, s, stats = K.fused_slice(x, fx, W, b, tau, return_stats=True)
     torch.cuda.synchronize()
-    assert lib.fs_tc_launch_count() - n0 == 1, "the tensor-core kernel did not run"
+    # the statistics (operand images, point-owning kernel), the slot-owning slice
+    assert lib.fs_tc_launch_count() - n0 == 3, "the tensor-core kernels did not run"
     st.set_engine("fma")
     try:
         ze, se = K.fused_slice(x, fx, W, b, tau, stats=stats)
@@ -95,8 +97,11 @@ def test_blocked_round_backward_on_tensor_cores(env, case):
 
     n0 = lib.fs_tc_launch_count()
     tc = round_("auto")
-    # the slot-owning slice forward, and the slot-owning halves of both backward ops
-    assert lib.fs_tc_launch_count() - n0 == 3
+    # the slice forward's statistics and slot-owning kernel, and each backward
+    # op's operand images, point-owning and slot-owning halves (the deslice
+    # forward, called here without statistics, forms them online on the FMA
+    # engine)
+    assert lib.fs_tc_launch_count() - n0 == 3 + 3 + 3
     ex = round_("fma")
     from oracle import eager_torch as E
     ref = E.coupling_round(*[t.detach().double().clone().requires_grad_(True)
@@ -106,4 +111,97 @@ def test_blocked_round_backward_on_tensor_cores(env, case):
         # the value dots moves it most (the reference's bf16 gate, 2e-2)
         assert relerr(a, e) <= (2e-2 if k == "grad:tau" else 1e-2), (k, relerr(a, e))
         assert relerr(a, ref[k]) <= 2e-2, (k, relerr(a, ref[k]))
+    assert lib.fs_device_status(1) == 0
+
+
+@pytest.mark.parametrize("case", [
+    dict(B=1, N=5000, H=4, DV=64, G=128, mode="hgd", bias=True),
+    dict(B=2, N=4097, H=2, DV=32, G=256, mode="bhgd", bias=False),
+    dict(B=1, N=77, H=4, DV=64, G=1024, mode="gd", bias=True),
+], ids=["g128-hgd", "g256-bhgd-dv32", "g1024-n77"])
+def test_blocked_deslice_forward_on_tensor_cores(env, case):
+    """The deslice forward with the slice's statistics handed in: the
+    point-owning tensor-core kernel against the FMA kernel on the same
+    statistics and the float64 math; repeated calls agree bitwise."""
+    K, st, lib = env
+    x, fx, W, b, tau = _inputs(**case)
+    g = torch.Generator().manual_seed(5)
+    tok = torch.randn(case["B"], case["H"], case["G"], case["DV"], generator=g).cuda()
+    _, _, stats = K.fused_slice(x, fx, W, b, tau, return_stats=True)
+    n0 = lib.fs_tc_launch_count()
+    out = K.fused_deslice(x, W, b, tau, tok, stats=stats)
+    torch.cuda.synchronize()
+    assert lib.fs_tc_launch_count() - n0 == 2, "the tensor-core kernels did not run"
+    assert out.dtype == torch.bfloat16
+    out2 = K.fused_deslice(x, W, b, tau, tok, stats=stats)
+    assert torch.equal(out, out2)
+    st.set_engine("fma")
+    try:
+        oe = K.fused_deslice(x, W, b, tau, tok, stats=stats)
+    finally:
+        st.set_engine("auto")
+    assert relerr(out, oe) <= 1e-2, relerr(out, oe)
+    from oracle import eager_torch as E
+    bb = b if b is not None else torch.zeros(W.shape[-2], device="cuda")
+    ot = E.deslice_fwd(x.double(), W.double(), bb.double(), tau.double(), tok.double())
+    assert relerr(out, ot) <= 2e-2, relerr(out, ot)
+    assert lib.fs_device_status(1) == 0
+
+
+@pytest.mark.parametrize("case", [
+    dict(B=1, N=5000, H=4, DV=64, G=128, mode="hgd", bias=True),
+    dict(B=2, N=4097, H=2, DV=32, G=1024, mode="bhgd", bias=False),
+], ids=["g128", "g1024-dv32"])
+def test_blocked_statistics_on_tensor_cores(env, case):
+    """The per-point statistics on the tensor cores (two passes; logits from
+    W in two bf16 parts, within 2^-17 of each product) against the FMA
+    engine's exact-fp32 ones: m and l to about 1e-5 relative, two to three
+    orders below the bf16 dot mode's own rounding."""
+    K, st, lib = env
+    x, fx, W, b, tau = _inputs(**case)
+    _, _, s_tc = K.fused_slice(x, fx, W, b, tau, return_stats=True)
+    st.set_engine("fma")
+    try:
+        _, _, s_fma = K.fused_slice(x, fx, W, b, tau, return_stats=True)
+    finally:
+        st.set_engine("auto")
+    m, mf = s_tc[:, :, 0], s_fma[:, :, 0]
+    assert float((m - mf).abs().max()) <= 1e-5 * (1 + float(mf.abs().max())), float((m - mf).abs().max())
+    l, lf = s_tc[:, :, 1], s_fma[:, :, 1]
+    assert float(((l - lf).abs() / lf).max()) <= 1e-4, float(((l - lf).abs() / lf).max())
+    assert lib.fs_device_status(1) == 0
+
+
+def test_blocked_coupling_round_on_tensor_cores(env):
+    """fused_coupling on the blocked family hands the slice's statistics to
+    the deslice (as the reference's layer does): every kernel of the round
+    on the tensor cores; values against the FMA engine's round."""
+    K, st, lib = env
+    case = dict(B=2, N=20_000, H=8, DV=64, G=1024, mode="bhgd", bias=False)
+    x, fx, W, b, tau = _inputs(**case)
+    g = torch.Generator().manual_seed(9)
+    up = torch.randn(x.shape[:3] + (64,), generator=g).bfloat16().cuda()
+    bb = torch.zeros(W.shape[-2], device="cuda")
+
+    def round_(engine):
+        st.set_engine(engine)
+        try:
+            L = [t.clone().requires_grad_(True) for t in (x, fx, W, bb, tau)]
+            out = K.fused_coupling(*L)
+            (out.float() * up.float()).sum().backward()
+            torch.cuda.synchronize()
+            return [out] + [t.grad for t in L]
+        finally:
+            st.set_engine("auto")
+
+    n0 = lib.fs_tc_launch_count()
+    tc = round_("auto")
+    # slice forward 3, deslice forward 2, the two backward ops 3 each
+    assert lib.fs_tc_launch_count() - n0 == 3 + 2 + 3 + 3
+    ex = round_("fma")
+    for a, e, k in zip(tc, ex, ("out", "grad:x", "grad:fx", "grad:W", "grad:b", "grad:tau")):
+        assert relerr(a, e) <= (2e-2 if k == "grad:tau" else 1e-2), (k, relerr(a, e))
+    tc2 = round_("auto")
+    for a, a2 in zip(tc, tc2):
+        assert torch.equal(a, a2)
     assert lib.fs_device_status(1) == 0
