@@ -168,7 +168,7 @@ bool blk_tc_params(const fs_problem& p, const fs_tensor4* x, const fs_tensor4* v
   return true;
 }
 
-// CTAs per (b, h) of the blocked point-owning tensor-core kernels: one per
+// CTAs per (b, h) of the blocked point-owning tensor-core kernels: two per
 // SM over all (b, h), within the dtau partial buffer (s.Pn per (b, h)).
 struct Setup;
 int pown_P(const fs_problem& p, const Setup& s);
@@ -234,7 +234,7 @@ struct Setup {
 };
 
 int pown_P(const fs_problem& p, const Setup& s) {
-  int64_t P = kSmCount / ((int64_t)p.B * p.H);
+  int64_t P = 2 * kSmCount / ((int64_t)p.B * p.H);
   if (P > s.Pn) P = s.Pn;
   if (P > s.ntiles) P = s.ntiles;
   return (int)(P < 1 ? 1 : P);
@@ -303,7 +303,7 @@ Setup setup(int op, const fs_problem& p) {
       (op == FS_OP_SLICE_FWD || op == FS_OP_DESLICE_FWD || op == FS_OP_SLICE_BWD ||
        op == FS_OP_DESLICE_BWD)) {
     s.has_img = true;
-    s.img = take(BH * (G / 128) * (int64_t)tcx::blk_image_bytes(DV) / 4);
+    s.img = take(BH * (G / 64) * (int64_t)tcx::blk_image_bytes(DV) / 4);
   }
   s.total = off;
   return s;

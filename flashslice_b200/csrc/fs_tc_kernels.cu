@@ -1818,35 +1818,36 @@ __global__ void __launch_bounds__(256, 1) k_tc_blk_bwd_g_bf16(const __grid_const
 }
 
 // ------------------------------------------------------------ blocked point-owning kernels, bf16 dots
-// Operand image of one (b, h, 128-slot block) for the point-owning kernels,
-// written once per call by k_tc_blk_image and copied into shared memory by
-// one bulk copy wherever a kernel walks that block:
-//   [bias log2(e) / tau, 128 floats][ds, 128 floats (zeros without ds)]
-//   [W mid][W hi]  128 x 32 bf16 each, K-major rows g (8 KB)
-//   [M hi][M mid]  128 x DV bf16 each, K-major rows g
+// Operand image of one (b, h, block of 64 slots) for the point-owning
+// kernels, written once per call by k_tc_blk_image and copied into shared
+// memory by one bulk copy wherever a kernel walks that block:
+//   [bias log2(e) / tau, 64 floats][ds, 64 floats (zeros without ds)]
+//   [W mid][W hi]  64 x 32 bf16 each, K-major rows g (4 KB)
+//   [M hi][M mid]  64 x DV bf16 each, K-major rows g
 // W and M (tokens or dz_num) in two bf16 parts (16 significant bits); the hi
 // parts are also the value dots' bf16 operands, read MN-major. Without M
 // (p.M null, the statistics) the M parts are left unwritten.
-constexpr int kImBias = 0, kImDs = 512, kImW = 1024, kImM = kImW + 2 * 8192;
-__host__ __device__ constexpr int im_mpart(int dv) { return kBgSlots * dv * 2; }
+constexpr int kPnSlots = 64;
+constexpr int kImBias = 0, kImDs = 256, kImW = 512, kImM = kImW + 2 * 4096;
+__host__ __device__ constexpr int im_mpart(int dv) { return kPnSlots * dv * 2; }
 __host__ __device__ constexpr int im_bytes(int dv) { return kImM + 2 * im_mpart(dv); }
-static_assert(im_bytes(32) % 1024 == 0 && im_bytes(64) % 1024 == 0, "image alignment");
+static_assert(im_bytes(32) % 16 == 0 && im_bytes(64) % 16 == 0, "image alignment");
 
 __global__ void __launch_bounds__(256) k_tc_blk_image(const __grid_constant__ TcParams p) {
   const int gb = blockIdx.x, bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
-  const int g0 = gb * kBgSlots, DV = p.dv, mp = im_mpart(DV);
-  uint8_t* im = p.img + ((int64_t)bh * (p.G / kBgSlots) + gb) * im_bytes(DV);
+  const int g0 = gb * kPnSlots, DV = p.dv, mp = im_mpart(DV);
+  uint8_t* im = p.img + ((int64_t)bh * (p.G / kPnSlots) + gb) * im_bytes(DV);
   const float* Wb = p.W + (int64_t)b * p.swb + (int64_t)h * p.swh + (int64_t)g0 * 32;
-  for (int i = threadIdx.x; i < kBgSlots * 32; i += 256) {
+  for (int i = threadIdx.x; i < kPnSlots * 32; i += 256) {
     const int r = i >> 5, k = i & 31;
     __nv_bfloat16 hi, mi;
     split2(Wb[i], hi, mi);
     const uint32_t o = kmajor_off(r, k, 32);
     *(__nv_bfloat16*)(im + kImW + o) = mi;
-    *(__nv_bfloat16*)(im + kImW + 8192 + o) = hi;
+    *(__nv_bfloat16*)(im + kImW + 4096 + o) = hi;
   }
   const float* Mb = p.M + ((int64_t)bh * p.G + g0) * DV;
-  for (int i = threadIdx.x; p.M && i < kBgSlots * DV; i += 256) {
+  for (int i = threadIdx.x; p.M && i < kPnSlots * DV; i += 256) {
     const int r = i / DV, k = i - r * DV;
     __nv_bfloat16 hi, mi;
     split2(Mb[i], hi, mi);
@@ -1854,7 +1855,7 @@ __global__ void __launch_bounds__(256) k_tc_blk_image(const __grid_constant__ Tc
     *(__nv_bfloat16*)(im + kImM + o) = hi;
     *(__nv_bfloat16*)(im + kImM + mp + o) = mi;
   }
-  if (threadIdx.x < kBgSlots) {
+  if (threadIdx.x < kPnSlots) {
     const float inv_tau = __frcp_rn(p.tau[h]);
     const int g = g0 + threadIdx.x;
     ((float*)(im + kImBias))[threadIdx.x] =
@@ -1866,7 +1867,7 @@ __global__ void __launch_bounds__(256) k_tc_blk_image(const __grid_constant__ Tc
 // The point-owning kernels of the blocked family for bf16 point tensors in
 // the bf16 dot mode, D = 32, DV in {32, 64}, G a multiple of 128, given the
 // statistics (m, l), or forming them. A CTA owns a 128-point tile at a time
-// and walks the slot blocks, their operand images double-buffered:
+// and walks the blocks of 64 slots, their operand images double-buffered:
 //  MODE 3, the statistics, two passes (blocked.py:350-400): m = max_g logit,
 //  then l = sum_g exp(logit - m) with m as its consumers read it;
 //  MODE 2, deslice forward (blocked.py:466-510): out = sum_g e tok / l;
@@ -1880,28 +1881,30 @@ __global__ void __launch_bounds__(256) k_tc_blk_image(const __grid_constant__ Tc
 // the very products the slot-owning kernels form; the value dots round e,
 // dl, tok, dz and W to bf16 (the bf16 dot mode, blocked.py). delta and l go
 // to the slot-owning kernels through p.delta.
-// Two threads per point row (64 slots each). One CTA per SM (TMEM, smem).
-// smem: [image x 3][x tile][v tile][e / dl tile][row exchange][bars]
-// TMEM: logits 0, dw 128, value accumulator 256 (DV), dx 320 (32).
-constexpr int kPnBufs = 3;  // operand images in flight: the walked one and two ahead
-constexpr int kPnIm = im_bytes(64), kPnX = kPnBufs * kPnIm, kPnV = kPnX + 8192, kPnE = kPnV + 16384,
-              kPnRed = kPnE + 32768, kPnBar = kPnRed + 3072, kPnBytes = kPnBar + kBarBytes;
-static_assert(kPnX % 1024 == 0 && kPnE % 1024 == 0, "point-owning layout");
+// Two threads per point row (32 slots each). Two CTAs per SM, so that one's
+// MMAs run while the other forms its rows.
+// smem: [image x 2][x tile][v tile][e / dl tile][row exchange][bars]
+// TMEM: logits 0, dw 64, the value accumulator (dfx or out, then dx) 128.
+constexpr int kPnIm = 25 * 1024;  // one image buffer (im_bytes(64) rounded up)
+constexpr int kPnX = 2 * kPnIm, kPnV = kPnX + 8192, kPnE = kPnV + 16384,
+              kPnRed = kPnE + 16384, kPnBar = kPnRed + 2048, kPnBytes = kPnBar + kBarBytes;
+static_assert(im_bytes(64) <= kPnIm && kPnX % 1024 == 0 && kPnE % 1024 == 0,
+              "point-owning layout");
 
 template <int MODE>
-__global__ void __launch_bounds__(256, 1) k_tc_blk_pown_bf16(const __grid_constant__ TcParams p) {
+__global__ void __launch_bounds__(256, 2) k_tc_blk_pown_bf16(const __grid_constant__ TcParams p) {
   constexpr bool BWD = MODE <= 1, SLICE = MODE == 1, STATS = MODE == 3;
   constexpr int NPASS = MODE == 2 ? 1 : 2;
   extern __shared__ __align__(16) uint8_t sm_raw[];
   uint8_t* sm = align_smem(sm_raw);
   const int bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H, DV = p.dv, N = p.N;
-  const int nblk = p.G / kBgSlots, mp = im_mpart(DV);
+  const int nblk = p.G / kPnSlots, mp = im_mpart(DV);
   const Span sp = span_of(p, b);
-  Ctl c = prologue_begin<512>(sm, kPnBar);
+  Ctl c = prologue_begin<256>(sm, kPnBar);
   prologue_end(c);
   const float inv_tau = __frcp_rn(p.tau[h]);
   const float scale = inv_tau * kLog2e;
-  const uint32_t tL = c.tmem, tD = c.tmem + 128, tA = c.tmem + 256, tX = c.tmem + 320;
+  const uint32_t tL = c.tmem, tD = c.tmem + 64, tA = c.tmem + 128;
   const int warp = threadIdx.x >> 5, row = 32 * (warp & 3) + (threadIdx.x & 31), half = warp >> 2;
   const uint32_t tlane = (uint32_t)(32 * (warp & 3)) << 16;
   const uint8_t* img_bh = p.img + (int64_t)bh * nblk * im_bytes(DV);
@@ -1912,8 +1915,7 @@ __global__ void __launch_bounds__(256, 1) k_tc_blk_pown_bf16(const __grid_consta
   uint8_t* const vs = sm + kPnV;
   uint8_t* const et = sm + kPnE;
   float* const red = (float*)(sm + kPnRed);
-  uint8_t* const etrow = et + (row >> 3) * 2048 + (row & 7) * 16;
-  auto imb = [&](int qb) { return sm + qb * kPnIm; };  // image buffer qb = q mod kPnBufs
+  uint8_t* const etrow = et + (row >> 3) * 1024 + (row & 7) * 16;
   auto load_tile = [&](int tile) {  // x (4 boxes) and, backward, v (DV / 8 boxes)
     mbar_arrive_expect_tx(c.bar + kBarTma, stage_b);
     for (int i = 0; i < 4; ++i)
@@ -1922,24 +1924,22 @@ __global__ void __launch_bounds__(256, 1) k_tc_blk_pown_bf16(const __grid_consta
       for (int i = 0; i < DV / 8; ++i)
         tma_load_4d(vs + i * 2048, &p.mv, 8 * i, h, sp.row(tile), sp.bc, c.bar + kBarTma);
   };
-  auto load_image = [&](int qb, int j) {  // into buffer qb, slot block j's image
-    uint64_t* bar = c.bar + kG3 + qb;
+  auto load_image = [&](int q, int j) {  // block-pass q walks slot block j
+    uint64_t* bar = c.bar + kG3 + (q & 1);
     mbar_arrive_expect_tx(bar, im_copy);
-    bulk_load(imb(qb), img_bh + (int64_t)j * im_bytes(DV), im_copy, bar);
+    bulk_load(sm + (q & 1) * kPnIm, img_bh + (int64_t)j * im_bytes(DV), im_copy, bar);
   };
-  const uint32_t id_l = idesc_bf16(128, 128, 0, 0);
+  const uint32_t id_l = idesc_bf16(128, kPnSlots, 0, 0);
   const uint32_t id_a = idesc_bf16(128, DV == 64 ? 64 : 32, 0, 1), id_x = idesc_bf16(128, 32, 0, 1);
   const int n_my = sp.ntiles > (int)blockIdx.x ? (sp.ntiles - 1 - (int)blockIdx.x) / p.P + 1 : 0;
   const int nq = n_my * NPASS * nblk;
   if (threadIdx.x == 0 && nq > 0) {
     load_tile(blockIdx.x);
     load_image(0, 0);
-    if (nq > 1) load_image(1, 1 % nblk);
   }
   float dt_acc = 0.f;
   bool v_pending = false;  // value MMAs committed on kG2 and not yet waited for
-  int q = 0, qb = 0;  // block-pass, and its image buffer
-  static_assert(kPnBufs == 3 && kG3 + 2 == kG5, "one barrier per image buffer");
+  int q = 0;
   for (int k = 0; k < n_my; ++k) {
     const int tile = blockIdx.x + k * p.P;
     const int n = tile * kTile + row;
@@ -1957,21 +1957,19 @@ __global__ void __launch_bounds__(256, 1) k_tc_blk_pown_bf16(const __grid_consta
       // statistics pass 0: row max (m2 = 0), pass 1: row sum
       float acc_l = STATS && pass == 0 ? -INFINITY : 0.f, acc_u = 0.f;
       const bool value_mma = MODE == 2 || SLICE || (BWD && pass == 1);
-      for (int j = 0; j < nblk; ++j, ++q, qb = qb == kPnBufs - 1 ? 0 : qb + 1) {
-        const uint8_t* im = imb(qb);
+      for (int j = 0; j < nblk; ++j, ++q) {
+        const uint8_t* im = sm + (q & 1) * kPnIm;
         // constant barrier indices keep the phase bits in registers
-        if (qb == 0)
-          wait_bar(c, kG3, p.status);
-        else if (qb == 1)
+        if (q & 1)
           wait_bar(c, kG4, p.status);
         else
-          wait_bar(c, kG5, p.status);
+          wait_bar(c, kG3, p.status);
         if (threadIdx.x == 0) {
           // logits = x W^T and dw = v M^T, the small parts first
           for (int part = 0; part < 2; ++part)  // W mid, hi
             for (int ks = 0; ks < 2; ++ks)
               mma_bf16(tL, smem_desc(smem_u32(xs) + ks * 4096, 2048, 128),
-                       smem_desc(smem_u32(im + kImW + part * 8192) + ks * 256, 128, 512), id_l,
+                       smem_desc(smem_u32(im + kImW + part * 4096) + ks * 256, 128, 512), id_l,
                        (part | ks) != 0);
           if (BWD)
             for (int pi = 0; pi < 2; ++pi)  // M mid, hi
@@ -1985,30 +1983,27 @@ __global__ void __launch_bounds__(256, 1) k_tc_blk_pown_bf16(const __grid_consta
           wait_bar(c, kG2, p.status);
           v_pending = false;
         }
-        // two block-passes ahead, into block-pass q - 1's buffer
-        if (threadIdx.x == 0 && q + 2 < nq)
-          load_image(qb == 0 ? kPnBufs - 1 : qb - 1, (j + 2) % nblk);
+        if (threadIdx.x == 0 && q + 1 < nq) load_image(q + 1, j + 1 < nblk ? j + 1 : 0);
         wait_bar(c, kG1, p.status);
         // The tile's last products have read x and v: fetch the next tile's.
         // Every thread must have waited for this tile's phase of the TMA
         // barrier first (else a lagging thread would see it two phases on):
-        // a barrier of an earlier block-pass of the tile guarantees it, and
-        // with one block-pass a tile, the barrier below.
-        const bool next_tile = j == nblk - 1 && pass == NPASS - 1 && k + 1 < n_my;
-        if (threadIdx.x == 0 && next_tile && nblk * NPASS > 1) load_tile(tile + p.P);
+        // the barrier of the tile's first block-pass guarantees it (nblk >= 2).
+        if (threadIdx.x == 0 && j == nblk - 1 && pass == NPASS - 1 && k + 1 < n_my)
+          load_tile(tile + p.P);
         const float* bias2 = (const float*)(im + kImBias);
         const float* dss = (const float*)(im + kImDs);
 #pragma unroll
-        for (int ch = 0; ch < 2; ++ch) {
-          const int c0 = half * 64 + ch * 32;
-          uint32_t lr[32], dr[32];
-          tld<32>(tL + tlane + c0, lr);
-          if (BWD) tld<32>(tD + tlane + c0, dr);
+        for (int ch = 0; ch < 2; ++ch) {  // this thread's 32 slots, 16 at a time
+          const int c0 = half * 32 + ch * 16;
+          uint32_t lr[16], dr[16];
+          tld<16>(tL + tlane + c0, lr);
+          if (BWD) tld<16>(tD + tlane + c0, dr);
           tld_wait();
-          float va[32], vb[32];
-          uint32_t e2[16];
+          float va[16], vb[16];
+          uint32_t e2[8];
 #pragma unroll
-          for (int jj = 0; jj < 16; ++jj) {
+          for (int jj = 0; jj < 8; ++jj) {
             float ov[2];
 #pragma unroll
             for (int s2 = 0; s2 < 2; ++s2) {
@@ -2042,30 +2037,29 @@ __global__ void __launch_bounds__(256, 1) k_tc_blk_pown_bf16(const __grid_consta
           if (STATS) {
             if (pass == 0) {
 #pragma unroll
-              for (int i = 0; i < 32; ++i) acc_l = fmaxf(acc_l, va[i]);
+              for (int i = 0; i < 16; ++i) acc_l = fmaxf(acc_l, va[i]);
             } else {
               acc_l += tree_sum2(va);
             }
           }
           if (value_mma) {
 #pragma unroll
-            for (int i4 = 0; i4 < 4; ++i4)  // slots c0 + 8 i4 .. + 7: one 16-byte chunk
+            for (int i4 = 0; i4 < 2; ++i4)  // slots c0 + 8 i4 .. + 7: one 16-byte chunk
               *(uint4*)(etrow + ((c0 >> 3) + i4) * 128) =
                   make_uint4(e2[4 * i4], e2[4 * i4 + 1], e2[4 * i4 + 2], e2[4 * i4 + 3]);
           }
         }
         to_async_barrier();
-        if (threadIdx.x == 0 && next_tile && nblk * NPASS == 1) load_tile(tile + p.P);
         if (value_mma) {
           if (threadIdx.x == 0) {
             if (BWD && pass == 1) {  // dx += dl W (W hi, MN-major)
-              for (int ks = 0; ks < 8; ++ks)
-                mma_bf16(tX, smem_desc(smem_u32(et) + ks * 256, 128, 2048),
-                         smem_desc(smem_u32(im + kImW + 8192) + ks * 1024, 512, 128), id_x,
+              for (int ks = 0; ks < 4; ++ks)
+                mma_bf16(tA, smem_desc(smem_u32(et) + ks * 256, 128, 1024),
+                         smem_desc(smem_u32(im + kImW + 4096) + ks * 1024, 512, 128), id_x,
                          (j | ks) != 0);
             } else {  // dfx += e dz or out += e tok (M hi, MN-major)
-              for (int ks = 0; ks < 8; ++ks)
-                mma_bf16(tA, smem_desc(smem_u32(et) + ks * 256, 128, 2048),
+              for (int ks = 0; ks < 4; ++ks)
+                mma_bf16(tA, smem_desc(smem_u32(et) + ks * 256, 128, 1024),
                          smem_desc(smem_u32(im + kImM) + ks * 2 * DV * 16, DV * 16, 128), id_a,
                          (j | ks) != 0);
             }
@@ -2120,7 +2114,7 @@ __global__ void __launch_bounds__(256, 1) k_tc_blk_pown_bf16(const __grid_consta
                 : (__nv_bfloat16*)p.out2 + sp.bc * p.so2[0] + ni * p.so2[1] + h * p.so2[2] + col;
         for (int c16 = 0; c16 < w; c16 += 16) {
           uint32_t r[16];
-          tld<16>((dxo ? tX : tA) + tlane + col + c16, r);
+          tld<16>(tA + tlane + col + c16, r);
           tld_wait();
           uint32_t o[8];
 #pragma unroll
@@ -2141,7 +2135,7 @@ __global__ void __launch_bounds__(256, 1) k_tc_blk_pown_bf16(const __grid_consta
     const float tot = cta_sum_nt<256>(dt_acc, red);
     if (threadIdx.x == 0) p.partDt[(int64_t)bh * p.P + blockIdx.x] = -inv_tau * tot * kLn2;
   }
-  epilogue<512>(c);
+  epilogue<256>(c);
 }
 
 // ------------------------------------------------------------ wait self-test
@@ -2269,7 +2263,7 @@ cudaError_t run_tc(TcKind k, const TcParams& p, cudaStream_t s) {
         k_tc_blk_bwd_g_bf16<false><<<grid, 256, kBbBytes + kSmemPad, s>>>(p);
     }
   } else if (k == TcKind::BlkImage) {
-    k_tc_blk_image<<<dim3(p.G / kBgSlots, p.B * p.H), 256, 0, s>>>(p);
+    k_tc_blk_image<<<dim3(p.G / kPnSlots, p.B * p.H), 256, 0, s>>>(p);
     e = cudaSuccess;
   } else if (k == TcKind::BlkSliceBwdN || k == TcKind::BlkDesliceBwdN ||
              k == TcKind::BlkDesliceFwd || k == TcKind::BlkStats) {
@@ -2325,11 +2319,11 @@ int tc_ctas_per_sm(TcKind k) {
     case TcKind::BlkSliceFwd: return 2;
     case TcKind::BlkSliceBwdG:
     case TcKind::BlkDesliceBwdG:
-    case TcKind::BlkImage:
+    case TcKind::BlkImage: return 1;
     case TcKind::BlkSliceBwdN:
     case TcKind::BlkDesliceBwdN:
     case TcKind::BlkDesliceFwd:
-    case TcKind::BlkStats: return 1;
+    case TcKind::BlkStats: return 2;
   }
   return 1;
 }
@@ -2339,7 +2333,7 @@ int tc_ctas_per_sm(TcKind k) {
 static_assert((kSfBytes + kSmemPad + 1024) * kCtasSliceFwd <= 228 * 1024, "slice fwd smem");
 static_assert((kBgBytes + kSmemPad + 1024) * 2 <= 228 * 1024, "blocked slice fwd smem");
 static_assert(kBbBytes + kSmemPad + 1024 <= 228 * 1024, "blocked backward smem");
-static_assert(kPnBytes + kSmemPad + 1024 <= 228 * 1024, "blocked point-owning smem");
+static_assert((kPnBytes + kSmemPad + 1024) * 2 <= 228 * 1024, "blocked point-owning smem");
 static_assert(im_bytes(32) == blk_image_bytes(32) && im_bytes(64) == blk_image_bytes(64),
               "operand image size");
 static_assert((kDfBytes + kSmemPad + 1024) * kCtasDesliceFwd <= 228 * 1024, "deslice fwd smem");

@@ -65,8 +65,8 @@ struct TcParams {
 cudaError_t run_tc(TcKind k, const TcParams& p, cudaStream_t s);
 
 // Bytes of one operand image of the blocked point-owning kernels (one per
-// b, h and block of 128 slots), value width dv.
-constexpr int blk_image_bytes(int dv) { return 1024 + 2 * 8192 + 2 * 128 * dv * 2; }
+// b, h and block of 64 slots), value width dv.
+constexpr int blk_image_bytes(int dv) { return 512 + 2 * 4096 + 2 * 64 * dv * 2; }
 
 // one bounded wait that runs out (limit_ns), on `s`: sets the status word
 cudaError_t run_wait_selftest(uint64_t limit_ns, cudaStream_t s);
