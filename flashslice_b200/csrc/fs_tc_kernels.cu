@@ -1494,7 +1494,7 @@ constexpr int kBgWs = 0, kBgBias = 2 * 8192, kBgX = kBgBias + 1024, kBgF = kBgX 
               kBgBytes = kBgBar + kBarBytes;
 static_assert(kBgX % 1024 == 0 && kBgF % 1024 == 0 && kBgW % 1024 == 0, "blocked slice layout");
 
-__global__ void __launch_bounds__(128, 2) k_tc_blk_slice_fwd_bf16(const __grid_constant__ TcParams p) {
+__global__ void __launch_bounds__(256, 2) k_tc_blk_slice_fwd_bf16(const __grid_constant__ TcParams p) {
   extern __shared__ __align__(16) uint8_t sm_raw[];
   uint8_t* sm = align_smem(sm_raw);
   const int gb = blockIdx.y, bh = blockIdx.z, b = bh / p.H, h = bh - b * p.H;
@@ -1504,7 +1504,7 @@ __global__ void __launch_bounds__(128, 2) k_tc_blk_slice_fwd_bf16(const __grid_c
   // W rows g0 .. g0 + 127, two bf16 parts (mid, hi), K-major (rows g, k = d)
   {
     const float* Wb = p.W + (int64_t)b * p.swb + (int64_t)h * p.swh + (int64_t)g0 * 32;
-    for (int i = threadIdx.x; i < kBgSlots * 32; i += 128) {
+    for (int i = threadIdx.x; i < kBgSlots * 32; i += 256) {
       const int r = i >> 5, k = i & 31;
       __nv_bfloat16 hi, mi;
       split2(Wb[i], hi, mi);
@@ -1514,17 +1514,19 @@ __global__ void __launch_bounds__(128, 2) k_tc_blk_slice_fwd_bf16(const __grid_c
     }
     const float inv_tau = __frcp_rn(p.tau[h]);
     float* bias2 = (float*)(sm + kBgBias);
-    bias2[threadIdx.x] = p.bias[(int64_t)b * p.sbb + (int64_t)h * p.sbh + g0 + threadIdx.x] *
-                         inv_tau * kLog2e;
+    if (threadIdx.x < kBgSlots)
+      bias2[threadIdx.x] = p.bias[(int64_t)b * p.sbb + (int64_t)h * p.sbh + g0 + threadIdx.x] *
+                           inv_tau * kLog2e;
     uint32_t* ones = (uint32_t*)(sm + kBgOnes);
-    for (int i = threadIdx.x; i < 1024; i += 128) ones[i] = 0x3F803F80u;  // bf16 1.0 pairs
+    for (int i = threadIdx.x; i < 1024; i += 256) ones[i] = 0x3F803F80u;  // bf16 1.0 pairs
   }
   prologue_end(c);
   const float scale = __frcp_rn(p.tau[h]) * kLog2e;
   const float* bias2 = (const float*)(sm + kBgBias);
   const uint32_t tL = c.tmem, tZ = c.tmem + 128, tS = c.tmem + 192;
-  const int row = threadIdx.x;                                       // point row / slot
-  const uint32_t tlane = (uint32_t)((threadIdx.x >> 5) * 32) << 16;  // its TMEM lane
+  // two threads per point row (64 slots each); threads 0-127 own a slot each at the end
+  const int warp = threadIdx.x >> 5, row = 32 * (warp & 3) + (threadIdx.x & 31), half = warp >> 2;
+  const uint32_t tlane = (uint32_t)(32 * (warp & 3)) << 16;  // its TMEM lanes
   const uint32_t stage_b = (uint32_t)(4 + DV / 8) * 2048;  // bytes of one tile's boxes
   auto xs = [&](int k) { return sm + kBgX + (k & 1) * 8192; };
   auto fs = [&](int k) { return sm + kBgF + (k & 1) * 16384; };
@@ -1565,7 +1567,8 @@ __global__ void __launch_bounds__(128, 2) k_tc_blk_slice_fwd_bf16(const __grid_c
       }
       uint8_t* wrow = sm + kBgW + (row >> 3) * (kBgSlots * 16) + (row & 7) * 16;
 #pragma unroll
-      for (int ch = 0; ch < 4; ++ch) {
+      for (int hc = 0; hc < 2; ++hc) {
+        const int ch = 2 * half + hc;  // this thread's 32-slot chunks
         uint32_t r[32];
         tld<32>(tL + tlane + ch * 32, r);
         tld_wait();
@@ -1598,11 +1601,12 @@ __global__ void __launch_bounds__(128, 2) k_tc_blk_slice_fwd_bf16(const __grid_c
   }
   if (n_my > 0) wait_bar(c, kG2, p.status);
   tc_fence_after();
-  // this CTA's partial sums: row = slot g0 + row
+  // this CTA's partial sums: threads 0-127, slot g0 + row
   const int64_t slot = (int64_t)bh * p.P + blockIdx.x;
   float* pz = p.partA + (slot * p.G + g0 + row) * DV;
   float* ps = p.partS + slot * p.G + g0 + row;
-  if (n_my > 0) {
+  if (half == 1) {
+  } else if (n_my > 0) {
     uint32_t r[32];
     for (int ch = 0; ch < DV / 32; ++ch) {
       tld<32>(tZ + tlane + ch * 32, r);
@@ -1633,7 +1637,7 @@ __global__ void __launch_bounds__(128, 2) k_tc_blk_slice_fwd_bf16(const __grid_c
 //    slot-major operands (the bf16 value dots);
 //  * dW += dl^T x, db += dl^T 1 and, deslice, dtokens += w^T d_out,
 //    accumulated in TMEM over the CTA's tiles.
-// Two threads per point row (64 slots each). One CTA per SM (TMEM).
+// Four threads per point row (32 slots each). One CTA per SM (TMEM).
 // smem: [W parts][M parts][bias][ds][x stage x 2][v stage x 2][dl tile][w tile][ones][bars]
 // TMEM: logits 0, dw 128, dW 256 (32), db 288 (16), dtokens 320 (DV).
 constexpr int kBbW = 0, kBbM = 2 * 8192, kBbBias = kBbM + 2 * 16384, kBbDs = kBbBias + 512,
@@ -1643,7 +1647,7 @@ constexpr int kBbW = 0, kBbM = 2 * 8192, kBbBias = kBbM + 2 * 16384, kBbDs = kBb
 static_assert(kBbX % 1024 == 0 && kBbDl % 1024 == 0, "blocked backward layout");
 
 template <bool SLICE>
-__global__ void __launch_bounds__(256, 1) k_tc_blk_bwd_g_bf16(const __grid_constant__ TcParams p) {
+__global__ void __launch_bounds__(512, 1) k_tc_blk_bwd_g_bf16(const __grid_constant__ TcParams p) {
   extern __shared__ __align__(16) uint8_t sm_raw[];
   uint8_t* sm = align_smem(sm_raw);
   const int gb = blockIdx.y, bh = blockIdx.z, b = bh / p.H, h = bh - b * p.H;
@@ -1655,7 +1659,7 @@ __global__ void __launch_bounds__(256, 1) k_tc_blk_bwd_g_bf16(const __grid_const
     // W rows g0 .. g0 + 127 (K = d, 32) and M rows (K = dv) in two bf16 parts
     // (mid, hi)
     const float* Wb = p.W + (int64_t)b * p.swb + (int64_t)h * p.swh + (int64_t)g0 * 32;
-    for (int i = threadIdx.x; i < kBgSlots * 32; i += 256) {
+    for (int i = threadIdx.x; i < kBgSlots * 32; i += 512) {
       const int r = i >> 5, k = i & 31;
       __nv_bfloat16 hi, mi;
       split2(Wb[i], hi, mi);
@@ -1664,7 +1668,7 @@ __global__ void __launch_bounds__(256, 1) k_tc_blk_bwd_g_bf16(const __grid_const
       *(__nv_bfloat16*)(sm + kBbW + 8192 + o) = hi;
     }
     const float* Mb = p.M + ((int64_t)bh * p.G + g0) * DV;
-    for (int i = threadIdx.x; i < kBgSlots * DV; i += 256) {
+    for (int i = threadIdx.x; i < kBgSlots * DV; i += 512) {
       const int r = i / DV, k = i - r * DV;
       __nv_bfloat16 hi, mi;
       split2(Mb[i], hi, mi);
@@ -1679,7 +1683,7 @@ __global__ void __launch_bounds__(256, 1) k_tc_blk_bwd_g_bf16(const __grid_const
       ((float*)(sm + kBbDs))[threadIdx.x] = SLICE ? p.ds[(int64_t)bh * p.G + g0 + threadIdx.x] : 0.f;
     }
     uint32_t* ones = (uint32_t*)(sm + kBbOnes);
-    for (int i = threadIdx.x; i < 1024; i += 256) ones[i] = 0x3F803F80u;
+    for (int i = threadIdx.x; i < 1024; i += 512) ones[i] = 0x3F803F80u;
   }
   prologue_end(c);
   const float scale = inv_tau * kLog2e;
@@ -1687,7 +1691,8 @@ __global__ void __launch_bounds__(256, 1) k_tc_blk_bwd_g_bf16(const __grid_const
   const float* dss = (const float*)(sm + kBbDs);
   const uint32_t tL = c.tmem, tD = c.tmem + 128, tW = c.tmem + 256, tB = c.tmem + 288,
                  tT = c.tmem + 320;
-  const int warp = threadIdx.x >> 5, row = 32 * (warp & 3) + (threadIdx.x & 31), half = warp >> 2;
+  // four threads per point row, a quarter of the slots each
+  const int warp = threadIdx.x >> 5, row = 32 * (warp & 3) + (threadIdx.x & 31), quarter = warp >> 2;
   const uint32_t tlane = (uint32_t)(32 * (warp & 3)) << 16;
   const uint32_t stage_b = (uint32_t)(4 + DV / 8) * 2048;
   auto xs = [&](int k) { return sm + kBbX + (k & 1) * 8192; };
@@ -1735,9 +1740,8 @@ __global__ void __launch_bounds__(256, 1) k_tc_blk_bwd_g_bf16(const __grid_const
       }
       uint8_t* dlrow = sm + kBbDl + (row >> 3) * (kBgSlots * 16) + (row & 7) * 16;
       uint8_t* wrow = sm + kBbWt + (row >> 3) * (kBgSlots * 16) + (row & 7) * 16;
-#pragma unroll
-      for (int ch = 0; ch < 2; ++ch) {
-        const int c0 = half * 64 + ch * 32;
+      {
+        const int c0 = quarter * 32;
         uint32_t lr[32], dr[32];
         tld<32>(tL + tlane + c0, lr);
         tld<32>(tD + tlane + c0, dr);
@@ -2258,9 +2262,9 @@ cudaError_t run_tc(TcKind k, const TcParams& p, cudaStream_t s) {
     if (e == cudaSuccess) {
       const dim3 grid(p.P, p.G / kBgSlots, p.B * p.H);
       if (sl)
-        k_tc_blk_bwd_g_bf16<true><<<grid, 256, kBbBytes + kSmemPad, s>>>(p);
+        k_tc_blk_bwd_g_bf16<true><<<grid, 512, kBbBytes + kSmemPad, s>>>(p);
       else
-        k_tc_blk_bwd_g_bf16<false><<<grid, 256, kBbBytes + kSmemPad, s>>>(p);
+        k_tc_blk_bwd_g_bf16<false><<<grid, 512, kBbBytes + kSmemPad, s>>>(p);
     }
   } else if (k == TcKind::BlkImage) {
     k_tc_blk_image<<<dim3(p.G / kPnSlots, p.B * p.H), 256, 0, s>>>(p);
@@ -2288,7 +2292,7 @@ cudaError_t run_tc(TcKind k, const TcParams& p, cudaStream_t s) {
   } else if (k == TcKind::BlkSliceFwd) {
     e = set_smem((const void*)k_tc_blk_slice_fwd_bf16, kBgBytes + kSmemPad);
     if (e == cudaSuccess)
-      k_tc_blk_slice_fwd_bf16<<<dim3(p.P, p.G / kBgSlots, p.B * p.H), 128, kBgBytes + kSmemPad,
+      k_tc_blk_slice_fwd_bf16<<<dim3(p.P, p.G / kBgSlots, p.B * p.H), 256, kBgBytes + kSmemPad,
                                 s>>>(p);
   } else {
     e = p.pdt == 1 ? run_tc_t<__nv_bfloat16>(k, p, s) : run_tc_t<float>(k, p, s);
