@@ -388,7 +388,9 @@ int run_stats(const fs_problem& p, const Setup& s, const fs_tensor4* x, const fl
     tn.P = pown_P(p, s);
     route_note("stats", "tensor-core-blocked", p, x, x);
     FS_TRY(tcx::run_tc(tcx::TcKind::BlkImage, tn, st));
-    FS_TRY(tcx::run_tc(tcx::TcKind::BlkStats, tn, st));
+    // the online or two-pass statistics, as the problem's stats mode asks
+    FS_TRY(tcx::run_tc(p.stats_mode == 1 ? tcx::TcKind::BlkStats : tcx::TcKind::BlkStatsOnline,
+                       tn, st));
     return FS_OK;
   }
   Params q = base_params(p, s, W, bias, tau);

@@ -1874,6 +1874,8 @@ __global__ void __launch_bounds__(256) k_tc_blk_image(const __grid_constant__ Tc
 // and walks the blocks of 64 slots, their operand images double-buffered:
 //  MODE 3, the statistics, two passes (blocked.py:350-400): m = max_g logit,
 //  then l = sum_g exp(logit - m) with m as its consumers read it;
+//  MODE 4, the statistics online, one pass (blocked.py:293-346): a running
+//  max per thread, its sum rescaled by exp(m_old - m_new) when it moves;
 //  MODE 2, deslice forward (blocked.py:466-510): out = sum_g e tok / l;
 //  MODE 1, slice backward (blocked.py:577-673), and MODE 0, deslice backward
 //  (blocked.py:745-815): pass 1 forms the row sum l = sum_g e, delta =
@@ -1897,8 +1899,8 @@ static_assert(im_bytes(64) <= kPnIm && kPnX % 1024 == 0 && kPnE % 1024 == 0,
 
 template <int MODE>
 __global__ void __launch_bounds__(256, 2) k_tc_blk_pown_bf16(const __grid_constant__ TcParams p) {
-  constexpr bool BWD = MODE <= 1, SLICE = MODE == 1, STATS = MODE == 3;
-  constexpr int NPASS = MODE == 2 ? 1 : 2;
+  constexpr bool BWD = MODE <= 1, SLICE = MODE == 1, STATS = MODE == 3, ONLINE = MODE == 4;
+  constexpr int NPASS = MODE == 2 || ONLINE ? 1 : 2;
   extern __shared__ __align__(16) uint8_t sm_raw[];
   uint8_t* sm = align_smem(sm_raw);
   const int bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H, DV = p.dv, N = p.N;
@@ -1913,7 +1915,8 @@ __global__ void __launch_bounds__(256, 2) k_tc_blk_pown_bf16(const __grid_consta
   const uint32_t tlane = (uint32_t)(32 * (warp & 3)) << 16;
   const uint8_t* img_bh = p.img + (int64_t)bh * nblk * im_bytes(DV);
   // the deslice forward reads W and M's hi part only, the statistics W only
-  const uint32_t im_copy = BWD ? (uint32_t)im_bytes(DV) : STATS ? (uint32_t)kImM : (uint32_t)(kImM + mp);
+  const uint32_t im_copy = BWD ? (uint32_t)im_bytes(DV)
+                           : STATS || ONLINE ? (uint32_t)kImM : (uint32_t)(kImM + mp);
   const uint32_t stage_b = (uint32_t)(BWD ? 4 + DV / 8 : 4) * 2048;
   uint8_t* const xs = sm + kPnX;
   uint8_t* const vs = sm + kPnV;
@@ -1951,7 +1954,7 @@ __global__ void __launch_bounds__(256, 2) k_tc_blk_pown_bf16(const __grid_consta
     const int64_t ni = sp.n0 + n;
     const int64_t sbase = (int64_t)bh * 2 * N;
     float m2 = 0.f, inv_l = 0.f, delta = 0.f;
-    if (valid && !STATS) {
+    if (valid && !STATS && !ONLINE) {
       m2 = p.stats_in[sbase + ni] * kLog2e;
       if (!BWD) inv_l = __frcp_rn(p.stats_in[sbase + N + ni]);
     }
@@ -1959,7 +1962,8 @@ __global__ void __launch_bounds__(256, 2) k_tc_blk_pown_bf16(const __grid_consta
     for (int pass = 0; pass < NPASS; ++pass) {
       // backward pass 0: row sum and sum e dw; pass 1: the temperature term;
       // statistics pass 0: row max (m2 = 0), pass 1: row sum
-      float acc_l = STATS && pass == 0 ? -INFINITY : 0.f, acc_u = 0.f;
+      // online statistics: running max acc_u (log2 units) and its sum acc_l
+      float acc_l = STATS && pass == 0 ? -INFINITY : 0.f, acc_u = ONLINE ? -INFINITY : 0.f;
       const bool value_mma = MODE == 2 || SLICE || (BWD && pass == 1);
       for (int j = 0; j < nblk; ++j, ++q) {
         const uint8_t* im = sm + (q & 1) * kPnIm;
@@ -2028,6 +2032,8 @@ __global__ void __launch_bounds__(256, 2) k_tc_blk_pown_bf16(const __grid_consta
                 }
               } else if (STATS) {
                 va[i] = pass == 0 ? t2 : e;
+              } else if (ONLINE) {
+                va[i] = t2;
               } else {
                 ov[s2] = e;
               }
@@ -2037,6 +2043,16 @@ __global__ void __launch_bounds__(256, 2) k_tc_blk_pown_bf16(const __grid_consta
           if (BWD) {
             if (pass == 0) acc_l += tree_sum2(va);
             acc_u += tree_sum2(vb);
+          }
+          if (ONLINE) {
+            float bm = va[0];
+#pragma unroll
+            for (int i = 1; i < 16; ++i) bm = fmaxf(bm, va[i]);
+            const float mn = fmaxf(acc_u, bm);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) va[i] = ex2(va[i] - mn);
+            acc_l = acc_l * ex2(acc_u - mn) + tree_sum2(va);
+            acc_u = mn;
           }
           if (STATS) {
             if (pass == 0) {
@@ -2073,6 +2089,20 @@ __global__ void __launch_bounds__(256, 2) k_tc_blk_pown_bf16(const __grid_consta
         }
       }
       // ---- end of a pass
+      if (ONLINE) {
+        red[half * 128 + row] = acc_u;
+        red[256 + half * 128 + row] = acc_l;
+        __syncthreads();
+        if (half == 0 && valid) {
+          const float ma = red[row], mb = red[128 + row], mx = fmaxf(ma, mb);
+          // m in the logits' units; l taken to m on the log2 scale as its
+          // readers form it (m log2(e), a rounding away from mx)
+          const float m = mx * kLn2, mr = m * kLog2e;
+          const float l = red[256 + row] * ex2(ma - mr) + red[384 + row] * ex2(mb - mr);
+          p.stats_out[sbase + ni] = m;
+          p.stats_out[sbase + N + ni] = l;
+        }
+      }
       if (STATS) {
         red[half * 128 + row] = acc_l;
         __syncthreads();
@@ -2270,13 +2300,16 @@ cudaError_t run_tc(TcKind k, const TcParams& p, cudaStream_t s) {
     k_tc_blk_image<<<dim3(p.G / kPnSlots, p.B * p.H), 256, 0, s>>>(p);
     e = cudaSuccess;
   } else if (k == TcKind::BlkSliceBwdN || k == TcKind::BlkDesliceBwdN ||
-             k == TcKind::BlkDesliceFwd || k == TcKind::BlkStats) {
+             k == TcKind::BlkDesliceFwd || k == TcKind::BlkStats ||
+             k == TcKind::BlkStatsOnline) {
     const int mode = k == TcKind::BlkDesliceBwdN ? 0
                      : k == TcKind::BlkSliceBwdN ? 1
                      : k == TcKind::BlkDesliceFwd ? 2
-                                                  : 3;
-    const void* fns[4] = {(const void*)k_tc_blk_pown_bf16<0>, (const void*)k_tc_blk_pown_bf16<1>,
-                          (const void*)k_tc_blk_pown_bf16<2>, (const void*)k_tc_blk_pown_bf16<3>};
+                     : k == TcKind::BlkStats      ? 3
+                                                  : 4;
+    const void* fns[5] = {(const void*)k_tc_blk_pown_bf16<0>, (const void*)k_tc_blk_pown_bf16<1>,
+                          (const void*)k_tc_blk_pown_bf16<2>, (const void*)k_tc_blk_pown_bf16<3>,
+                          (const void*)k_tc_blk_pown_bf16<4>};
     e = set_smem(fns[mode], kPnBytes + kSmemPad);
     if (e == cudaSuccess) {
       const dim3 grid(p.P, p.B * p.H);
@@ -2286,8 +2319,10 @@ cudaError_t run_tc(TcKind k, const TcParams& p, cudaStream_t s) {
         k_tc_blk_pown_bf16<1><<<grid, 256, kPnBytes + kSmemPad, s>>>(p);
       else if (mode == 2)
         k_tc_blk_pown_bf16<2><<<grid, 256, kPnBytes + kSmemPad, s>>>(p);
-      else
+      else if (mode == 3)
         k_tc_blk_pown_bf16<3><<<grid, 256, kPnBytes + kSmemPad, s>>>(p);
+      else
+        k_tc_blk_pown_bf16<4><<<grid, 256, kPnBytes + kSmemPad, s>>>(p);
     }
   } else if (k == TcKind::BlkSliceFwd) {
     e = set_smem((const void*)k_tc_blk_slice_fwd_bf16, kBgBytes + kSmemPad);
@@ -2327,7 +2362,8 @@ int tc_ctas_per_sm(TcKind k) {
     case TcKind::BlkSliceBwdN:
     case TcKind::BlkDesliceBwdN:
     case TcKind::BlkDesliceFwd:
-    case TcKind::BlkStats: return 2;
+    case TcKind::BlkStats:
+    case TcKind::BlkStatsOnline: return 2;
   }
   return 1;
 }

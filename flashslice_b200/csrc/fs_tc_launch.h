@@ -25,6 +25,7 @@ enum class TcKind {
   BlkDesliceBwdN,  // blocked point-owning deslice backward (delta, dx, dtau), bf16 dots
   BlkDesliceFwd,   // blocked point-owning deslice forward with statistics, bf16 dots
   BlkStats,        // blocked per-point statistics (m, l), two passes, bf16 points
+  BlkStatsOnline,  // the same statistics online, one pass
 };
 
 constexpr int kMaxSplits = 128;  // FS_MAX_SPLITS

@@ -153,22 +153,39 @@ def test_blocked_deslice_forward_on_tensor_cores(env, case):
     dict(B=2, N=4097, H=2, DV=32, G=1024, mode="bhgd", bias=False),
 ], ids=["g128", "g1024-dv32"])
 def test_blocked_statistics_on_tensor_cores(env, case):
-    """The per-point statistics on the tensor cores (two passes; logits from
-    W in two bf16 parts, within 2^-17 of each product) against the FMA
-    engine's exact-fp32 ones: m and l to about 1e-5 relative, two to three
-    orders below the bf16 dot mode's own rounding."""
+    """The per-point statistics on the tensor cores, online (one pass, the
+    default stats mode) and two-pass (logits from W in two bf16 parts,
+    within 2^-17 of each product), against the FMA engine's exact-fp32 ones:
+    m and l to about 1e-5 relative, two to three orders below the bf16 dot
+    mode's own rounding; the two modes' m bitwise equal (a max is exact)
+    (``parity_ops.py:213-235``)."""
+    from flashslice_b200.kernels.blocked import set_stats_mode
     K, st, lib = env
     x, fx, W, b, tau = _inputs(**case)
-    _, _, s_tc = K.fused_slice(x, fx, W, b, tau, return_stats=True)
-    st.set_engine("fma")
+    got = {}
     try:
-        _, _, s_fma = K.fused_slice(x, fx, W, b, tau, return_stats=True)
+        for mode in ("online", "two-pass"):
+            set_stats_mode(mode)
+            n0 = lib.fs_tc_launch_count()
+            _, _, got[mode] = K.fused_slice(x, fx, W, b, tau, return_stats=True)
+            torch.cuda.synchronize()
+            assert lib.fs_tc_launch_count() - n0 == 3
+            st.set_engine("fma")
+            try:
+                _, _, s_fma = K.fused_slice(x, fx, W, b, tau, return_stats=True)
+            finally:
+                st.set_engine("auto")
+            m, mf = got[mode][:, :, 0], s_fma[:, :, 0]
+            dm = float((m - mf).abs().max())
+            assert dm <= 1e-5 * (1 + float(mf.abs().max())), (mode, dm)
+            l, lf = got[mode][:, :, 1], s_fma[:, :, 1]
+            dl = float(((l - lf).abs() / lf).max())
+            assert dl <= 1e-4, (mode, dl)
     finally:
-        st.set_engine("auto")
-    m, mf = s_tc[:, :, 0], s_fma[:, :, 0]
-    assert float((m - mf).abs().max()) <= 1e-5 * (1 + float(mf.abs().max())), float((m - mf).abs().max())
-    l, lf = s_tc[:, :, 1], s_fma[:, :, 1]
-    assert float(((l - lf).abs() / lf).max()) <= 1e-4, float(((l - lf).abs() / lf).max())
+        set_stats_mode("online")
+    assert torch.equal(got["online"][:, :, 0], got["two-pass"][:, :, 0])
+    lo, lt = got["online"][:, :, 1], got["two-pass"][:, :, 1]
+    assert float(((lo - lt).abs() / lt).max()) <= 1e-5
     assert lib.fs_device_status(1) == 0
 
 
