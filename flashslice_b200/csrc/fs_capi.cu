@@ -662,7 +662,11 @@ int fs_deslice_fwd(const fs_problem* p, const fs_tensor4* x_mid, const float* we
   }
   if (stats_in) return with_stats(stats_in);
   float* dst = s.internal_stats ? at(workspace, s.stats) : stats_out;
-  if (p->stats_mode == 0) {
+  // Online statistics: formed in the same pass as out on the FMA engine; on
+  // the tensor cores, by the online statistics kernel and then the deslice
+  // with them (two passes over x_mid, each far faster).
+  const bool blk_tc = s.has_img && tc_tensor_ok(x_mid) && tc_tensor_ok(out);
+  if (p->stats_mode == 0 && !blk_tc) {
     route_note("deslice_fwd", "fma-blocked", *p, x_mid, out);
     q.stats_out = dst;
     return launch_kind(Kind::DesliceFwdOnline, *p, s, q, P, st);

@@ -60,6 +60,13 @@ def test_workspace_sizes():
     # deterministic: a pure function of the problem
     assert ws(nat.OP_SLICE_BWD, blk) == ws(nat.OP_SLICE_BWD, blk)
     assert ws(nat.OP_SLICE_FWD, prob(D=300)) == 0         # invalid problem
+    # bf16 points in the bf16 dot mode, G a multiple of 128: room for the
+    # tensor-core kernels' operand images, one per (b, h, 64 slots), each
+    # 512 + 2 * 4096 + 2 * 64 * DV * 2 bytes
+    tc = dict(family=1, G=1024, DV=64, act_dtype=1, dot=3, flags=nat.FLAG_STATS_IN)
+    img = 2 * (1024 // 64) * (512 + 2 * 4096 + 2 * 64 * 64 * 2)
+    for op in (nat.OP_SLICE_FWD, nat.OP_DESLICE_FWD, nat.OP_SLICE_BWD, nat.OP_DESLICE_BWD):
+        assert ws(op, prob(**tc)) >= ws(op, prob(**dict(tc, dot=0))) + img, op
 
 
 @pytest.mark.parametrize("kw,code", [

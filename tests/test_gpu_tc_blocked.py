@@ -97,11 +97,11 @@ def test_blocked_round_backward_on_tensor_cores(env, case):
 
     n0 = lib.fs_tc_launch_count()
     tc = round_("auto")
-    # the slice forward's statistics and slot-owning kernel, and each backward
-    # op's operand images, point-owning and slot-owning halves (the deslice
-    # forward, called here without statistics, forms them online on the FMA
-    # engine)
-    assert lib.fs_tc_launch_count() - n0 == 3 + 3 + 3
+    # the slice forward's statistics and slot-owning kernel; the deslice
+    # forward, called here without statistics: its own (images, statistics)
+    # and then its images and kernel; each backward op's images,
+    # point-owning and slot-owning halves
+    assert lib.fs_tc_launch_count() - n0 == 3 + 4 + 3 + 3
     ex = round_("fma")
     from oracle import eager_torch as E
     ref = E.coupling_round(*[t.detach().double().clone().requires_grad_(True)
@@ -133,6 +133,13 @@ def test_blocked_deslice_forward_on_tensor_cores(env, case):
     torch.cuda.synchronize()
     assert lib.fs_tc_launch_count() - n0 == 2, "the tensor-core kernels did not run"
     assert out.dtype == torch.bfloat16
+    # without statistics (the deslice -> slice order): formed on the tensor
+    # cores first, then the same kernel; they match the slice's
+    n1 = lib.fs_tc_launch_count()
+    out_o, st_o = K.fused_deslice(x, W, b, tau, tok, return_stats=True)
+    torch.cuda.synchronize()
+    assert lib.fs_tc_launch_count() - n1 == 4
+    assert torch.equal(st_o, stats) and torch.equal(out_o, out)
     out2 = K.fused_deslice(x, W, b, tau, tok, stats=stats)
     assert torch.equal(out, out2)
     st.set_engine("fma")
