@@ -1486,6 +1486,7 @@ __global__ void __launch_bounds__(128 * kTCoupledBwd, kCtasCoupledBwd)
 //    in TMEM over the CTA's tiles.
 // Point tiles arrive by TMA as 16-byte column boxes, which lays them out as
 // the MMAs' operands directly (x K-major, fx point-major), double-buffered.
+// Two threads per point row (64 slots each); two CTAs per SM.
 // smem: [W parts x 2 (16 KB)][bias][x stage x 2][fx stage x 2][w tile][ones][bars]
 // TMEM: logits at 0 (128 columns), z_num at 128 (DV), s at 192 (16).
 constexpr int kBgSlots = 128;
