@@ -411,28 +411,19 @@ static __device__ __align__(256) float fs_noalloc_scratch[FS_NOALLOC_SCRATCH_BYT
 
 namespace {
 
-constexpr int kMaxDevices = 64;
-std::mutex g_noalloc_mu;
-float* g_noalloc_ptr[kMaxDevices] = {};
-
-// The device address of fs_noalloc_scratch on the current device. The name
-// of the array in host code is only a host-side stand-in, so the address is
-// asked of the runtime once per device (with that device current) and kept.
+// The device address of fs_noalloc_scratch in the calling thread's current
+// context. The array's name in host code is only a host-side stand-in, and
+// the address the runtime gives belongs to one context (a caller may run in
+// a context of its own, or reset the device and get a new one), so it is
+// asked for on every call: a host-only lookup that allocates nothing. The
+// first call in a context loads this library's device code into it.
 int noalloc_scratch(float** out) {
-  int dev = 0;
-  FS_TRY(cudaGetDevice(&dev));
-  if (dev < 0 || dev >= kMaxDevices)
-    return fail(FS_ERR_UNSUPPORTED, "device ordinal %d beyond %d", dev, kMaxDevices);
-  std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (!g_noalloc_ptr[dev]) {
-    void* ptr = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&ptr, fs_noalloc_scratch);
-    if (e != cudaSuccess || !ptr)
-      return fail(FS_ERR_CUDA, "cudaGetSymbolAddress(fs_noalloc_scratch) failed: %s",
-                  cudaGetErrorString(e));
-    g_noalloc_ptr[dev] = (float*)ptr;
-  }
-  *out = g_noalloc_ptr[dev];
+  void* ptr = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&ptr, fs_noalloc_scratch);
+  if (e != cudaSuccess || !ptr)
+    return fail(FS_ERR_CUDA, "cudaGetSymbolAddress(fs_noalloc_scratch) failed: %s",
+                cudaGetErrorString(e));
+  *out = (float*)ptr;
   return FS_OK;
 }
 

@@ -2190,16 +2190,14 @@ __global__ void k_tc_wait_selftest(int* status, uint64_t limit_ns) {
 
 static __device__ int fs_tc_status_word;
 
+// The status word's device address in the current context, looked up on
+// every call (a host-only query): the address belongs to one context, so a
+// cached one would go stale for a caller in another context or after a
+// device reset, and nothing shared is written.
 int* device_status() {
-  static int* ptrs[64] = {};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-  if (!ptrs[dev]) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, fs_tc_status_word) != cudaSuccess) return nullptr;
-    ptrs[dev] = (int*)p;
-  }
-  return ptrs[dev];
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, fs_tc_status_word) != cudaSuccess) return nullptr;
+  return (int*)p;
 }
 
 bool make_point_map(CUtensorMap* map, const void* data, int64_t B, int64_t N, int64_t H,

@@ -1,3 +1,8 @@
+# Portions of this file restate code from flashslice (https://github.com/Shizheng-Wen/flashslice),
+# Copyright 2026 Shizheng Wen, licensed under the Apache License 2.0, which in
+# turn derives from Transolver (https://github.com/thuml/Transolver),
+# Copyright (c) 2024 THUML @ Tsinghua University, used under the MIT License.
+
 """The pointwise MLP of every Transolver block (parameter names as the
 reference's ``flashslice/layers/basic.py:28-53``: linear_pre, linears,
 linear_post)."""
@@ -5,7 +10,7 @@ linear_post)."""
 import torch.nn as nn
 
 ACTIVATION = {"gelu": nn.GELU, "tanh": nn.Tanh, "sigmoid": nn.Sigmoid, "relu": nn.ReLU,
-              "leaky_relu": nn.LeakyReLU(0.1), "softplus": nn.Softplus, "ELU": nn.ELU,
+              "leaky_relu": lambda: nn.LeakyReLU(0.1), "softplus": nn.Softplus, "ELU": nn.ELU,
               "silu": nn.SiLU}
 
 

@@ -1,3 +1,8 @@
+# Portions of this file restate code from flashslice (https://github.com/Shizheng-Wen/flashslice),
+# Copyright 2026 Shizheng Wen, licensed under the Apache License 2.0, which in
+# turn derives from Transolver (https://github.com/thuml/Transolver),
+# Copyright (c) 2024 THUML @ Tsinghua University, used under the MIT License.
+
 """Physics-attention for irregular meshes with the slice/deslice coupling on
 the B200 ops.
 

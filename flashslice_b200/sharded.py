@@ -91,6 +91,29 @@ def rank_sum(x, group=None):
     return _RankSum.apply(x, group)
 
 
+class _RankSumMany(torch.autograd.Function):
+    """Several tensors summed over the ranks through one all-gather, and
+    their gradients likewise through one all-gather in the backward."""
+
+    @staticmethod
+    def forward(ctx, group, *xs):
+        ctx.group = group
+        ctx.like = [(x.shape, x.dtype, x.device) for x in xs]
+        return tuple(ordered_sum_many(list(xs), group))
+
+    @staticmethod
+    def backward(ctx, *gs):
+        # every rank takes the same collective, so a missing gradient is a zero one
+        gs = [g if g is not None else torch.zeros(sh, dtype=dt, device=dv)
+              for g, (sh, dt, dv) in zip(gs, ctx.like)]
+        return (None,) + tuple(ordered_sum_many(gs, ctx.group))
+
+
+def rank_sum_many(xs, group=None):
+    """``rank_sum`` of each tensor of ``xs`` with one collective each way."""
+    return _RankSumMany.apply(group, *xs)
+
+
 def sharded_slice(x_mid, fx_mid, weight, bias, tau, group=None, slice_fn=None):
     """``fused_slice`` of this rank's points, summed over the ranks: returns
     the global z_num (B, H, G, DV) and s (B, H, G) on every rank.
@@ -99,7 +122,8 @@ def sharded_slice(x_mid, fx_mid, weight, bias, tau, group=None, slice_fn=None):
     if slice_fn is None:
         from .kernels import fused_slice as slice_fn
     z_num, s = slice_fn(x_mid, fx_mid, weight, bias, tau)
-    return rank_sum(z_num, group), rank_sum(s, group)
+    z_num, s = rank_sum_many([z_num, s], group)
+    return z_num, s
 
 
 def sharded_coupling(x_mid, fx_mid, weight, bias, tau, mix=None, eps=1e-5, group=None,

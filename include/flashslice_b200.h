@@ -194,8 +194,11 @@ FS_API int fs_deslice_bwd(const fs_problem* p, const fs_tensor4* x_mid,
                    void* workspace, size_t workspace_bytes, void* stream);
 
 /* Slice forward without any device allocation by the caller or the library:
- * the same results as fs_slice_fwd, with the per-CTA partial sums kept in a
- * fixed scratch array inside this library instead of a caller workspace.
+ * the same values as fs_slice_fwd to fp32 rounding (it always runs the
+ * exact-fp32 FMA slice forward, where fs_slice_fwd may run the tensor-core
+ * kernel, so the two may differ in the last bits), with the per-CTA partial
+ * sums kept in a fixed scratch array inside this library instead of a
+ * caller workspace.
  * No counterpart in the reference. For callers that cannot allocate device
  * memory -- a host that owns and pre-plans all device memory (an engine
  * plugin, an FFI caller with no device allocator at hand) or a code path
@@ -207,8 +210,10 @@ FS_API int fs_deslice_bwd(const fs_problem* p, const fs_tensor4* x_mid,
  *    FS_ERR_UNSUPPORTED; use fs_slice_fwd with a workspace for those.
  *  - The scratch (FS_NOALLOC_SCRATCH_BYTES) is a static device array: every
  *    GPU that loads this library holds it until the process exits.
- *  - The first call on each device looks up the array's device address
- *    (cudaGetSymbolAddress, with that device current); make that first call
+ *  - Every call looks up the array's device address in the calling
+ *    thread's current context (cudaGetSymbolAddress: a host-side query, no
+ *    allocation); the scratch is per context. The first call in a context
+ *    loads the library's device code into it, so make that first call
  *    before any stream capture. No call allocates or frees device memory.
  *  - All calls share the one scratch array: calls that overlap on the GPU
  *    (different streams, or different host threads on one device) race and

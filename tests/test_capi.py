@@ -136,3 +136,34 @@ def test_wait_selftest_argument_checked_without_gpu():
     assert lib.fs_selftest_wait_timeout(0, None) == nat.FS_ERR_ARGUMENT
     assert lib.fs_selftest_wait_timeout(3_000_000_000, None) == nat.FS_ERR_ARGUMENT
 
+
+
+@pytest.mark.parametrize("kw,codes", [
+    (dict(flags=1), (nat.FS_ERR_ARGUMENT,)),                      # statistics handed in
+    (dict(flags=2), (nat.FS_ERR_ARGUMENT,)),                      # statistics asked for
+    (dict(family=1), (nat.FS_ERR_UNSUPPORTED, nat.FS_ERR_ARGUMENT)),  # blocked family, G <= 32
+    (dict(G=64), (nat.FS_ERR_UNSUPPORTED,)),                      # beyond the single-tile family
+])
+def test_noalloc_refusals_without_gpu(kw, codes):
+    """fs_slice_fwd_noalloc refuses, before any launch, what it does not
+    serve: statistics in or out, the blocked family, G > 32, ragged rows."""
+    lib = nat.load()
+    t = nat.Tensor4(ctypes.c_void_p(16), (ctypes.c_int64 * 4)(0, 0, 0, 1))
+    one = ctypes.c_void_p(16)
+    p = prob(**kw)
+    rc = lib.fs_slice_fwd_noalloc(ctypes.byref(p), ctypes.byref(t), ctypes.byref(t), one, one,
+                                  one, one, one, None)
+    assert rc in codes, (kw, rc)
+    assert lib.fs_last_error()
+
+
+def test_noalloc_refuses_row_splits_without_gpu():
+    lib = nat.load()
+    t = nat.Tensor4(ctypes.c_void_p(16), (ctypes.c_int64 * 4)(0, 0, 0, 1))
+    one = ctypes.c_void_p(16)
+    arr = (ctypes.c_int64 * 3)(0, 400, 1000)
+    p = prob(B=2)
+    p.row_splits = ctypes.cast(arr, ctypes.c_void_p)
+    rc = lib.fs_slice_fwd_noalloc(ctypes.byref(p), ctypes.byref(t), ctypes.byref(t), one, one,
+                                  one, one, one, None)
+    assert rc == nat.FS_ERR_UNSUPPORTED
