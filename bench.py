@@ -83,8 +83,9 @@ def parse():
                     help="config 4: let the model's torch GEMMs use TF32 (the coupling ops "
                          "stay exact fp32 either way)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--cpu-sample", type=int, default=131072,
-                    help="points per CPU-baseline step")
+    ap.add_argument("--cpu-sample", type=int, default=None,
+                    help="points per CPU step (default: the workload's points per GPU, "
+                         "at most 2^20)")
     return ap.parse_args()
 
 
@@ -136,6 +137,41 @@ def zero_grads(*ts):
     for t in ts:
         if t is not None:
             t.grad = None
+
+
+def op_by_op_step(K, x, fx, W, b, tau, r):
+    """The same round through the reference's own surface: ``fused_slice``,
+    the normalisation, ``fused_deslice`` and autograd's backward of the two
+    ops (deslice backward, slice backward, and the sum of their dx)."""
+    z, s = K.fused_slice(x, fx, W, b, tau)
+    out = K.fused_deslice(x, W, b, tau, z / (s + EPS)[..., None])
+    out.backward(r)
+    return out
+
+
+def reverse_step(K, x, fx, W, b, tau, tok, r, rz, rs):
+    """The reverse call order of config 2: deslice first (tokens given, the
+    per-point statistics returned), then the slice of the same points with
+    those statistics handed in, forward and backward of
+    sum(out r) + sum(z_num rz) + sum(s rs)."""
+    out, st = K.fused_deslice(x, W, b, tau, tok, return_stats=True)
+    z, s = K.fused_slice(x, fx, W, b, tau, stats=st)
+    torch.autograd.backward([out, z, s], [r, rz, rs])
+    return out
+
+
+def timed_rounds(step, steps, warmup=2):
+    """Mean device time (ms) of ``steps`` calls of ``step`` after ``warmup``."""
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
 
 
 PROFILE_SUMMARY = os.path.join(ROOT, "profiles", "tc_kernels_ncu_full_small.md")
@@ -389,12 +425,20 @@ def cpu_baseline(cfg, sample, reps=3):
                       "over %d points of the same shape, median of %d" % (sample, reps)}
 
 
+def cpu_sample(args, cfg):
+    """Points per CPU step: the workload's points per GPU (config 2: all
+    2^20, so the CPU arm runs the same configuration), at most 2^20."""
+    if args.cpu_sample is not None:
+        return args.cpu_sample
+    return min(cfg["N"], 1 << 20)
+
+
 def run_reference(args, cfg):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     threads = os.cpu_count() or 1
-    sample = args.cpu_sample
+    sample = cpu_sample(args, cfg)
     from oracle import eager_torch as E
     torch.set_num_threads(threads)
     x, fx, W, b, tau, r = make_inputs(cfg, sample, "cpu", 0)
@@ -416,8 +460,10 @@ def run_reference(args, cfg):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(sec * 1e3, 3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic", "impl": "reference",
-            "config": {"workload": args.config + " (CPU sample)", "B": cfg["B"], "N": sample,
-                       "H": cfg["H"], "D": cfg["D"], "DV": cfg["DV"], "G": cfg["G"]},
+            "config": {"workload": args.config if sample == cfg["N"] else
+                       args.config + " (CPU sample)", "B": cfg["B"], "N": sample,
+                       "H": cfg["H"], "D": cfg["D"], "DV": cfg["DV"], "G": cfg["G"],
+                       "same_config": sample == cfg["N"]},
             "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": threads,
                              "kind": "port",
                              "sample": "eager coupling round over %d points per step" % sample},
@@ -579,7 +625,10 @@ def main():
     points = cfg["B"] * (cfg["N"] if cfg["split"] else n_local * world)
     value = points / (ms * 1e-3) / 1e6
 
-    # end to end: inputs from pinned host memory, parameter gradients back
+    # end to end: inputs from pinned host memory; every result back to pinned
+    # host memory -- the round's output and the point gradients dx, dfx (the
+    # op's results are point tensors: a host caller wants them on the host)
+    # and the parameter gradients
     e2e = None
     if not args.no_e2e:
         xh = x.detach().cpu().pin_memory()
@@ -587,15 +636,21 @@ def main():
         params = (W, tau) + ((b,) if b is not None else ())
         res_bytes = sum(t.numel() * t.element_size() for t in params)
         outs = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in params]
+        pt_host = [torch.empty(x.shape, dtype=x.dtype, pin_memory=True) for _ in range(3)]
+        res_bytes += sum(t.numel() * t.element_size() for t in pt_host)
         # Two sets of device inputs: the host copy of step i + 1's inputs runs
-        # on a copy stream while step i computes (every step still copies its
-        # own inputs and reads its gradients back inside the timed region).
+        # on a copy stream while step i computes, and step i's results go back
+        # on a third stream while step i + 1 computes (PCIe is full duplex);
+        # every step still copies its own inputs in and its results out
+        # inside the timed region.
         sets = [(x, fx), (x.detach().clone().requires_grad_(True),
                           fx.detach().clone().requires_grad_(True))]
         main = torch.cuda.current_stream()
         copy_stream = torch.cuda.Stream(device=device)
+        back_stream = torch.cuda.Stream(device=device)
         ready = [torch.cuda.Event() for _ in sets]
         free = [torch.cuda.Event() for _ in sets]
+        done = torch.cuda.Event()
 
         def load(k, after_use):
             with torch.cuda.stream(copy_stream):
@@ -608,6 +663,7 @@ def main():
 
         def e2e_steps(n):
             copy_stream.wait_stream(main)
+            back_stream.wait_stream(main)
             for k in range(min(n, 2)):
                 load(k, False)
             for i in range(n):
@@ -615,12 +671,20 @@ def main():
                 main.wait_event(ready[k])
                 xs, fs = sets[k]
                 zero_grads(xs, fs, W, b, tau)
-                coupling_step(K, xs, fs, W, b, tau, r, group)
+                out = coupling_step(K, xs, fs, W, b, tau, r, group)
                 free[k].record(main)
+                done.record(main)
+                with torch.cuda.stream(back_stream):
+                    back_stream.wait_event(done)
+                    with torch.no_grad():
+                        res = [out, xs.grad, fs.grad] + [t.grad for t in params]
+                        for o, t in zip(pt_host + outs, res):
+                            # the allocator keeps t's memory until the copy is done
+                            t.record_stream(back_stream)
+                            o.copy_(t, non_blocking=True)
                 if i + 2 < n:
                     load(k, True)
-                for o, t in zip(outs, params):
-                    o.copy_(t.grad, non_blocking=True)
+            main.wait_stream(back_stream)
 
         e2e_steps(2)
         torch.cuda.synchronize()
@@ -641,9 +705,11 @@ def main():
                "h2d_bytes_per_step": (xh.numel() * xh.element_size()
                                       + fh.numel() * fh.element_size()),
                "d2h_bytes_per_step": res_bytes,
-               "path": "fused_coupling + autograd, inputs copied from pinned host "
-                       "memory and parameter gradients read back every step (the next "
-                       "step's host copy overlaps this step's compute)"}
+               "path": "fused_coupling + autograd; every step copies x_mid and fx_mid in "
+                       "from pinned host memory and copies out, dx_mid, dfx_mid and the "
+                       "parameter gradients back to pinned host memory (the next step's "
+                       "inputs and the last step's results cross PCIe while a step "
+                       "computes)"}
 
     # per-op device times of the same round, for the roofline
     dot = K.slice_ops._dot_mode(x)
@@ -689,9 +755,40 @@ def main():
                     "op_ms": {k: round(v, 4) for k, v in opt.items()},
                     "round_frac": round(round_bytes / (ms * 1e-3) / 1e9 / peak, 4)}
 
+    # the reference's surface (op by op) and the reverse call order, same inputs
+    extra = {}
+    if world == 1 and not K.slice_ops._use_blocked(cfg["D"], cfg["G"], cfg["DV"], dot,
+                                                    x.device):
+        def obo():
+            zero_grads(x, fx, W, b, tau)
+            op_by_op_step(K, x, fx, W, b, tau, r)
+
+        t = timed_rounds(obo, args.steps)
+        extra["op_by_op"] = {
+            "value": round(points / (t * 1e-3) / 1e6, 3), "unit": UNIT, "ms_per_step": round(t, 4),
+            "round_frac": round(sum(UNITS.values()) * unit_bytes / (t * 1e-3) / 1e9 / peak, 4),
+            "path": "fused_slice + fused_deslice + autograd (the reference's surface: slice "
+                    "forward, deslice forward, deslice backward, slice backward, dx summed)"}
+        gen = torch.Generator(device=device).manual_seed(4321)
+        shp = (cfg["B"], cfg["H"], cfg["G"], cfg["DV"])
+        tok = torch.randn(*shp, generator=gen, device=device).requires_grad_(True)
+        rz = torch.randn(*shp, generator=gen, device=device)
+        rs = torch.randn(*shp[:3], generator=gen, device=device)
+
+        def rev():
+            zero_grads(x, fx, W, b, tau, tok)
+            reverse_step(K, x, fx, W, b, tau, tok, r, rz, rs)
+
+        t = timed_rounds(rev, args.steps)
+        extra["reverse_order"] = {
+            "value": round(points / (t * 1e-3) / 1e6, 3), "unit": UNIT,
+            "ms_per_step": round(t, 4),
+            "path": "fused_deslice(return_stats=True) then fused_slice(stats=...) of the same "
+                    "points, forward and backward; tokens ~ N(0, 1)"}
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        cpu = cpu_baseline(cfg, min(args.cpu_sample, cfg["N"]))
+        cpu = cpu_baseline(cfg, cpu_sample(args, cfg))
 
     if rank == 0:
         line = {"metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world,
@@ -707,7 +804,7 @@ def main():
                            "l2": "inputs larger than L2 (%d MiB per point tensor), no flush"
                                  % (unit_bytes >> 20)},
                 "e2e": e2e, "gpu_launches": int(launches), "roofline": roofline,
-                "cpu_baseline": cpu, "clocks": clk}
+                "cpu_baseline": cpu, "clocks": clk, **extra}
         print(json.dumps(line), flush=True)
     if group is not None:
         import torch.distributed as dist

@@ -20,7 +20,7 @@ import torch
 
 from . import _native as nat
 from . import _state
-from .slice_ops import (native_deslice, native_deslice_bwd, native_slice,  # noqa: F401
+from .slice_ops import (_fresh, native_deslice, native_deslice_bwd, native_slice,  # noqa: F401
                         native_slice_bwd, native_stats, set_tile_table, tile_table)
 
 
@@ -113,8 +113,8 @@ def _(x_mid, fx_mid, weight, bias, tau, stats, dot):
 
 @torch.library.register_fake("flashslice::slice_blk_bwd")
 def _(x_mid, fx_mid, weight, bias, tau, stats, dz_num, ds, dot):
-    return (torch.empty_like(x_mid), torch.empty_like(fx_mid), torch.empty_like(weight),
-            torch.empty_like(bias), torch.empty_like(tau))
+    return (torch.empty_like(x_mid), torch.empty_like(fx_mid), _fresh(weight), _fresh(bias),
+            _fresh(tau))
 
 
 @torch.library.register_fake("flashslice::deslice_blk")
@@ -126,8 +126,8 @@ def _(x_mid, weight, bias, tau, tokens, stats, dot):
 
 @torch.library.register_fake("flashslice::deslice_blk_bwd")
 def _(x_mid, weight, bias, tau, tokens, stats, d_out, dot):
-    return (torch.empty_like(x_mid), torch.empty_like(tokens), torch.empty_like(weight),
-            torch.empty_like(bias), torch.empty_like(tau))
+    return (torch.empty_like(x_mid), _fresh(tokens), _fresh(weight), _fresh(bias),
+            _fresh(tau))
 
 
 def _slice_setup(ctx, inputs, output):

@@ -523,10 +523,18 @@ def _(x_mid, fx_mid, weight, bias, tau, dot):
             x_mid.new_empty((B, H, G), dtype=torch.float32))
 
 
+def _fresh(t):
+    """An output in t's shape, dtype and device with contiguous strides: the
+    parameter and token gradients come back contiguous whatever the input's
+    strides (a permuted per-sample weight included), as the CUDA impls make
+    them, so that compiled graphs see the strides the kernels produce."""
+    return t.new_empty(t.shape)
+
+
 @torch.library.register_fake("flashslice::flash_slice_bwd")
 def _(x_mid, fx_mid, weight, bias, tau, dz_num, ds, dot):
-    return (torch.empty_like(x_mid), torch.empty_like(fx_mid), torch.empty_like(weight),
-            torch.empty_like(bias), torch.empty_like(tau))
+    return (torch.empty_like(x_mid), torch.empty_like(fx_mid), _fresh(weight), _fresh(bias),
+            _fresh(tau))
 
 
 @torch.library.register_fake("flashslice::flash_deslice")
@@ -537,14 +545,14 @@ def _(x_mid, weight, bias, tau, tokens, dot):
 
 @torch.library.register_fake("flashslice::flash_deslice_bwd")
 def _(x_mid, weight, bias, tau, tokens, d_out, dot):
-    return (torch.empty_like(x_mid), torch.empty_like(tokens), torch.empty_like(weight),
-            torch.empty_like(bias), torch.empty_like(tau))
+    return (torch.empty_like(x_mid), _fresh(tokens), _fresh(weight), _fresh(bias),
+            _fresh(tau))
 
 
 @torch.library.register_fake("flashslice::coupled_bwd")
 def _(x_mid, fx_mid, d_out, weight, bias, tau, tokens, dz_num, ds, dot):
-    return (torch.empty_like(x_mid), torch.empty_like(fx_mid), torch.empty_like(weight),
-            torch.empty_like(bias), torch.empty_like(tau))
+    return (torch.empty_like(x_mid), torch.empty_like(fx_mid), _fresh(weight), _fresh(bias),
+            _fresh(tau))
 
 
 def _slice_setup(ctx, inputs, output):
@@ -693,8 +701,12 @@ def fused_coupling(x_mid, fx_mid, weight, bias, tau, mix=None, mix_params=None, 
     params = tuple(q for q in mix_params if q.requires_grad)
     if group is not None and torch.distributed.get_world_size(group) == 1:
         group = None
+    # Under torch.compile the round is the plain composition of the custom
+    # ops (each with its registered autograd), which traces into one graph
+    # with its backward; the tied backward's autograd.Function runs a Python
+    # mix through torch.autograd.grad, which a compiled graph cannot hold.
     if _ops is None and (_use_blocked(D, G, DV, dot, x_mid.device) or
-                         not torch.is_grad_enabled()):
+                         not torch.is_grad_enabled() or torch.compiler.is_compiling()):
         if group is not None:
             from ..sharded import sharded_coupling
             return sharded_coupling(x_mid, fx_mid, weight, bias, tau, mix, eps, group)

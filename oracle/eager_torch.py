@@ -8,7 +8,8 @@ deslice as einsums, the backward by torch autograd. In fp32 this is the
 ``bench.py`` times it (all host threads) as the CPU baseline of the
 slice -> normalise -> identity mix -> deslice coupling round.
 
-Nothing here runs on the GPU or in the product path.
+The GPU parity tests also run it on device tensors, as their checker; it
+never runs in the product path.
 """
 
 import torch

@@ -83,3 +83,27 @@ def test_blocked_coupling_hands_statistics_to_the_deslice():
             break
         node = node.args[0]
     assert node.args[0] is sl[0] and node.args[1] == 2
+
+
+def test_fake_parameter_gradients_are_contiguous_for_a_permuted_weight():
+    """The reference's per-sample weight is a permuted view (tokens @ Wk viewed
+    (B, G, H, D) and permuted to (B, H, G, D)); the CUDA impls return its
+    gradient contiguous, and so must the fakes, or a compiled graph's stride
+    checks would fail on the real output."""
+    with FakeTensorMode():
+        L = _leaves(G=32, DV=32, dtype=torch.float32)
+        x, fx, b, tau = L["x"], L["fx"], L["b"], L["tau"]
+        Wp = torch.empty(2, 32, 4, 32, device="cuda").permute(0, 2, 1, 3)
+        assert not Wp.is_contiguous()
+        z, s = ops.flash_slice(x, fx, Wp, b, tau, 0)
+        for g in (ops.flash_slice_bwd(x, fx, Wp, b, tau, z, s, 0),
+                  ops.flash_deslice_bwd(x, Wp, b, tau, z, x, 0),
+                  ops.coupled_bwd(x, fx, x, Wp, b, tau, z, z, s, 0)):
+            assert g[2].shape == Wp.shape and g[2].is_contiguous()
+        Lb = _leaves()
+        Wb = torch.empty(2, 1024, 4, 32, device="cuda").permute(0, 2, 1, 3)
+        z, s, st = ops.slice_blk(Lb["x"], Lb["fx"], Wb, Lb["b"], Lb["tau"], None, 3)
+        g = ops.slice_blk_bwd(Lb["x"], Lb["fx"], Wb, Lb["b"], Lb["tau"], st, z, s, 3)
+        assert g[2].is_contiguous()
+        g = ops.deslice_blk_bwd(Lb["x"], Wb, Lb["b"], Lb["tau"], Lb["tok"], st, Lb["dout"], 3)
+        assert g[2].is_contiguous()
