@@ -43,50 +43,61 @@ def _no_breaks(fn, *args):
     assert exp.graph_count == 1, exp.graph_count
 
 
+def _gate_vs_truth(got, ref_eager, truth):
+    """Compiled fused results against the float64 truth, at least nearly as
+    close as the reference's fp32 eager path (the gate of the layer tests:
+    the temperature gradients are cancellations, so a fixed relative bound
+    between two fp32 evaluations says little about them)."""
+    assert set(got) == set(truth), set(got) ^ set(truth)
+    for k in truth:
+        ef, ee = relerr(got[k], truth[k]), relerr(ref_eager[k], truth[k])
+        assert ef <= max(2.0 * ee, 1e-5), (k, ef, ee)
+
+
 @pytest.mark.parametrize("kw", [{}, {"no_token_attention": True}, {"untied_deslice": True}],
                          ids=["tied", "notokattn", "untied"])
 def test_layer_compiles_into_one_graph_with_its_backward(cuda_device, kw):
     torch.backends.cuda.matmul.allow_tf32 = False
     from flashslice_b200 import Physics_Attention_Irregular_Mesh
     torch.manual_seed(0)
-    layer = Physics_Attention_Irregular_Mesh(128, heads=4, dim_head=32, slice_num=32,
-                                             use_fused_slice=True, **kw).cuda()
+    mk = lambda fused: Physics_Attention_Irregular_Mesh(  # noqa: E731
+        128, heads=4, dim_head=32, slice_num=32, use_fused_slice=fused, **kw)
+    layer = mk(True)
+    eager, truth = mk(False), mk(False)
+    eager.load_state_dict(layer.state_dict())
+    truth.load_state_dict(layer.state_dict())
+    layer, eager, truth = layer.cuda(), eager.cuda(), truth.double().cuda()
     assert layer.use_fused_slice
     g = torch.Generator().manual_seed(1)
     x = torch.randn(2, 3000, 128, generator=g).cuda()
     up = torch.randn(2, 3000, 128, generator=g).cuda()
     _no_breaks(layer, x)
-    ref = _module_run(layer, [x], up)
     torch._dynamo.reset()
-    comp = torch.compile(layer, fullgraph=True)
-    got = _module_run(comp, [x], up)
-    assert set(got) == set(ref)
-    # compiled (op-by-op backward, inductor-fused elementwise work) against
-    # eager (the tied backward): the same exact-fp32 products, summed in
-    # another order
-    for k in ref:
-        assert relerr(got[k], ref[k]) <= 2e-5, (k, relerr(got[k], ref[k]))
+    got = _module_run(torch.compile(layer, fullgraph=True), [x], up)
+    _gate_vs_truth(got, _module_run(eager, [x], up),
+                   _module_run(truth, [x.double()], up.double()))
 
 
 def test_transolver_compiles_into_one_graph_with_its_backward(cuda_device):
     torch.backends.cuda.matmul.allow_tf32 = False
     from flashslice_b200 import Transolver
     torch.manual_seed(3)
-    model = Transolver(space_dim=3, fun_dim=1, out_dim=4, n_hidden=128, n_heads=4,
-                       n_layers=2, slice_num=32, use_fused_slice=True).cuda()
+    kw = dict(space_dim=3, fun_dim=1, out_dim=4, n_hidden=128, n_heads=4, n_layers=2,
+              slice_num=32)
+    model = Transolver(use_fused_slice=True, **kw)
+    eager, truth = Transolver(**kw), Transolver(**kw)
+    eager.load_state_dict(model.state_dict())
+    truth.load_state_dict(model.state_dict())
+    model, eager, truth = model.cuda(), eager.cuda(), truth.double().cuda()
     g = torch.Generator().manual_seed(4)
     xc = torch.rand(1, 3000, 3, generator=g).cuda()
     fv = torch.randn(1, 3000, 1, generator=g).cuda()
     up = torch.randn(1, 3000, 4, generator=g).cuda()
     _no_breaks(model, xc, fv)
-    ref = _module_run(model, [xc, fv], up)
     torch._dynamo.reset()
-    comp = torch.compile(model, fullgraph=True)
-    got = _module_run(comp, [xc, fv], up)
-    assert set(got) == set(ref)
-    # two layers of inductor-fused layer norms and MLPs around the ops
-    for k in ref:
-        assert relerr(got[k], ref[k]) <= 1e-4, (k, relerr(got[k], ref[k]))
+    got = _module_run(torch.compile(model, fullgraph=True), [xc, fv], up)
+    _gate_vs_truth(got, _module_run(eager, [xc, fv], up),
+                   _module_run(truth, [xc.double(), fv.double()], up.double()))
 
 
 @pytest.mark.parametrize("G,dt", [(32, torch.float32), (64, torch.float32),
