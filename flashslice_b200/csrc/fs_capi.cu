@@ -125,6 +125,14 @@ bool tc_shape(const fs_problem& p) {
          p.D == 32 && p.DV == 32 && p.G == 32 && p.N >= 1;
 }
 
+// The G = 64 tensor-core kernels: the single-tile family with D = DV = 32
+// and 64 slots (config 5's shape), fp32 or bf16 point tensors, no statistics.
+bool tc64_shape(const fs_problem& p) {
+  return p.engine == FS_ENGINE_AUTO && p.family == FS_FAMILY_SINGLE &&
+         (p.act_dtype == FS_F32 || p.act_dtype == FS_BF16) && p.D == 32 && p.DV == 32 &&
+         p.G == 64 && p.N >= 1 && !p.flags;
+}
+
 // The slot-owning slice forward on the tensor cores (shapes past the single
 // tile, either family): bf16 point tensors in the bf16 dot mode (the value
 // dot rounds the weights w to bf16, blocked.py), D = 32, DV = 32 or 64, G a
@@ -559,6 +567,15 @@ int fs_slice_fwd(const fs_problem* p, const fs_tensor4* x_mid, const fs_tensor4*
     P = tq.P;
     route_note("slice_fwd", "tensor-core", *p, x_mid, fx_mid);
     FS_TRY(tcx::run_tc(tcx::TcKind::SliceFwd, tq, st));
+  } else if (tc64_shape(*p) && tc_tensor_ok(x_mid) && tc_tensor_ok(fx_mid) &&
+             tc_params(*p, tcx::TcKind::SliceFwd64, x_mid, fx_mid, weight, bias, tau, tq)) {
+    // partials of the slot-blocked layout: at most s.Pg programs per (b, h)
+    if (tq.P > s.Pg) tq.P = s.Pg;
+    tq.partA = q.partA;
+    tq.partS = q.partS;
+    P = tq.P;
+    route_note("slice_fwd", "tensor-core-g64", *p, x_mid, fx_mid);
+    FS_TRY(tcx::run_tc(tcx::TcKind::SliceFwd64, tq, st));
   } else if (p->row_splits) {
     return ragged_unsupported("slice forward");
   } else if (s.fused) {

@@ -2173,6 +2173,254 @@ __global__ void __launch_bounds__(256, 2) k_tc_blk_pown_bf16(const __grid_consta
   epilogue<256>(c);
 }
 
+// ------------------------------------------------------------ G = 64
+// The single-tile family at G = 64 with D = DV = 32 (config 5's shape): the
+// same exact three-part products as the G = 32 kernels above, with the 64
+// slots of a row split over its two threads (thread cs owns slots
+// [32 cs, 32 cs + 32)). Point tensors still have 32 values a row, so the
+// point operands (x, fx, d_out) are split and staged exactly as at G = 32.
+//  * logits = x W^T with W's three parts of 64 rows (K-major, +0, +4096,
+//    +8192): the NW = 64 schedule with N = 128 ([x W_mid | x W_hi]), eight
+//    MMAs;
+//  * pools are formed transposed, D[point-operand parts][slot parts]: the
+//    point operand's parts stacked along M ([lo; mid; hi; ones], the ones
+//    row giving the plain sums s or db), the slot operand's three parts of
+//    64 slots stacked along N (N = 192): one MMA per 16 points, all nine
+//    partial products; the threads drain each tile's pool into fp32
+//    registers, adding the slot parts small first, and the point operand's
+//    parts are added once, at the end.
+constexpr int kRS4 = 2048;               // point split with a ones part: 8-row group stride
+constexpr int kSplit4 = 16 * kRS4;       // 32 KB
+constexpr int kRSW = 3072;               // 64-slot split, N-stacked: 8-row group stride
+constexpr int kSplitW = 16 * kRSW;       // 48 KB
+constexpr int kSmall64 = 3 * 4096;       // a 64 x 32 matrix, three K-major parts
+constexpr uint32_t kIdPool64 = idesc_bf16(128, 192, 1, 1);
+
+// A 64 x 32 fp32 matrix M (row-major) split into three K-major parts (rows
+// r, k = c) at +0 (lo), +4096 (mid), +8192 (hi).
+template <int NT>
+__device__ __forceinline__ void put_small64(uint8_t* dst, const float* M) {
+  for (int i = threadIdx.x; i < 64 * 32; i += NT) {
+    const int r = i >> 5, c = i & 31;
+    __nv_bfloat16 h, m, l;
+    split3(M[i], h, m, l);
+    const uint32_t o = kmajor_off(r, c, 32);
+    *(__nv_bfloat16*)(dst + o) = l;
+    *(__nv_bfloat16*)(dst + 4096 + o) = m;
+    *(__nv_bfloat16*)(dst + 8192 + o) = h;
+  }
+}
+
+// Per-head row constants for 64 slots (bias2 holds 64 floats).
+template <int NT>
+__device__ __forceinline__ RowConst row_const64(float* bias_s, const float* bias, float tau) {
+  const float scale = __frcp_rn(tau) * kLog2e;
+  if (threadIdx.x < 64) bias_s[threadIdx.x] = bias[threadIdx.x] * scale;
+  return RowConst{scale, bias_s};
+}
+
+// D (128 x 128) = [x W_mid | x W_hi], A = the point operand in TMEM at a
+// (parts lo, mid, hi at +0, +16, +32 columns, K = 32), bd = the 64-row
+// small operand: A lo and mid times [W_mid | W_hi], A hi times W_lo into
+// the W_mid group, A hi times [W_mid | W_hi] -- seven of the nine partial
+// products (the two left out are below 2^-26 of the result), small first.
+__device__ __forceinline__ void logits64(uint32_t d, uint32_t a, uint64_t bd) {
+  constexpr uint32_t id128 = idesc_bf16(128, 128, 0, 0), id64 = idesc_bf16(128, 64, 0, 0);
+#pragma unroll
+  for (int pa = 0; pa < 2; ++pa)
+#pragma unroll
+    for (int ks = 0; ks < 2; ++ks)
+      mma_ts(d, a + pa * 16 + ks * 8, bd + ((4096 + ks * 256) >> 4), id128, (pa | ks) != 0);
+#pragma unroll
+  for (int ks = 0; ks < 2; ++ks) mma_ts(d, a + 32 + ks * 8, bd + ((ks * 256) >> 4), id64, true);
+#pragma unroll
+  for (int ks = 0; ks < 2; ++ks)
+    mma_ts(d, a + 32 + ks * 8, bd + ((4096 + ks * 256) >> 4), id128, true);
+}
+
+// This thread's 32 logits (slots 32 cs ..) from the [W_mid | W_hi] groups.
+__device__ __forceinline__ void ld_logits64(uint32_t taddr, int cs, float (&v)[32]) {
+#pragma unroll
+  for (int hf = 0; hf < 2; ++hf) {
+    uint32_t a[16], b[16];
+    tld<16>(taddr + 32 * cs + 16 * hf, a);
+    tld<16>(taddr + 64 + 32 * cs + 16 * hf, b);
+    tld_wait();
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      put2(v, 8 * hf + k,
+           __fadd2_rn(make_float2(__uint_as_float(a[2 * k]), __uint_as_float(a[2 * k + 1])),
+                      make_float2(__uint_as_float(b[2 * k]), __uint_as_float(b[2 * k + 1]))));
+  }
+}
+
+// A point row's 16 values (columns 16 cs ..) split into a stacked buffer
+// with a ones part: per 8-row group lo, mid, hi, ones at +0, +512, +1024,
+// +1536 (the M-stacked operand [lo; mid; hi; ones] of a transposed pool).
+__device__ __forceinline__ void split_to_smem4(const Split<16>& sp, uint8_t* buf, int row, int cs) {
+  uint8_t* base = buf + (row >> 3) * kRS4 + (row & 7) * 16;
+  const uint4 ones = make_uint4(0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u);
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int j = 2 * cs + i;
+    *(uint4*)(base + j * 128) = make_uint4(sp.lw[4 * i], sp.lw[4 * i + 1], sp.lw[4 * i + 2], sp.lw[4 * i + 3]);
+    *(uint4*)(base + 512 + j * 128) = make_uint4(sp.mw[4 * i], sp.mw[4 * i + 1], sp.mw[4 * i + 2], sp.mw[4 * i + 3]);
+    *(uint4*)(base + 1024 + j * 128) = make_uint4(sp.hw[4 * i], sp.hw[4 * i + 1], sp.hw[4 * i + 2], sp.hw[4 * i + 3]);
+    *(uint4*)(base + 1536 + j * 128) = ones;
+  }
+}
+
+// A row's 32 slot values (slots 32 cs ..) split into the N-stacked 64-slot
+// buffer: per 8-row group the lo, mid, hi parts of the 64 slots (128 bytes
+// each, 8 core matrices) at +0, +1024, +2048.
+__device__ __forceinline__ void split_to_smemw(const Split<32>& sp, uint8_t* buf, int row, int cs) {
+  uint8_t* base = buf + (row >> 3) * kRSW + (row & 7) * 16;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int j = 4 * cs + i;
+    *(uint4*)(base + j * 128) = make_uint4(sp.lw[4 * i], sp.lw[4 * i + 1], sp.lw[4 * i + 2], sp.lw[4 * i + 3]);
+    *(uint4*)(base + 1024 + j * 128) = make_uint4(sp.mw[4 * i], sp.mw[4 * i + 1], sp.mw[4 * i + 2], sp.mw[4 * i + 3]);
+    *(uint4*)(base + 2048 + j * 128) = make_uint4(sp.hw[4 * i], sp.hw[4 * i + 1], sp.hw[4 * i + 2], sp.hw[4 * i + 3]);
+  }
+}
+
+// D (128 x 192) = transposed pool over the tile's points: A = the stacked
+// point buffer with a ones part (M-stacked), B = the N-stacked 64-slot
+// buffer; eight K steps of 16 points.
+__device__ __forceinline__ void mma_pool64(uint32_t d, const uint8_t* a, const uint8_t* b) {
+  const uint64_t ad = smem_desc(smem_u32(a), kRS4, 128), bd = smem_desc(smem_u32(b), kRSW, 128);
+#pragma unroll
+  for (int ks = 0; ks < 8; ++ks)
+    mma_bf16(d, ad + ((ks * 2 * kRS4) >> 4), bd + ((ks * 2 * kRSW) >> 4), kIdPool64, ks > 0);
+}
+
+// Add this thread's 32 columns of its pool row (slots 32 cs .. of the slot
+// parts lo, mid, hi, small first) into acc.
+__device__ __forceinline__ void drain_pool64(uint32_t taddr, int cs, float (&acc)[32]) {
+#pragma unroll
+  for (int hf = 0; hf < 2; ++hf) {
+    uint32_t a[16], b[16], c[16];
+    tld<16>(taddr + 32 * cs + 16 * hf, a);
+    tld<16>(taddr + 64 + 32 * cs + 16 * hf, b);
+    tld<16>(taddr + 128 + 32 * cs + 16 * hf, c);
+    tld_wait();
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float2 s = __fadd2_rn(
+          __fadd2_rn(make_float2(__uint_as_float(a[2 * k]), __uint_as_float(a[2 * k + 1])),
+                     make_float2(__uint_as_float(b[2 * k]), __uint_as_float(b[2 * k + 1]))),
+          make_float2(__uint_as_float(c[2 * k]), __uint_as_float(c[2 * k + 1])));
+      put2(acc, 8 * hf + k, __fadd2_rn(f2(acc, 8 * hf + k), s));
+    }
+  }
+}
+
+// Transposed pool partials: thread (q, cs) with TMEM lane 32 q + t holds,
+// for point-operand part q (q = 3: the ones row) and value t, its sums over
+// slots 32 cs + i. Writes part[g][c] = (lo + mid) + hi for the 64 x 32
+// partial, and the plain sums (ones row) into sums[g] when sums is given;
+// xch holds 3 x 32 x 65 floats.
+__device__ __forceinline__ void pool64_write(float* xch, const float (&acc)[32], float* part,
+                                             float* sums, const Th<2>& th) {
+  const int t = threadIdx.x & 31;
+  __syncthreads();
+  if (th.q < 3) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) xch[(th.q * 32 + t) * 65 + 32 * th.cs + i] = acc[i];
+  } else if (sums && t == 0) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) sums[32 * th.cs + i] = acc[i];
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < 64 * 32; i += 256) {
+    const int g = i >> 5, c = i & 31;
+    part[i] = (xch[c * 65 + g] + xch[(32 + c) * 65 + g]) + xch[(64 + c) * 65 + g];
+  }
+}
+
+// ------------------------------------------------------------ slice forward, G = 64
+// One CTA of 256 threads (two per point row), two CTAs per SM; the phases
+// of a tile run in turn (the co-resident CTA fills the gaps).
+// smem: [stage x][F: fx staged, then its split with a ones part][WS: w, 64
+//       slots][W][bias][red][bars]
+// TMEM (256 columns): logits at 0 (128), the z pool at 0 (192, once the
+// logits are read), the x point operand at 192.
+constexpr int kS6StageX = 0, kS6F = kStage, kS6WS = kS6F + kSplit4, kS6Ws = kS6WS + kSplitW,
+              kS6Bias = kS6Ws + kSmall64, kS6Red = kS6Bias + 256,
+              kS6Bar = kS6Red + red_bytes(2, 2), kS6Bytes = kS6Bar + kBarBytes;
+static_assert(kS6F % 1024 == 0, "fx staging tile needs 1 KB alignment");
+
+template <typename PT>
+__global__ void __launch_bounds__(256, 2) k_tc_slice_fwd64(const __grid_constant__ TcParams p) {
+  constexpr int T = 2, NT = 256;
+  extern __shared__ __align__(16) uint8_t sm_raw[];
+  uint8_t* sm = align_smem(sm_raw);
+  const Th<T> th;
+  const int bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
+  const Span sp = span_of(p, b);
+  Ctl c = prologue_begin<256>(sm, kS6Bar);
+  float* red = (float*)(sm + kS6Red);
+  put_small64<NT>(sm + kS6Ws, p.W + (int64_t)b * p.swb + (int64_t)h * p.swh);
+  const RowConst rc = row_const64<NT>((float*)(sm + kS6Bias),
+                                      p.bias + (int64_t)b * p.sbb + (int64_t)h * p.sbh, p.tau[h]);
+  prologue_end(c);
+  const uint32_t tL = c.tmem, tP = c.tmem, tX = c.tmem + 192;
+  const uint64_t dWs = desc_smallK(sm + kS6Ws);
+  uint8_t* stX = sm + kS6StageX;
+  uint8_t* F = sm + kS6F;
+  uint8_t* WS = sm + kS6WS;
+  float acc[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) acc[i] = 0.f;
+  int tile = blockIdx.x;
+  if (threadIdx.x == 0 && tile < sp.ntiles) tma_tile<PT>(p, stX, F, h, sp, tile, c.bar);
+  for (; tile < sp.ntiles; tile += p.P) {
+    const int n0 = tile * kTile;
+    const bool more = tile + p.P < sp.ntiles;
+    wait_bar(c, kBarTma, p.status);
+    RowVals<16, PT> x, f;
+    x.load(stX, th.row, th.cs);
+    f.load(F, th.row, th.cs);
+    // every staged fx row is in registers before F is overwritten, and the
+    // last tile's pool is read out of TMEM before the logits overwrite it
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    x.split().to_tmem(tX + th.lane_off, th.cs);
+    split_to_smem4(f.split(), F, th.row, th.cs);
+    tst_wait();
+    to_async_barrier();
+    if (threadIdx.x == 0) {
+      if (more) {  // the next tile's x now, its fx once the pool is done with F
+        mbar_arrive_expect_tx(c.bar + kBarTma, 2 * stage_bytes<PT>());
+        tma_load_4d(stX, &p.mx, 0, h, sp.row(tile + p.P), sp.bc, c.bar + kBarTma);
+      }
+      logits64(tL, tX, dWs);
+      commit(c, kG1);
+    }
+    wait_bar(c, kG1, p.status);
+    {
+      float lg[32];
+      ld_logits64(tL + th.lane_off, th.cs, lg);
+      softmax_fwd<T, 32>(lg, rc, n0 + th.row < sp.N, red, th);
+      split_to_smemw(Split<32>(lg), WS, th.row, th.cs);
+    }
+    to_async_barrier();
+    if (threadIdx.x == 0) {
+      mma_pool64(tP, F, WS);  // [fx; 1]^T w
+      commit(c, kG2);
+    }
+    wait_bar(c, kG2, p.status);
+    if (threadIdx.x == 0 && more)
+      tma_load_4d(F, &p.mv, 0, h, sp.row(tile + p.P), sp.bc, c.bar + kBarTma);
+    drain_pool64(tP + th.lane_off, th.cs, acc);
+  }
+  const int64_t slot = (int64_t)bh * p.P + blockIdx.x;
+  tc_fence_before();
+  pool64_write((float*)WS, acc, p.partA + slot * 64 * 32, p.partS + slot * 64, th);
+  epilogue<256>(c);
+}
+
 // ------------------------------------------------------------ wait self-test
 // One thread waits, with a limit of limit_ns, on an mbarrier that nothing
 // arrives at: the bounded-wait path of the kernels (status word set, the
@@ -2278,6 +2526,8 @@ static cudaError_t run_tc_t(TcKind k, const TcParams& p, cudaStream_t s) {
       return launch_tc(k_tc_deslice_bwd<PT>, kTDesliceBwd, kDbBytes, p, s);
     case TcKind::CoupledBwd:
       return launch_tc(k_tc_coupled_bwd<PT>, kTCoupledBwd, kCbBytes, p, s);
+    case TcKind::SliceFwd64: return launch_tc(k_tc_slice_fwd64<PT>, 2, kS6Bytes, p, s);
+    default: break;
   }
   return cudaErrorInvalidValue;
 }
@@ -2363,6 +2613,9 @@ int tc_ctas_per_sm(TcKind k) {
     case TcKind::BlkDesliceFwd:
     case TcKind::BlkStats:
     case TcKind::BlkStatsOnline: return 2;
+    case TcKind::SliceFwd64: return 2;
+    case TcKind::DesliceFwd64: return 2;
+    case TcKind::CoupledBwd64: return 1;
   }
   return 1;
 }
@@ -2379,6 +2632,7 @@ static_assert((kDfBytes + kSmemPad + 1024) * kCtasDesliceFwd <= 228 * 1024, "des
 static_assert((kSbBytes + kSmemPad + 1024) * kCtasSliceBwd <= 228 * 1024, "slice bwd smem");
 static_assert((kDbBytes + kSmemPad + 1024) * kCtasDesliceBwd <= 228 * 1024, "deslice bwd smem");
 static_assert((kCbBytes + kSmemPad + 1024) * kCtasCoupledBwd <= 228 * 1024, "coupled bwd smem");
+static_assert((kS6Bytes + kSmemPad + 1024) * 2 <= 228 * 1024, "slice fwd G=64 smem");
 // TMEM per SM (512 columns) holds the co-resident CTAs' allocations
 static_assert(256 * kCtasSliceFwd <= 512 && kDfCols * kCtasDesliceFwd <= 512 &&
                   256 * kCtasSliceBwd <= 512 && 256 * kCtasDesliceBwd <= 512,

@@ -26,6 +26,9 @@ enum class TcKind {
   BlkDesliceFwd,   // blocked point-owning deslice forward with statistics, bf16 dots
   BlkStats,        // blocked per-point statistics (m, l), two passes, bf16 points
   BlkStatsOnline,  // the same statistics online, one pass
+  SliceFwd64,      // single-tile family at G = 64 (D = DV = 32): slice forward
+  DesliceFwd64,    // ... deslice forward
+  CoupledBwd64,    // ... coupled backward of a round
 };
 
 constexpr int kMaxSplits = 128;  // FS_MAX_SPLITS
@@ -44,9 +47,9 @@ struct TcParams {
   const float* bias;
   const float* tau;
   int64_t swb, swh, sbb, sbh;
-  const float* M;   // tokens or dz_num (B, H, 32, 32)
+  const float* M;   // tokens or dz_num (B, H, G, 32), G = 32 or 64
   const float* M2;  // dz_num of the coupled backward (M is tokens there)
-  const float* ds;  // (B, H, 32)
+  const float* ds;  // (B, H, G)
   void* out;        // deslice out / dx_mid (B, N, H, 32), element strides so
   int64_t so[4];
   void* out2;       // dfx_mid

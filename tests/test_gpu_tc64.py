@@ -1,0 +1,90 @@
+"""The G = 64 tensor-core kernels (the single-tile family at D = DV = 32 with
+64 slots: config 5's shape) against the exact-fp32 FMA kernels and the
+float64 truth, over weight layouts, ragged point counts, strided and bf16
+inputs; plus proof that the tensor-core path ran and no bounded device wait
+gave up."""
+
+import pytest
+import torch
+
+from parity import relerr
+
+pytestmark = pytest.mark.gpu
+
+G = 64
+
+
+@pytest.fixture(scope="module")
+def env(cuda_device):
+    torch.backends.cuda.matmul.allow_tf32 = False
+    import flashslice_b200.kernels as K
+    from flashslice_b200.kernels import _native as nat
+    from flashslice_b200.kernels import _state
+    lib = nat.load()
+    lib.fs_device_status(1)
+    return K, _state, lib
+
+
+def _inputs(N, mode, B=1, H=4, seed=3, strided=False):
+    g = torch.Generator().manual_seed(seed)
+    r = lambda *s: torch.randn(*s, generator=g, dtype=torch.float64)  # noqa: E731
+    x, fx = r(B, N, H, 32), r(B, N, H, 32)
+    if strided:
+        x = x.permute(0, 2, 1, 3).contiguous().permute(0, 2, 1, 3)
+    W = {"gd": r(G, 32), "hgd": r(H, G, 32), "bhgd": r(B, H, G, 32)}[mode] / 32 ** 0.5
+    b = {"gd": r(G), "hgd": r(H, G), "bhgd": r(B, H, G)}[mode] * 0.1
+    tau = 0.3 + 0.7 * torch.rand(H, generator=g, dtype=torch.float64)
+    tok = r(B, H, G, 32)
+    return [t.cuda() for t in (x, fx, W, b, tau, tok)]
+
+
+def _slice(K, st, engine, x, fx, W, b, tau, dt=torch.float32):
+    st.set_engine(engine)
+    try:
+        f = [t.to(dt) if i < 2 else t.float() for i, t in enumerate((x, fx, W, b, tau))]
+        z, s = K.fused_slice(*f)
+        torch.cuda.synchronize()
+        return z, s
+    finally:
+        st.set_engine("auto")
+
+
+@pytest.mark.parametrize("N", [1, 77, 129, 4097, 100_003])
+@pytest.mark.parametrize("mode", ["gd", "hgd", "bhgd"])
+def test_slice_forward_matches_exact_engine(env, N, mode):
+    K, st, lib = env
+    x, fx, W, b, tau, _ = _inputs(N, mode, B=2 if mode == "bhgd" else 1)
+    n0 = lib.fs_tc_launch_count()
+    tc = _slice(K, st, "auto", x, fx, W, b, tau)
+    assert lib.fs_tc_launch_count() - n0 == 1, "the tensor-core kernel did not run"
+    ex = _slice(K, st, "fma", x, fx, W, b, tau)
+    from oracle import eager_torch as E
+    z64, s64 = E.slice_fwd(x, fx, W, b, tau)
+    for name, a, e, ref in (("z_num", tc[0], ex[0], z64), ("s", tc[1], ex[1], s64)):
+        et, ee = relerr(a, ref), relerr(e, ref)
+        # the split products on the tensor cores are at least nearly as
+        # accurate as fp32 FMA
+        assert et <= max(2.0 * ee, 1e-6), (name, et, ee)
+        assert relerr(a, e) <= 1e-5, (name, relerr(a, e))
+    assert lib.fs_device_status(1) == 0
+
+
+def test_slice_forward_strided_bf16_deterministic(env):
+    K, st, lib = env
+    x, fx, W, b, tau, _ = _inputs(50_000, "hgd", B=2, strided=True)
+    assert not x.is_contiguous()
+    tc = _slice(K, st, "auto", x, fx, W, b, tau)
+    ex = _slice(K, st, "fma", x, fx, W, b, tau)
+    for a, e in zip(tc, ex):
+        assert relerr(a, e) <= 1e-5
+    again = _slice(K, st, "auto", x, fx, W, b, tau)
+    for a, c in zip(tc, again):
+        assert torch.equal(a, c)
+    # bf16 point tensors: the same exact products on the bf16 values
+    n0 = lib.fs_tc_launch_count()
+    tb = _slice(K, st, "auto", x, fx, W, b, tau, torch.bfloat16)
+    assert lib.fs_tc_launch_count() - n0 == 1
+    eb = _slice(K, st, "fma", x, fx, W, b, tau, torch.bfloat16)
+    for a, e in zip(tb, eb):
+        assert relerr(a, e) <= 1e-5
+    assert lib.fs_device_status(1) == 0
