@@ -641,6 +641,15 @@ int fs_deslice_fwd(const fs_problem* p, const fs_tensor4* x_mid, const float* we
     FS_TRY(tcx::run_tc(tcx::TcKind::DesliceFwd, tq, st));
     return FS_OK;
   }
+  if (tc64_shape(*p) && tc_tensor_ok(x_mid) && tc_tensor_ok(out) &&
+      tc_params(*p, tcx::TcKind::DesliceFwd64, x_mid, nullptr, weight, bias, tau, tq)) {
+    tq.M = tokens;
+    tq.out = out->data;
+    for (int i = 0; i < 4; ++i) tq.so[i] = out->stride[i];
+    route_note("deslice_fwd", "tensor-core-g64", *p, x_mid, out);
+    FS_TRY(tcx::run_tc(tcx::TcKind::DesliceFwd64, tq, st));
+    return FS_OK;
+  }
   if (p->row_splits) return ragged_unsupported("deslice forward");
   int P = s.Pn;  // no partials: any count serves
   // the blocked deslice with statistics: point-owning tensor-core kernel when

@@ -2421,6 +2421,117 @@ __global__ void __launch_bounds__(256, 2) k_tc_slice_fwd64(const __grid_constant
   epilogue<256>(c);
 }
 
+// ------------------------------------------------------------ deslice forward, G = 64
+// The 64-slot tokens as the N-stacked MN-major operand of out = w tokens
+// (K = 64 slots, in 8-row groups of 1536 bytes, parts at +0, +512, +1024).
+template <int NT>
+__device__ __forceinline__ void put_small_stacked64(uint8_t* dst, const float* M) {
+  for (int i = threadIdx.x; i < 64 * 32; i += NT) {
+    const int r = i >> 5, c = i & 31;
+    __nv_bfloat16 h, m, l;
+    split3(M[i], h, m, l);
+    const uint32_t o = (r >> 3) * kRS + (r & 7) * 16 + (c >> 3) * 128 + (c & 7) * 2;
+    *(__nv_bfloat16*)(dst + o) = l;
+    *(__nv_bfloat16*)(dst + 512 + o) = m;
+    *(__nv_bfloat16*)(dst + 1024 + o) = h;
+  }
+}
+
+// A row's 32 slot values (slots 32 cs ..) as this thread's part of a K = 64
+// point operand in TMEM: parts lo, mid, hi at +0, +32, +64 columns, two bf16
+// per column (even slot low), the thread's 16 columns at 16 cs.
+__device__ __forceinline__ void split_to_tmem64(const Split<32>& sp, uint32_t taddr, int cs) {
+  const uint32_t a = taddr + 16 * cs;
+  tst<16>(a, sp.lw);
+  tst<16>(a + 32, sp.mw);
+  tst<16>(a + 64, sp.hw);
+}
+
+// D (128 x 96) = A B^T with A = a K = 64 point operand in TMEM (parts at
+// +0, +32, +64) and B = an N-stacked MN-major 64-row operand at bd: twelve
+// MMAs, A parts lo, mid, hi one after the other (all nine partial products).
+__device__ __forceinline__ void wide64_mn96(uint32_t d, uint32_t a, uint64_t bd) {
+  constexpr uint32_t id = idesc_bf16(128, 96, 0, 1);
+#pragma unroll
+  for (int pa = 0; pa < 3; ++pa)
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks)
+      mma_ts(d, a + pa * 32 + ks * 8, bd + ((ks * 2 * kRS) >> 4), id, (pa | ks) != 0);
+}
+
+// smem: [stage x, two tiles][W][tokens][bias][red][bars]
+// TMEM (256 columns): logits at 0 (128), out at 0 (96, once the logits are
+// read), the x operand at 128 (48) and then the w operand at 128 (96).
+// Two x stages: the tile after next loads while this one is worked on.
+constexpr int kD6Stage = 0, kD6Ws = 2 * kStage, kD6Ts = kD6Ws + kSmall64,
+              kD6Bias = kD6Ts + 8 * kRS, kD6Red = kD6Bias + 256,
+              kD6Bar = kD6Red + red_bytes(2, 2), kD6Bytes = kD6Bar + kBarBytes;
+
+template <typename PT>
+__global__ void __launch_bounds__(256, 2) k_tc_deslice_fwd64(const __grid_constant__ TcParams p) {
+  constexpr int T = 2, NT = 256;
+  extern __shared__ __align__(16) uint8_t sm_raw[];
+  uint8_t* sm = align_smem(sm_raw);
+  const Th<T> th;
+  const int bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
+  const Span sp = span_of(p, b);
+  Ctl c = prologue_begin<256>(sm, kD6Bar);
+  float* red = (float*)(sm + kD6Red);
+  put_small64<NT>(sm + kD6Ws, p.W + (int64_t)b * p.swb + (int64_t)h * p.swh);
+  put_small_stacked64<NT>(sm + kD6Ts, p.M + (int64_t)bh * 64 * 32);
+  const RowConst rc = row_const64<NT>((float*)(sm + kD6Bias),
+                                      p.bias + (int64_t)b * p.sbb + (int64_t)h * p.sbh, p.tau[h]);
+  prologue_end(c);
+  const uint32_t tL = c.tmem, tO = c.tmem, tX = c.tmem + 128, tA = c.tmem + 128;
+  const uint64_t dWs = desc_smallK(sm + kD6Ws), dTs = desc_stacked(sm + kD6Ts);
+  auto stage = [&](int k) { return sm + kD6Stage + (k & 1) * kStage; };
+  // stage k & 1 completes on barrier kBarTma (even) or kG3 (odd)
+  auto sbar = [&](int k) { return (k & 1) ? kG3 : kBarTma; };
+  const int n_my = sp.ntiles > (int)blockIdx.x ? (sp.ntiles - 1 - (int)blockIdx.x) / p.P + 1 : 0;
+  if (threadIdx.x == 0) {
+    for (int k = 0; k < 2 && k < n_my; ++k)
+      tma_tile<PT>(p, stage(k), nullptr, h, sp, blockIdx.x + k * p.P, c.bar + sbar(k));
+  }
+  for (int k = 0; k < n_my; ++k) {
+    const int tile = blockIdx.x + k * p.P, n0 = tile * kTile;
+    wait_bar(c, sbar(k), p.status);
+    RowVals<16, PT> x;
+    x.load(stage(k), th.row, th.cs);
+    // the last tile's out is read out of TMEM before the logits overwrite it
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    x.split().to_tmem(tX + th.lane_off, th.cs);
+    tst_wait();
+    to_async_barrier();
+    if (threadIdx.x == 0) {
+      if (k + 2 < n_my)  // stage k & 1 is consumed: the tile after next
+        tma_tile<PT>(p, stage(k), nullptr, h, sp, tile + 2 * p.P, c.bar + sbar(k));
+      logits64(tL, tX, dWs);
+      commit(c, kG1);
+    }
+    wait_bar(c, kG1, p.status);
+    {
+      float lg[32];
+      ld_logits64(tL + th.lane_off, th.cs, lg);
+      softmax_fwd<T, 32>(lg, rc, true, red, th);
+      split_to_tmem64(Split<32>(lg), tA + th.lane_off, th.cs);  // over the consumed x operand
+      tst_wait();
+    }
+    to_async_barrier();
+    if (threadIdx.x == 0) {
+      wide64_mn96(tO, tA, dTs);  // out = w tokens, over the consumed logits
+      commit(c, kG2);
+    }
+    wait_bar(c, kG2, p.status);
+    store_result<96, 16>(tO, th.q, th.cs,
+                         (PT*)p.out + (int64_t)sp.bc * p.so[0] + (sp.n0 + n0) * p.so[1] +
+                             (int64_t)h * p.so[2],
+                         p.so[1], sp.N - n0);
+  }
+  epilogue<256>(c);
+}
+
 // ------------------------------------------------------------ wait self-test
 // One thread waits, with a limit of limit_ns, on an mbarrier that nothing
 // arrives at: the bounded-wait path of the kernels (status word set, the
@@ -2527,6 +2638,7 @@ static cudaError_t run_tc_t(TcKind k, const TcParams& p, cudaStream_t s) {
     case TcKind::CoupledBwd:
       return launch_tc(k_tc_coupled_bwd<PT>, kTCoupledBwd, kCbBytes, p, s);
     case TcKind::SliceFwd64: return launch_tc(k_tc_slice_fwd64<PT>, 2, kS6Bytes, p, s);
+    case TcKind::DesliceFwd64: return launch_tc(k_tc_deslice_fwd64<PT>, 2, kD6Bytes, p, s);
     default: break;
   }
   return cudaErrorInvalidValue;
@@ -2633,6 +2745,8 @@ static_assert((kSbBytes + kSmemPad + 1024) * kCtasSliceBwd <= 228 * 1024, "slice
 static_assert((kDbBytes + kSmemPad + 1024) * kCtasDesliceBwd <= 228 * 1024, "deslice bwd smem");
 static_assert((kCbBytes + kSmemPad + 1024) * kCtasCoupledBwd <= 228 * 1024, "coupled bwd smem");
 static_assert((kS6Bytes + kSmemPad + 1024) * 2 <= 228 * 1024, "slice fwd G=64 smem");
+static_assert((kD6Bytes + kSmemPad + 1024) * 2 <= 228 * 1024, "deslice fwd G=64 smem");
+static_assert(kD6Ts % 16 == 0 && kD6Ws % 16 == 0, "G=64 operand alignment");
 // TMEM per SM (512 columns) holds the co-resident CTAs' allocations
 static_assert(256 * kCtasSliceFwd <= 512 && kDfCols * kCtasDesliceFwd <= 512 &&
                   256 * kCtasSliceBwd <= 512 && 256 * kCtasDesliceBwd <= 512,

@@ -88,3 +88,45 @@ def test_slice_forward_strided_bf16_deterministic(env):
     for a, e in zip(tb, eb):
         assert relerr(a, e) <= 1e-5
     assert lib.fs_device_status(1) == 0
+
+
+def _deslice(K, st, engine, x, W, b, tau, tok, dt=torch.float32):
+    st.set_engine(engine)
+    try:
+        out = K.fused_deslice(x.to(dt), W.float(), b.float(), tau.float(), tok.float())
+        torch.cuda.synchronize()
+        return out
+    finally:
+        st.set_engine("auto")
+
+
+@pytest.mark.parametrize("N", [1, 77, 129, 4097, 100_003])
+@pytest.mark.parametrize("mode", ["gd", "hgd", "bhgd"])
+def test_deslice_forward_matches_exact_engine(env, N, mode):
+    K, st, lib = env
+    x, _, W, b, tau, tok = _inputs(N, mode, B=2 if mode == "bhgd" else 1)
+    n0 = lib.fs_tc_launch_count()
+    tc = _deslice(K, st, "auto", x, W, b, tau, tok)
+    assert lib.fs_tc_launch_count() - n0 == 1, "the tensor-core kernel did not run"
+    ex = _deslice(K, st, "fma", x, W, b, tau, tok)
+    from oracle import eager_torch as E
+    ref = E.deslice_fwd(x, W, b, tau, tok)
+    et, ee = relerr(tc, ref), relerr(ex, ref)
+    assert et <= max(2.0 * ee, 1e-6), (et, ee)
+    assert relerr(tc, ex) <= 1e-5, relerr(tc, ex)
+    assert lib.fs_device_status(1) == 0
+
+
+def test_deslice_forward_strided_bf16_deterministic(env):
+    K, st, lib = env
+    x, _, W, b, tau, tok = _inputs(50_000, "hgd", B=2, strided=True)
+    tc = _deslice(K, st, "auto", x, W, b, tau, tok)
+    ex = _deslice(K, st, "fma", x, W, b, tau, tok)
+    assert relerr(tc, ex) <= 1e-5
+    assert torch.equal(tc, _deslice(K, st, "auto", x, W, b, tau, tok))
+    n0 = lib.fs_tc_launch_count()
+    tb = _deslice(K, st, "auto", x, W, b, tau, tok, torch.bfloat16)
+    assert lib.fs_tc_launch_count() - n0 == 1 and tb.dtype == torch.bfloat16
+    eb = _deslice(K, st, "fma", x, W, b, tau, tok, torch.bfloat16)
+    assert relerr(tb.float(), eb.float()) <= 1e-2  # one bf16 rounding of the output apart
+    assert lib.fs_device_status(1) == 0
