@@ -843,8 +843,8 @@ int fs_deslice_bwd(const fs_problem* p, const fs_tensor4* x_mid, const float* we
 
 int fs_coupled_supported(const fs_problem* p) {
   if (check_problem(p) != FS_OK) return 0;
-  return setup(FS_OP_SLICE_BWD, *p).fused && tc_shape(*p) && !p->flags &&
-                 (!p->row_splits || p->B <= FS_MAX_SPLITS)
+  const bool tc32 = setup(FS_OP_SLICE_BWD, *p).fused && tc_shape(*p);
+  return (tc32 || tc64_shape(*p)) && !p->flags && (!p->row_splits || p->B <= FS_MAX_SPLITS)
              ? 1
              : 0;
 }
@@ -872,16 +872,22 @@ int fs_coupled_bwd(const fs_problem* p, const fs_tensor4* x_mid, const fs_tensor
   if (p->flags) return fail(FS_ERR_ARGUMENT, "the coupled backward takes no statistics");
   const Setup s = setup(FS_OP_SLICE_BWD, *p);
   FS_CHECK(check_ws(s, workspace, workspace_bytes));
-  if (!(s.fused && tc_shape(*p) && tc_tensor_ok(x_mid) && tc_tensor_ok(fx_mid) &&
+  const bool g64 = tc64_shape(*p);
+  if (!((g64 || (s.fused && tc_shape(*p))) && tc_tensor_ok(x_mid) && tc_tensor_ok(fx_mid) &&
         tc_tensor_ok(d_out) && tc_tensor_ok(dx_mid) && tc_tensor_ok(dfx_mid)))
     return fail(FS_ERR_UNSUPPORTED,
-                "the coupled backward serves fp32 single-tile problems with D = DV = G = 32 "
-                "(engine auto) and point tensors of unit width stride and 16-byte aligned "
-                "strides");
+                "the coupled backward serves single-tile problems with D = DV = 32 and G = 32 "
+                "or 64 (engine auto, fp32 or bf16 points) and point tensors of unit width "
+                "stride and 16-byte aligned strides");
+  const tcx::TcKind kind = g64 ? tcx::TcKind::CoupledBwd64 : tcx::TcKind::CoupledBwd;
   tcx::TcParams tq;
-  if (!tc_params(*p, tcx::TcKind::CoupledBwd, x_mid, fx_mid, weight, bias, tau, tq) ||
+  if (!tc_params(*p, kind, x_mid, fx_mid, weight, bias, tau, tq) ||
       !point_map(&tq.mo, *p, d_out))
     return fail(FS_ERR_UNSUPPORTED, "no TMA tensor map for the point tensors");
+  if (g64) {  // partials of the slot-blocked layout
+    if (tq.P > s.Pg) tq.P = s.Pg;
+    if (tq.P > s.Pn) tq.P = s.Pn;
+  }
   cudaStream_t st = (cudaStream_t)stream;
   tq.M = tokens;
   tq.M2 = dz_num;
@@ -896,8 +902,8 @@ int fs_coupled_bwd(const fs_problem* p, const fs_tensor4* x_mid, const fs_tensor
   tq.partA = at(workspace, s.partA);
   tq.partS = at(workspace, s.partS);
   tq.partDt = at(workspace, s.partDt);
-  route_note("coupled_bwd", "tensor-core", *p, x_mid, d_out);
-  FS_TRY(tcx::run_tc(tcx::TcKind::CoupledBwd, tq, st));
+  route_note("coupled_bwd", g64 ? "tensor-core-g64" : "tensor-core", *p, x_mid, d_out);
+  FS_TRY(tcx::run_tc(kind, tq, st));
   const int B = (int)p->B, H = (int)p->H, P = tq.P;
   FS_TRY(run_reduce(tq.partA, dW, B, H, P, p->G * p->D, p->w_batch, p->w_heads, st));
   FS_TRY(run_reduce(tq.partS, db, B, H, P, p->G, p->b_batch, p->b_heads, st));

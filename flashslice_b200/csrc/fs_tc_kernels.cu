@@ -2532,6 +2532,188 @@ __global__ void __launch_bounds__(256, 2) k_tc_deslice_fwd64(const __grid_consta
   epilogue<256>(c);
 }
 
+// ------------------------------------------------------------ coupled backward, G = 64
+// The tied backward of a round (as k_tc_coupled_bwd) at 64 slots: one CTA
+// of 256 threads per SM with all 512 TMEM columns; the phases of a tile run
+// in turn, the next tile's point tiles loading meanwhile.
+//  A: logits = x W^T (x split in shared memory, K-major view), dw = d_out
+//     tok^T + fx dz_num^T (point operands in TMEM), each N = 128;
+//  threads: softmax Jacobian -> w, dl/tau;
+//  B1: dfx = w dz_num and dx = (dl/tau) W (K = 64 slots, w and dl/tau in
+//      TMEM, dz_num and W as N-stacked MN-major operands), N = 96 each;
+//  B2: the transposed pool [x; 1]^T (dl/tau) -> dW and db (N = 192), formed
+//      while the threads store dfx and dx.
+// smem: [stage x][stage fx][stage d_out][XS: x split + ones][US: dl/tau,
+//       64 slots][W K-major][W stacked][tokens K-major][dz K-major]
+//       [dz stacked][bias][ds][red][bars]
+// TMEM (512 columns): A: logits 0, dw 128, fx 256, d_out 304; B1: dfx 0,
+// dx 96, dl/tau 256, w 352; B2: pool 192 (over the consumed B1 operands).
+constexpr int kC6StX = 0, kC6StF = kStage, kC6StO = 2 * kStage, kC6XS = 3 * kStage,
+              kC6US = kC6XS + kSplit4, kC6Wk = kC6US + kSplitW, kC6Wm = kC6Wk + kSmall64,
+              kC6Tk = kC6Wm + 8 * kRS, kC6Zk = kC6Tk + kSmall64, kC6Zm = kC6Zk + kSmall64,
+              kC6Bias = kC6Zm + 8 * kRS, kC6Ds = kC6Bias + 256, kC6Red = kC6Ds + 256,
+              kC6Bar = kC6Red + red_bytes(2, 3), kC6Bytes = kC6Bar + kBarBytes;
+static_assert(kC6XS % 1024 == 0, "stage tiles need 1 KB alignment");
+
+// logits64 with the point operand x in shared memory (the stacked buffer
+// with a ones part, read K-major: part p at +512 p)
+__device__ __forceinline__ void logits64_ss(uint32_t d, const uint8_t* xs, uint64_t bd) {
+  constexpr uint32_t id128 = idesc_bf16(128, 128, 0, 0), id64 = idesc_bf16(128, 64, 0, 0);
+  auto ad = [&](int part, int ks) { return smem_desc(smem_u32(xs + 512 * part + 256 * ks), 128, kRS4); };
+#pragma unroll
+  for (int pa = 0; pa < 2; ++pa)
+#pragma unroll
+    for (int ks = 0; ks < 2; ++ks)
+      mma_bf16(d, ad(pa, ks), bd + ((4096 + ks * 256) >> 4), id128, (pa | ks) != 0);
+#pragma unroll
+  for (int ks = 0; ks < 2; ++ks) mma_bf16(d, ad(2, ks), bd + ((ks * 256) >> 4), id64, true);
+#pragma unroll
+  for (int ks = 0; ks < 2; ++ks)
+    mma_bf16(d, ad(2, ks), bd + ((4096 + ks * 256) >> 4), id128, true);
+}
+
+// D = A1 B1^T + A2 B2^T into one 128-column accumulator [. B_mid | . B_hi]
+// (64-row small operands, point operands in TMEM, K = 32): the logits64
+// schedule of both products, their partial products interleaved.
+__device__ __forceinline__ void wide64_pair(uint32_t d, uint32_t a1, uint64_t b1, uint32_t a2,
+                                            uint64_t b2) {
+  constexpr uint32_t id128 = idesc_bf16(128, 128, 0, 0), id64 = idesc_bf16(128, 64, 0, 0);
+  const uint32_t a[2] = {a1, a2};
+  const uint64_t b[2] = {b1, b2};
+#pragma unroll
+  for (int pa = 0; pa < 2; ++pa)
+#pragma unroll
+    for (int s = 0; s < 2; ++s)
+#pragma unroll
+      for (int ks = 0; ks < 2; ++ks)
+        mma_ts(d, a[s] + pa * 16 + ks * 8, b[s] + ((4096 + ks * 256) >> 4), id128,
+               (pa | s | ks) != 0);
+#pragma unroll
+  for (int s = 0; s < 2; ++s)
+#pragma unroll
+    for (int ks = 0; ks < 2; ++ks) mma_ts(d, a[s] + 32 + ks * 8, b[s] + ((ks * 256) >> 4), id64, true);
+#pragma unroll
+  for (int s = 0; s < 2; ++s)
+#pragma unroll
+    for (int ks = 0; ks < 2; ++ks)
+      mma_ts(d, a[s] + 32 + ks * 8, b[s] + ((4096 + ks * 256) >> 4), id128, true);
+}
+
+template <typename PT>
+__global__ void __launch_bounds__(256, 1) k_tc_coupled_bwd64(const __grid_constant__ TcParams p) {
+  constexpr int T = 2, NT = 256;
+  extern __shared__ __align__(16) uint8_t sm_raw[];
+  uint8_t* sm = align_smem(sm_raw);
+  const Th<T> th;
+  const int bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
+  const Span sp = span_of(p, b);
+  Ctl c = prologue_begin<512>(sm, kC6Bar);
+  float* ds_s = (float*)(sm + kC6Ds);
+  float* red = (float*)(sm + kC6Red);
+  const float* Wp = p.W + (int64_t)b * p.swb + (int64_t)h * p.swh;
+  put_small64<NT>(sm + kC6Wk, Wp);
+  put_small_stacked64<NT>(sm + kC6Wm, Wp);
+  put_small64<NT>(sm + kC6Tk, p.M + (int64_t)bh * 64 * 32);
+  put_small64<NT>(sm + kC6Zk, p.M2 + (int64_t)bh * 64 * 32);
+  put_small_stacked64<NT>(sm + kC6Zm, p.M2 + (int64_t)bh * 64 * 32);
+  const RowConst rc = row_const64<NT>((float*)(sm + kC6Bias),
+                                      p.bias + (int64_t)b * p.sbb + (int64_t)h * p.sbh, p.tau[h]);
+  if (threadIdx.x < 64) ds_s[threadIdx.x] = p.ds[(int64_t)bh * 64 + threadIdx.x];
+  const float inv_tau = __frcp_rn(p.tau[h]);
+  prologue_end(c);
+  const uint32_t tL = c.tmem, tD = c.tmem + 128, tF = c.tmem + 256, tO = c.tmem + 304;
+  const uint32_t tDfx = c.tmem, tDx = c.tmem + 96, tU = c.tmem + 256, tW = c.tmem + 352,
+                 tP = c.tmem + 192;
+  const uint64_t dWk = desc_smallK(sm + kC6Wk), dWm = desc_stacked(sm + kC6Wm);
+  const uint64_t dTk = desc_smallK(sm + kC6Tk), dZk = desc_smallK(sm + kC6Zk),
+                 dZm = desc_stacked(sm + kC6Zm);
+  uint8_t* XS = sm + kC6XS;
+  uint8_t* US = sm + kC6US;
+  auto load3 = [&](int tile) {  // one thread: x, fx, d_out of a tile
+    mbar_arrive_expect_tx(c.bar + kBarTma, 3 * stage_bytes<PT>());
+    tma_load_4d(sm + kC6StX, &p.mx, 0, h, sp.row(tile), sp.bc, c.bar + kBarTma);
+    tma_load_4d(sm + kC6StF, &p.mv, 0, h, sp.row(tile), sp.bc, c.bar + kBarTma);
+    tma_load_4d(sm + kC6StO, &p.mo, 0, h, sp.row(tile), sp.bc, c.bar + kBarTma);
+  };
+  float acc[32], dt_acc = 0.f;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) acc[i] = 0.f;
+  int tile = blockIdx.x;
+  if (threadIdx.x == 0 && tile < sp.ntiles) load3(tile);
+  for (; tile < sp.ntiles; tile += p.P) {
+    const int n0 = tile * kTile;
+    const bool valid = n0 + th.row < sp.N;
+    wait_bar(c, kBarTma, p.status);
+    {
+      RowVals<16, PT> x, f, o;
+      x.load(sm + kC6StX, th.row, th.cs);
+      f.load(sm + kC6StF, th.row, th.cs);
+      o.load(sm + kC6StO, th.row, th.cs);
+      // (the last tile's pool is read out of TMEM, and its reads of XS and
+      // US are done, before anything here overwrites them)
+      split_to_smem4(x.split(), XS, th.row, th.cs);
+      f.split().to_tmem(tF + th.lane_off, th.cs);
+      o.split().to_tmem(tO + th.lane_off, th.cs);
+      tst_wait();
+    }
+    to_async_barrier();
+    if (threadIdx.x == 0) {
+      if (tile + p.P < sp.ntiles) load3(tile + p.P);  // the stages are consumed
+      logits64_ss(tL, XS, dWk);
+      commit(c, kG1);
+      wide64_pair(tD, tO, dTk, tF, dZk);  // d_out tok^T + fx dz_num^T
+      commit(c, kG2);
+    }
+    {
+      float w[32], dw[32];
+      wait_bar(c, kG1, p.status);
+      ld_logits64(tL + th.lane_off, th.cs, w);
+      wait_bar(c, kG2, p.status);
+      ld_logits64(tD + th.lane_off, th.cs, dw);
+      const float2* ds2 = (const float2*)(ds_s + 32 * th.cs);
+#pragma unroll
+      for (int k = 0; k < 16; ++k) put2(dw, k, __fadd2_rn(f2(dw, k), ds2[k]));
+      const float rdt = softmax_bwd<T, 32>(w, dw, rc, inv_tau, valid, red, th);
+      if (valid) dt_acc += rdt;
+      split_to_tmem64(Split<32>(w), tW + th.lane_off, th.cs);
+      const Split<32> us(dw);  // dl / tau
+      split_to_tmem64(us, tU + th.lane_off, th.cs);
+      split_to_smemw(us, US, th.row, th.cs);
+      tst_wait();
+    }
+    to_async_barrier();
+    if (threadIdx.x == 0) {
+      wide64_mn96(tDfx, tW, dZm);  // dfx = w dz_num
+      wide64_mn96(tDx, tU, dWm);   // dx = (dl/tau) W
+      commit(c, kG3);
+    }
+    wait_bar(c, kG3, p.status);
+    if (threadIdx.x == 0) {
+      mma_pool64(tP, XS, US);  // [x; 1]^T (dl/tau): dW and db, over the consumed operands
+      commit(c, kG4);
+    }
+    store_result<96, 16>(tDfx, th.q, th.cs,
+                         (PT*)p.out2 + (int64_t)sp.bc * p.so2[0] + (sp.n0 + n0) * p.so2[1] +
+                             (int64_t)h * p.so2[2],
+                         p.so2[1], sp.N - n0);
+    store_result<96, 16>(tDx, th.q, th.cs,
+                         (PT*)p.out + (int64_t)sp.bc * p.so[0] + (sp.n0 + n0) * p.so[1] +
+                             (int64_t)h * p.so[2],
+                         p.so[1], sp.N - n0);
+    wait_bar(c, kG4, p.status);
+    drain_pool64(tP + th.lane_off, th.cs, acc);
+    tc_fence_before();
+    __syncthreads();  // the pool is read out; XS and US are free
+    tc_fence_after();
+  }
+  const int64_t slot = (int64_t)bh * p.P + blockIdx.x;
+  tc_fence_before();
+  pool64_write((float*)US, acc, p.partA + slot * 64 * 32, p.partS + slot * 64, th);
+  const float tot = cta_sum_nt<NT>(dt_acc, (float*)XS);
+  if (threadIdx.x == 0) p.partDt[slot] = -inv_tau * kLn2 * tot;
+  epilogue<512>(c);
+}
+
 // ------------------------------------------------------------ wait self-test
 // One thread waits, with a limit of limit_ns, on an mbarrier that nothing
 // arrives at: the bounded-wait path of the kernels (status word set, the
@@ -2639,6 +2821,7 @@ static cudaError_t run_tc_t(TcKind k, const TcParams& p, cudaStream_t s) {
       return launch_tc(k_tc_coupled_bwd<PT>, kTCoupledBwd, kCbBytes, p, s);
     case TcKind::SliceFwd64: return launch_tc(k_tc_slice_fwd64<PT>, 2, kS6Bytes, p, s);
     case TcKind::DesliceFwd64: return launch_tc(k_tc_deslice_fwd64<PT>, 2, kD6Bytes, p, s);
+    case TcKind::CoupledBwd64: return launch_tc(k_tc_coupled_bwd64<PT>, 2, kC6Bytes, p, s);
     default: break;
   }
   return cudaErrorInvalidValue;
@@ -2747,6 +2930,7 @@ static_assert((kCbBytes + kSmemPad + 1024) * kCtasCoupledBwd <= 228 * 1024, "cou
 static_assert((kS6Bytes + kSmemPad + 1024) * 2 <= 228 * 1024, "slice fwd G=64 smem");
 static_assert((kD6Bytes + kSmemPad + 1024) * 2 <= 228 * 1024, "deslice fwd G=64 smem");
 static_assert(kD6Ts % 16 == 0 && kD6Ws % 16 == 0, "G=64 operand alignment");
+static_assert(kC6Bytes + kSmemPad + 1024 <= 228 * 1024, "coupled bwd G=64 smem");
 // TMEM per SM (512 columns) holds the co-resident CTAs' allocations
 static_assert(256 * kCtasSliceFwd <= 512 && kDfCols * kCtasDesliceFwd <= 512 &&
                   256 * kCtasSliceBwd <= 512 && 256 * kCtasDesliceBwd <= 512,

@@ -130,3 +130,82 @@ def test_deslice_forward_strided_bf16_deterministic(env):
     eb = _deslice(K, st, "fma", x, W, b, tau, tok, torch.bfloat16)
     assert relerr(tb.float(), eb.float()) <= 1e-2  # one bf16 rounding of the output apart
     assert lib.fs_device_status(1) == 0
+
+
+def _round(K, st, engine, x, fx, W, b, tau, r, tied=True, mix=None, params=(), dt=torch.float32):
+    """One round (fused_coupling, or the op-by-op composition) forward and
+    backward of sum(out * r)."""
+    st.set_engine(engine)
+    try:
+        L = [t.detach().to(dt if i < 2 else torch.float32).clone().requires_grad_(True)
+             for i, t in enumerate((x, fx, W, b, tau))]
+        if tied:
+            out = K.fused_coupling(*L, mix=mix, mix_params=list(params))
+        else:
+            z, s = K.fused_slice(*L)
+            tok = z / (s + 1e-5)[..., None]
+            out = K.fused_deslice(L[0], L[2], L[3], L[4], mix(tok) if mix else tok)
+        out.backward(r.to(out.dtype))
+        torch.cuda.synchronize()
+        res = {"out": out.detach().float()}
+        for k, v in zip(("x", "fx", "W", "b", "tau"), L):
+            res["grad:" + k] = v.grad.float()
+        for i, q in enumerate(params):
+            res["grad:p%d" % i] = q.grad.clone()
+            q.grad = None
+        return res
+    finally:
+        st.set_engine("auto")
+
+
+@pytest.mark.parametrize("N", [77, 4097, 100_003])
+@pytest.mark.parametrize("mode", ["gd", "hgd", "bhgd"])
+def test_round_matches_eager(env, N, mode):
+    """The tied round at G = 64 (slice, deslice, dtokens pass and coupled
+    backward, all four on the tensor cores) against the float64 eager round
+    and the exact FMA engine, every gradient."""
+    K, st, lib = env
+    x, fx, W, b, tau, _ = _inputs(N, mode, B=2 if mode == "bhgd" else 1)
+    r = torch.randn(x.shape, generator=torch.Generator().manual_seed(9),
+                    dtype=torch.float64).cuda()
+    n0 = lib.fs_tc_launch_count()
+    tc = _round(K, st, "auto", x, fx, W, b, tau, r)
+    assert lib.fs_tc_launch_count() - n0 == 4, "the tensor-core kernels did not run"
+    ex = _round(K, st, "fma", x, fx, W, b, tau, r, tied=False)
+    from oracle import eager_torch as E
+    ref = E.coupling_round(*[t.detach().clone().requires_grad_(True)
+                             for t in (x, fx, W, b, tau)], r)
+    for k in ("out", "grad:x", "grad:fx", "grad:W", "grad:b", "grad:tau"):
+        et, ee = relerr(tc[k], ref[k]), relerr(ex[k], ref[k])
+        assert relerr(tc[k], ex[k]) <= 1e-5 or et <= 1.25 * ee + 1e-6, (k, et, ee)
+    assert lib.fs_device_status(1) == 0
+
+
+def test_round_mix_strided_bf16_deterministic(env):
+    """A parameterised mix (the tied backward forms its gradient), strided
+    inputs, run-to-run bitwise identity, and bf16 point tensors within the
+    reference's 2e-2 gate of the float64 round on the same bf16 values."""
+    K, st, lib = env
+    x, fx, W, b, tau, _ = _inputs(30_000, "hgd", B=2, strided=True)
+    r = torch.randn(x.shape, generator=torch.Generator().manual_seed(4),
+                    dtype=torch.float64).cuda()
+    M = (torch.eye(32) + 0.1 * torch.randn(32, 32, generator=torch.Generator().manual_seed(1)))
+    M = M.cuda().requires_grad_(True)
+    mix = lambda t: t @ M  # noqa: E731
+    tc = _round(K, st, "auto", x, fx, W, b, tau, r, mix=mix, params=(M,))
+    ex = _round(K, st, "fma", x, fx, W, b, tau, r, tied=False, mix=mix, params=(M,))
+    for k in tc:
+        assert relerr(tc[k], ex[k]) <= 2e-5, (k, relerr(tc[k], ex[k]))
+    again = _round(K, st, "auto", x, fx, W, b, tau, r, mix=mix, params=(M,))
+    for k in tc:
+        assert torch.equal(tc[k], again[k]), k
+    n0 = lib.fs_tc_launch_count()
+    tb = _round(K, st, "auto", x, fx, W, b, tau, r, dt=torch.bfloat16)
+    assert lib.fs_tc_launch_count() - n0 == 4
+    from oracle import eager_torch as E
+    xb, fb = x.bfloat16().double(), fx.bfloat16().double()
+    ref = E.coupling_round(*[t.detach().clone().requires_grad_(True)
+                             for t in (xb, fb, W, b, tau)], r.bfloat16().double())
+    for k in ("out", "grad:x", "grad:fx", "grad:W", "grad:b", "grad:tau"):
+        assert relerr(tb[k], ref[k]) <= 2e-2, (k, relerr(tb[k], ref[k]))
+    assert lib.fs_device_status(1) == 0
