@@ -2238,13 +2238,14 @@ __device__ __forceinline__ void logits64(uint32_t d, uint32_t a, uint64_t bd) {
     mma_ts(d, a + 32 + ks * 8, bd + ((4096 + ks * 256) >> 4), id128, true);
 }
 
-// This thread's 32 logits (slots 32 cs ..) from the [W_mid | W_hi] groups.
-__device__ __forceinline__ void ld_logits64(uint32_t taddr, int cs, float (&v)[32]) {
+// This thread's CG logits (slots CG cs ..) from the [W_mid | W_hi] groups.
+template <int CG>
+__device__ __forceinline__ void ld_logits64(uint32_t taddr, int cs, float (&v)[CG]) {
 #pragma unroll
-  for (int hf = 0; hf < 2; ++hf) {
+  for (int hf = 0; hf < CG / 16; ++hf) {
     uint32_t a[16], b[16];
-    tld<16>(taddr + 32 * cs + 16 * hf, a);
-    tld<16>(taddr + 64 + 32 * cs + 16 * hf, b);
+    tld<16>(taddr + CG * cs + 16 * hf, a);
+    tld<16>(taddr + 64 + CG * cs + 16 * hf, b);
     tld_wait();
 #pragma unroll
     for (int k = 0; k < 8; ++k)
@@ -2254,15 +2255,16 @@ __device__ __forceinline__ void ld_logits64(uint32_t taddr, int cs, float (&v)[3
   }
 }
 
-// A point row's 16 values (columns 16 cs ..) split into a stacked buffer
+// A point row's C values (columns C cs ..) split into a stacked buffer
 // with a ones part: per 8-row group lo, mid, hi, ones at +0, +512, +1024,
 // +1536 (the M-stacked operand [lo; mid; hi; ones] of a transposed pool).
-__device__ __forceinline__ void split_to_smem4(const Split<16>& sp, uint8_t* buf, int row, int cs) {
+template <int C>
+__device__ __forceinline__ void split_to_smem4(const Split<C>& sp, uint8_t* buf, int row, int cs) {
   uint8_t* base = buf + (row >> 3) * kRS4 + (row & 7) * 16;
   const uint4 ones = make_uint4(0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u);
 #pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    const int j = 2 * cs + i;
+  for (int i = 0; i < C / 8; ++i) {
+    const int j = (C / 8) * cs + i;
     *(uint4*)(base + j * 128) = make_uint4(sp.lw[4 * i], sp.lw[4 * i + 1], sp.lw[4 * i + 2], sp.lw[4 * i + 3]);
     *(uint4*)(base + 512 + j * 128) = make_uint4(sp.mw[4 * i], sp.mw[4 * i + 1], sp.mw[4 * i + 2], sp.mw[4 * i + 3]);
     *(uint4*)(base + 1024 + j * 128) = make_uint4(sp.hw[4 * i], sp.hw[4 * i + 1], sp.hw[4 * i + 2], sp.hw[4 * i + 3]);
@@ -2270,14 +2272,15 @@ __device__ __forceinline__ void split_to_smem4(const Split<16>& sp, uint8_t* buf
   }
 }
 
-// A row's 32 slot values (slots 32 cs ..) split into the N-stacked 64-slot
+// A row's CG slot values (slots CG cs ..) split into the N-stacked 64-slot
 // buffer: per 8-row group the lo, mid, hi parts of the 64 slots (128 bytes
 // each, 8 core matrices) at +0, +1024, +2048.
-__device__ __forceinline__ void split_to_smemw(const Split<32>& sp, uint8_t* buf, int row, int cs) {
+template <int CG>
+__device__ __forceinline__ void split_to_smemw(const Split<CG>& sp, uint8_t* buf, int row, int cs) {
   uint8_t* base = buf + (row >> 3) * kRSW + (row & 7) * 16;
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int j = 4 * cs + i;
+  for (int i = 0; i < CG / 8; ++i) {
+    const int j = (CG / 8) * cs + i;
     *(uint4*)(base + j * 128) = make_uint4(sp.lw[4 * i], sp.lw[4 * i + 1], sp.lw[4 * i + 2], sp.lw[4 * i + 3]);
     *(uint4*)(base + 1024 + j * 128) = make_uint4(sp.mw[4 * i], sp.mw[4 * i + 1], sp.mw[4 * i + 2], sp.mw[4 * i + 3]);
     *(uint4*)(base + 2048 + j * 128) = make_uint4(sp.hw[4 * i], sp.hw[4 * i + 1], sp.hw[4 * i + 2], sp.hw[4 * i + 3]);
@@ -2294,15 +2297,16 @@ __device__ __forceinline__ void mma_pool64(uint32_t d, const uint8_t* a, const u
     mma_bf16(d, ad + ((ks * 2 * kRS4) >> 4), bd + ((ks * 2 * kRSW) >> 4), kIdPool64, ks > 0);
 }
 
-// Add this thread's 32 columns of its pool row (slots 32 cs .. of the slot
+// Add this thread's CG columns of its pool row (slots CG cs .. of the slot
 // parts lo, mid, hi, small first) into acc.
-__device__ __forceinline__ void drain_pool64(uint32_t taddr, int cs, float (&acc)[32]) {
+template <int CG>
+__device__ __forceinline__ void drain_pool64(uint32_t taddr, int cs, float (&acc)[CG]) {
 #pragma unroll
-  for (int hf = 0; hf < 2; ++hf) {
+  for (int hf = 0; hf < CG / 16; ++hf) {
     uint32_t a[16], b[16], c[16];
-    tld<16>(taddr + 32 * cs + 16 * hf, a);
-    tld<16>(taddr + 64 + 32 * cs + 16 * hf, b);
-    tld<16>(taddr + 128 + 32 * cs + 16 * hf, c);
+    tld<16>(taddr + CG * cs + 16 * hf, a);
+    tld<16>(taddr + 64 + CG * cs + 16 * hf, b);
+    tld<16>(taddr + 128 + CG * cs + 16 * hf, c);
     tld_wait();
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
@@ -2317,22 +2321,24 @@ __device__ __forceinline__ void drain_pool64(uint32_t taddr, int cs, float (&acc
 
 // Transposed pool partials: thread (q, cs) with TMEM lane 32 q + t holds,
 // for point-operand part q (q = 3: the ones row) and value t, its sums over
-// slots 32 cs + i. Writes part[g][c] = (lo + mid) + hi for the 64 x 32
+// slots CG cs + i. Writes part[g][c] = (lo + mid) + hi for the 64 x 32
 // partial, and the plain sums (ones row) into sums[g] when sums is given;
 // xch holds 3 x 32 x 65 floats.
-__device__ __forceinline__ void pool64_write(float* xch, const float (&acc)[32], float* part,
-                                             float* sums, const Th<2>& th) {
+template <int T>
+__device__ __forceinline__ void pool64_write(float* xch, const float (&acc)[64 / T], float* part,
+                                             float* sums, const Th<T>& th) {
+  constexpr int CG = 64 / T;
   const int t = threadIdx.x & 31;
   __syncthreads();
   if (th.q < 3) {
 #pragma unroll
-    for (int i = 0; i < 32; ++i) xch[(th.q * 32 + t) * 65 + 32 * th.cs + i] = acc[i];
+    for (int i = 0; i < CG; ++i) xch[(th.q * 32 + t) * 65 + CG * th.cs + i] = acc[i];
   } else if (sums && t == 0) {
 #pragma unroll
-    for (int i = 0; i < 32; ++i) sums[32 * th.cs + i] = acc[i];
+    for (int i = 0; i < CG; ++i) sums[CG * th.cs + i] = acc[i];
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < 64 * 32; i += 256) {
+  for (int i = threadIdx.x; i < 64 * 32; i += Th<T>::NT) {
     const int g = i >> 5, c = i & 31;
     part[i] = (xch[c * 65 + g] + xch[(32 + c) * 65 + g]) + xch[(64 + c) * 65 + g];
   }
@@ -2437,14 +2443,15 @@ __device__ __forceinline__ void put_small_stacked64(uint8_t* dst, const float* M
   }
 }
 
-// A row's 32 slot values (slots 32 cs ..) as this thread's part of a K = 64
+// A row's CG slot values (slots CG cs ..) as this thread's part of a K = 64
 // point operand in TMEM: parts lo, mid, hi at +0, +32, +64 columns, two bf16
-// per column (even slot low), the thread's 16 columns at 16 cs.
-__device__ __forceinline__ void split_to_tmem64(const Split<32>& sp, uint32_t taddr, int cs) {
-  const uint32_t a = taddr + 16 * cs;
-  tst<16>(a, sp.lw);
-  tst<16>(a + 32, sp.mw);
-  tst<16>(a + 64, sp.hw);
+// per column (even slot low), the thread's CG / 2 columns at (CG / 2) cs.
+template <int CG>
+__device__ __forceinline__ void split_to_tmem64(const Split<CG>& sp, uint32_t taddr, int cs) {
+  const uint32_t a = taddr + (CG / 2) * cs;
+  tst<CG / 2>(a, sp.lw);
+  tst<CG / 2>(a + 32, sp.mw);
+  tst<CG / 2>(a + 64, sp.hw);
 }
 
 // D (128 x 96) = A B^T with A = a K = 64 point operand in TMEM (parts at
@@ -2551,8 +2558,13 @@ __global__ void __launch_bounds__(256, 2) k_tc_deslice_fwd64(const __grid_consta
 constexpr int kC6StX = 0, kC6StF = kStage, kC6StO = 2 * kStage, kC6XS = 3 * kStage,
               kC6US = kC6XS + kSplit4, kC6Wk = kC6US + kSplitW, kC6Wm = kC6Wk + kSmall64,
               kC6Tk = kC6Wm + 8 * kRS, kC6Zk = kC6Tk + kSmall64, kC6Zm = kC6Zk + kSmall64,
-              kC6Bias = kC6Zm + 8 * kRS, kC6Ds = kC6Bias + 256, kC6Red = kC6Ds + 256,
-              kC6Bar = kC6Red + red_bytes(2, 3), kC6Bytes = kC6Bar + kBarBytes;
+              kC6Bias = kC6Zm + 8 * kRS, kC6Ds = kC6Bias + 256, kC6Red = kC6Ds + 256;
+#ifndef FS_TC_CB64_T
+#define FS_TC_CB64_T 2
+#endif
+constexpr int kTCoupled64 = FS_TC_CB64_T;  // threads per point row
+__host__ __device__ constexpr int c6_bar(int T) { return kC6Red + red_bytes(T, 3); }
+__host__ __device__ constexpr int c6_bytes(int T) { return c6_bar(T) + kBarBytes; }
 static_assert(kC6XS % 1024 == 0, "stage tiles need 1 KB alignment");
 
 // logits64 with the point operand x in shared memory (the stacked buffer
@@ -2599,15 +2611,15 @@ __device__ __forceinline__ void wide64_pair(uint32_t d, uint32_t a1, uint64_t b1
       mma_ts(d, a[s] + 32 + ks * 8, b[s] + ((4096 + ks * 256) >> 4), id128, true);
 }
 
-template <typename PT>
-__global__ void __launch_bounds__(256, 1) k_tc_coupled_bwd64(const __grid_constant__ TcParams p) {
-  constexpr int T = 2, NT = 256;
+template <typename PT, int T>
+__global__ void __launch_bounds__(128 * T, 1) k_tc_coupled_bwd64(const __grid_constant__ TcParams p) {
+  constexpr int NT = 128 * T, C = 32 / T, CG = 64 / T;
   extern __shared__ __align__(16) uint8_t sm_raw[];
   uint8_t* sm = align_smem(sm_raw);
   const Th<T> th;
   const int bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
   const Span sp = span_of(p, b);
-  Ctl c = prologue_begin<512>(sm, kC6Bar);
+  Ctl c = prologue_begin<512>(sm, c6_bar(T));
   float* ds_s = (float*)(sm + kC6Ds);
   float* red = (float*)(sm + kC6Red);
   const float* Wp = p.W + (int64_t)b * p.swb + (int64_t)h * p.swh;
@@ -2635,9 +2647,9 @@ __global__ void __launch_bounds__(256, 1) k_tc_coupled_bwd64(const __grid_consta
     tma_load_4d(sm + kC6StF, &p.mv, 0, h, sp.row(tile), sp.bc, c.bar + kBarTma);
     tma_load_4d(sm + kC6StO, &p.mo, 0, h, sp.row(tile), sp.bc, c.bar + kBarTma);
   };
-  float acc[32], dt_acc = 0.f;
+  float acc[CG], dt_acc = 0.f;
 #pragma unroll
-  for (int i = 0; i < 32; ++i) acc[i] = 0.f;
+  for (int i = 0; i < CG; ++i) acc[i] = 0.f;
   int tile = blockIdx.x;
   if (threadIdx.x == 0 && tile < sp.ntiles) load3(tile);
   for (; tile < sp.ntiles; tile += p.P) {
@@ -2645,7 +2657,7 @@ __global__ void __launch_bounds__(256, 1) k_tc_coupled_bwd64(const __grid_consta
     const bool valid = n0 + th.row < sp.N;
     wait_bar(c, kBarTma, p.status);
     {
-      RowVals<16, PT> x, f, o;
+      RowVals<C, PT> x, f, o;
       x.load(sm + kC6StX, th.row, th.cs);
       f.load(sm + kC6StF, th.row, th.cs);
       o.load(sm + kC6StO, th.row, th.cs);
@@ -2665,18 +2677,18 @@ __global__ void __launch_bounds__(256, 1) k_tc_coupled_bwd64(const __grid_consta
       commit(c, kG2);
     }
     {
-      float w[32], dw[32];
+      float w[CG], dw[CG];
       wait_bar(c, kG1, p.status);
       ld_logits64(tL + th.lane_off, th.cs, w);
       wait_bar(c, kG2, p.status);
       ld_logits64(tD + th.lane_off, th.cs, dw);
-      const float2* ds2 = (const float2*)(ds_s + 32 * th.cs);
+      const float2* ds2 = (const float2*)(ds_s + CG * th.cs);
 #pragma unroll
-      for (int k = 0; k < 16; ++k) put2(dw, k, __fadd2_rn(f2(dw, k), ds2[k]));
-      const float rdt = softmax_bwd<T, 32>(w, dw, rc, inv_tau, valid, red, th);
+      for (int k = 0; k < CG / 2; ++k) put2(dw, k, __fadd2_rn(f2(dw, k), ds2[k]));
+      const float rdt = softmax_bwd<T, CG>(w, dw, rc, inv_tau, valid, red, th);
       if (valid) dt_acc += rdt;
-      split_to_tmem64(Split<32>(w), tW + th.lane_off, th.cs);
-      const Split<32> us(dw);  // dl / tau
+      split_to_tmem64(Split<CG>(w), tW + th.lane_off, th.cs);
+      const Split<CG> us(dw);  // dl / tau
       split_to_tmem64(us, tU + th.lane_off, th.cs);
       split_to_smemw(us, US, th.row, th.cs);
       tst_wait();
@@ -2692,14 +2704,14 @@ __global__ void __launch_bounds__(256, 1) k_tc_coupled_bwd64(const __grid_consta
       mma_pool64(tP, XS, US);  // [x; 1]^T (dl/tau): dW and db, over the consumed operands
       commit(c, kG4);
     }
-    store_result<96, 16>(tDfx, th.q, th.cs,
-                         (PT*)p.out2 + (int64_t)sp.bc * p.so2[0] + (sp.n0 + n0) * p.so2[1] +
-                             (int64_t)h * p.so2[2],
-                         p.so2[1], sp.N - n0);
-    store_result<96, 16>(tDx, th.q, th.cs,
-                         (PT*)p.out + (int64_t)sp.bc * p.so[0] + (sp.n0 + n0) * p.so[1] +
-                             (int64_t)h * p.so[2],
-                         p.so[1], sp.N - n0);
+    store_result<96, C>(tDfx, th.q, th.cs,
+                        (PT*)p.out2 + (int64_t)sp.bc * p.so2[0] + (sp.n0 + n0) * p.so2[1] +
+                            (int64_t)h * p.so2[2],
+                        p.so2[1], sp.N - n0);
+    store_result<96, C>(tDx, th.q, th.cs,
+                        (PT*)p.out + (int64_t)sp.bc * p.so[0] + (sp.n0 + n0) * p.so[1] +
+                            (int64_t)h * p.so[2],
+                        p.so[1], sp.N - n0);
     wait_bar(c, kG4, p.status);
     drain_pool64(tP + th.lane_off, th.cs, acc);
     tc_fence_before();
@@ -2821,7 +2833,9 @@ static cudaError_t run_tc_t(TcKind k, const TcParams& p, cudaStream_t s) {
       return launch_tc(k_tc_coupled_bwd<PT>, kTCoupledBwd, kCbBytes, p, s);
     case TcKind::SliceFwd64: return launch_tc(k_tc_slice_fwd64<PT>, 2, kS6Bytes, p, s);
     case TcKind::DesliceFwd64: return launch_tc(k_tc_deslice_fwd64<PT>, 2, kD6Bytes, p, s);
-    case TcKind::CoupledBwd64: return launch_tc(k_tc_coupled_bwd64<PT>, 2, kC6Bytes, p, s);
+    case TcKind::CoupledBwd64:
+      return launch_tc(k_tc_coupled_bwd64<PT, kTCoupled64>, kTCoupled64, c6_bytes(kTCoupled64),
+                       p, s);
     default: break;
   }
   return cudaErrorInvalidValue;
@@ -2930,7 +2944,7 @@ static_assert((kCbBytes + kSmemPad + 1024) * kCtasCoupledBwd <= 228 * 1024, "cou
 static_assert((kS6Bytes + kSmemPad + 1024) * 2 <= 228 * 1024, "slice fwd G=64 smem");
 static_assert((kD6Bytes + kSmemPad + 1024) * 2 <= 228 * 1024, "deslice fwd G=64 smem");
 static_assert(kD6Ts % 16 == 0 && kD6Ws % 16 == 0, "G=64 operand alignment");
-static_assert(kC6Bytes + kSmemPad + 1024 <= 228 * 1024, "coupled bwd G=64 smem");
+static_assert(c6_bytes(kTCoupled64) + kSmemPad + 1024 <= 228 * 1024, "coupled bwd G=64 smem");
 // TMEM per SM (512 columns) holds the co-resident CTAs' allocations
 static_assert(256 * kCtasSliceFwd <= 512 && kDfCols * kCtasDesliceFwd <= 512 &&
                   256 * kCtasSliceBwd <= 512 && 256 * kCtasDesliceBwd <= 512,
