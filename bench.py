@@ -72,7 +72,10 @@ def parse():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--impl", choices=("ours", "reference", "reference-triton"), default="ours",
+                    help="reference: the reference's CPU path (the driver's arm); "
+                         "reference-triton: the unmodified reference's own Triton GPU kernels "
+                         "from baseline/_ref on this GPU, the GPU bar")
     ap.add_argument("--config", choices=sorted(CONFIGS) + ["cfg4"], default="cfg2")
     ap.add_argument("--n", type=int, default=None, help="override the point count")
     ap.add_argument("--no-e2e", action="store_true")
@@ -433,6 +436,70 @@ def cpu_sample(args, cfg):
     return min(cfg["N"], 1 << 20)
 
 
+def run_reference_triton(args, cfg):
+    """The same round through the unmodified reference (``baseline/_ref``,
+    installed from the reference's source tree) on one GPU: its public
+    ``fused_slice`` / ``fused_deslice`` and autograd, its Triton kernels at
+    its own default settings (ieee dot mode, the tile table it picks for
+    this GPU). Device-resident inputs, CUDA-event timing, the same metric,
+    config and seeds as our arm."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    why = None
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        why = "the reference has no multi-GPU path; this leg runs on one GPU"
+    elif not os.path.isdir(os.path.join(ref, "flashslice")):
+        why = "baseline/_ref is not installed (pip install --target baseline/_ref <reference>)"
+    elif not torch.cuda.is_available():
+        why = "no CUDA device"
+    if why:
+        print(json.dumps({"impl": "reference-triton", "unavailable": why}), flush=True)
+        return
+    sys.path.insert(0, ref)
+    import flashslice.kernels as R  # the reference's own package
+    device = torch.device("cuda", 0)
+    torch.backends.cuda.matmul.allow_tf32 = False
+    n = cfg["N"]
+    x, fx, W, b, tau, r = make_inputs(cfg, n, device, 1234)
+    _, _, W, b, tau, _ = make_inputs(cfg, 1, device, 99)
+    for t in (x, fx, W, b, tau):
+        if t is not None:
+            t.requires_grad_(True)
+
+    def step():
+        zero_grads(x, fx, W, b, tau)
+        z, s = R.fused_slice(x, fx, W, b, tau)
+        out = R.fused_deslice(x, W, b, tau, z / (s + EPS)[..., None])
+        out.backward(r)
+
+    ms = timed_rounds(step, args.steps, max(args.warmup, 1))
+    points = cfg["B"] * n
+    value = points / (ms * 1e-3) / 1e6
+    unit_bytes = points * cfg["H"] * cfg["D"] * x.element_size()
+    peak = None
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peak = json.load(f).get("hbm_gbs")
+    except (OSError, ValueError):
+        pass
+    line = {"metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32" if cfg["dtype"] == torch.float32 else "bf16",
+            "data": "synthetic (seeded torch.Generator on the device)",
+            "impl": "reference-triton",
+            "config": {"workload": args.config, "B": cfg["B"], "N": n, "H": cfg["H"],
+                       "D": cfg["D"], "DV": cfg["DV"], "G": cfg["G"], "weight": cfg["weight"],
+                       "dot": "the reference's default (ieee)",
+                       "path": "flashslice.kernels.fused_slice + fused_deslice + autograd "
+                               "(its Triton kernels), unmodified, from baseline/_ref"},
+            "round_frac": (round(11 * unit_bytes / (ms * 1e-3) / 1e9 / peak, 4)
+                           if peak and cfg["G"] <= 64 else None)}
+    print(json.dumps(line), flush=True)
+
+
 def run_reference(args, cfg):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -555,6 +622,8 @@ def main():
         cfg["N"] = args.n
     if args.impl == "reference":
         return run_reference(args, cfg)
+    if args.impl == "reference-triton":
+        return run_reference_triton(args, cfg)
     if not torch.cuda.is_available():
         raise SystemExit("bench.py: no CUDA device (the fused ops have no CPU implementation)")
 

@@ -152,6 +152,7 @@ bool blk_tc_params(const fs_problem& p, const fs_tensor4* x, const fs_tensor4* v
       (v && !tcx::make_point_map(&q.mv, v->data, p.B, p.N, p.H, v->stride, 2, (int)p.DV)))
     return false;
   q.status = tcx::device_status();
+  q.wait_ns = tcx::g_wait_limit_ns.load(std::memory_order_relaxed);
   if (!q.status) return false;
   q.B = (int)p.B;
   q.N = (int)p.N;
@@ -208,6 +209,7 @@ bool tc_params(const fs_problem& p, tcx::TcKind k, const fs_tensor4* x, const fs
     return false;
   }
   q.status = tcx::device_status();
+  q.wait_ns = tcx::g_wait_limit_ns.load(std::memory_order_relaxed);
   if (!q.status) {
     if (debug_routes()) fprintf(stderr, "[flashslice_b200] no device status word\n");
     return false;
@@ -485,6 +487,14 @@ const char* fs_last_error(void) { return g_err.c_str(); }
 uint64_t fs_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
 uint64_t fs_tc_launch_count(void) { return tcx::g_tc_launches.load(std::memory_order_relaxed); }
+
+int fs_set_wait_limit_ns(uint64_t limit_ns) {
+  if (limit_ns > 2000000000ull)
+    return fail(FS_ERR_ARGUMENT, "wait limit %llu ns is above the default 2e9",
+                (unsigned long long)limit_ns);
+  tcx::g_wait_limit_ns.store(limit_ns, std::memory_order_relaxed);
+  return FS_OK;
+}
 
 int fs_device_status(int reset) {
   int* word = tcx::device_status();

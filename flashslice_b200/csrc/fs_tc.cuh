@@ -62,15 +62,38 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   return t;
 }
 
+// Non-blocking probe: has the phase with the given parity completed?
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait for the phase with the given parity to complete; false (and *status
-// set) if it does not within limit_ns (kWaitNs in the kernels).
+// set) if it does not within limit_ns (kWaitNs in the kernels). A try_wait
+// may itself suspend the thread for longer than a short limit, so limits
+// below the default are kept by polling with the non-blocking test_wait.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status,
                                           uint64_t limit_ns = kWaitNs) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
-  for (uint32_t i = 0; i < (1u << 30); ++i) {
+  if (limit_ns >= kWaitNs) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (globaltimer_ns() - t0 > limit_ns) break;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t i = 0; i < (1u << 30); ++i) {
+      if (mbar_try_wait(bar, parity)) return true;
+      if (globaltimer_ns() - t0 > limit_ns) break;
+    }
+  } else {
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t i = 0; i < (1u << 30); ++i) {
+      if (mbar_test_wait(bar, parity)) return true;
+      if (globaltimer_ns() - t0 > limit_ns) break;
+    }
   }
   if (status) atomicExch(status, kErrTimeout);
   return false;

@@ -589,17 +589,37 @@ __device__ __forceinline__ void to_async_barrier() {
 
 // Kernel control block: the TMA barrier and up to five MMA-completion
 // barriers (one per group of MMAs committed together), each completing once
-// per tile, with their phases.
+// per tile, with their phases; the wait limit, and whether a wait of this
+// thread has given up.
+//
+// After a wait gives up (status word set), every later wait of that thread
+// returns at once, so a kernel whose arrivals are lost finishes after one
+// limit per thread instead of one per wait; the issuing thread (thread 0)
+// then issues no further TMA or MMA work -- it re-arms a barrier only after
+// a completed wait on it, so each barrier has at most one phase it armed and
+// did not see complete -- and before the TMEM is freed it waits, with a
+// short bound, for the phase each barrier still expects, so that the copies
+// and MMAs it issued are done before the CTA exits. Control flow is the same
+// for every thread either way: the CTA-wide barriers all meet.
 constexpr int kNumBars = 6;
+constexpr uint64_t kDrainNs = 50000000ull;  // 50 ms per barrier, failure path only
 struct Ctl {
   uint64_t* bar;  // [0] TMA, [1..5] MMA groups
   uint32_t tmem;
   uint32_t ph[kNumBars];
+  uint32_t fail;   // a wait of this thread gave up
+  uint64_t limit;  // ns a wait may take
+  // the thread that issues TMA loads and MMAs, while none of its waits failed
+  __device__ __forceinline__ bool issuer() const { return threadIdx.x == 0 && !fail; }
 };
 
 __device__ __forceinline__ void wait_bar(Ctl& c, int k, int* status) {
-  mbar_wait(c.bar + k, c.ph[k], status);
-  c.ph[k] ^= 1;
+  if (!c.fail) {
+    if (mbar_wait(c.bar + k, c.ph[k], status, c.limit))
+      c.ph[k] ^= 1;
+    else
+      c.fail = 1;
+  }
   tc_fence_after();
 }
 __device__ __forceinline__ void commit(Ctl& c, int k) { mma_commit(c.bar + k); }
@@ -800,8 +820,10 @@ __device__ __forceinline__ float cta_sum_nt(float v, float* red) {
 constexpr int kBarBytes = 128;  // kNumBars mbarriers and the TMEM address slot
 
 template <int NCOLS>
-__device__ __forceinline__ Ctl prologue_begin(uint8_t* sm, int bar_off) {
+__device__ __forceinline__ Ctl prologue_begin(uint8_t* sm, int bar_off, uint64_t limit_ns) {
   Ctl c;
+  c.fail = 0;
+  c.limit = limit_ns ? limit_ns : kWaitNs;
   c.bar = (uint64_t*)(sm + bar_off);
   uint32_t* tslot = (uint32_t*)(c.bar + kNumBars);
   if ((threadIdx.x >> 5) == 0) {
@@ -829,6 +851,11 @@ __device__ __forceinline__ void prologue_end(Ctl& c) {
 
 template <int NCOLS>
 __device__ __forceinline__ void epilogue(Ctl& c) {
+  if (c.issuer() && c.fail) {
+    // failure path: let the copies and MMAs this thread issued land first
+#pragma unroll
+    for (int k = 0; k < kNumBars; ++k) mbar_wait(c.bar + k, c.ph[k], nullptr, kDrainNs);
+  }
   tc_fence_before();
   __syncthreads();
   if ((threadIdx.x >> 5) == 0) tmem_dealloc(c.tmem, NCOLS);
@@ -931,7 +958,7 @@ __global__ void __launch_bounds__(128 * kTSliceFwd, kCtasSliceFwd)
   const Th<T> th;
   const int bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
   const Span sp = span_of(p, b);
-  Ctl c = prologue_begin<256>(sm, kSfBar);
+  Ctl c = prologue_begin<256>(sm, kSfBar, p.wait_ns);
   float* red = (float*)(sm + kSfRed);
   put_small<NT>(sm + kSfWs, p.W + (int64_t)b * p.swb + (int64_t)h * p.swh);
   const RowConst rc = row_const<NT>((float*)(sm + kSfBias),
@@ -959,10 +986,10 @@ __global__ void __launch_bounds__(128 * kTSliceFwd, kCtasSliceFwd)
   // (a CTA of a sample with fewer tiles than CTAs has none: it writes zero
   // partials; the condition is the same for every thread)
   if (tile < sp.ntiles) {
-    if (threadIdx.x == 0) tma_tile<PT>(p, stX, fbuf(0), h, sp, tile, c.bar);
+    if (c.issuer()) tma_tile<PT>(p, stX, fbuf(0), h, sp, tile, c.bar);
     split_tile(0);
     to_async_barrier();
-    if (threadIdx.x == 0) {
+    if (c.issuer()) {
       prefetch<PT>(p, stX, fbuf(1), h, sp, tile, c.bar);  // F[1] is unused yet
       wide_ts<96, false>(tL, tX, dWs);  // logits = x W^T
       commit(c, kG1);
@@ -982,14 +1009,14 @@ __global__ void __launch_bounds__(128 * kTSliceFwd, kCtasSliceFwd)
       for (int k = 0; k < C / 2; ++k) put2(accs, k, __fadd2_rn(f2(accs, k), f2(lg, k)));
     }
     to_async_barrier();
-    if (threadIdx.x == 0) {
+    if (c.issuer()) {
       mma_pool(tP, dWp, desc_stacked(fbuf(buf)));  // z += w^T fx
       commit(c, kG2);
     }
     if (more) {
       split_tile(buf ^ 1);
       to_async_barrier();
-      if (threadIdx.x == 0) {
+      if (c.issuer()) {
         if (more2) {  // tile i+2: its x now, its fx once tile i's pool is done with F[buf]
           mbar_arrive_expect_tx(c.bar + kBarTma, 2 * stage_bytes<PT>());
           tma_load_4d(stX, &p.mx, 0, h, sp.row(tile + 2 * p.P), sp.bc, c.bar + kBarTma);
@@ -999,7 +1026,7 @@ __global__ void __launch_bounds__(128 * kTSliceFwd, kCtasSliceFwd)
       }
     }
     wait_bar(c, kG2, p.status);
-    if (threadIdx.x == 0 && more2)
+    if (c.issuer() && more2)
       tma_load_4d(fbuf(buf), &p.mv, 0, h, sp.row(tile + 2 * p.P), sp.bc, c.bar + kBarTma);
     if (th.q < 3) drain_pool<C>(tP + th.lane_off, th.cs, accz);
   }
@@ -1029,7 +1056,7 @@ __global__ void __launch_bounds__(128 * kTDesliceFwd, kCtasDesliceFwd)
   const Th<T> th;
   const int bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
   const Span sp = span_of(p, b);
-  Ctl c = prologue_begin<kDfCols>(sm, kDfBar);
+  Ctl c = prologue_begin<kDfCols>(sm, kDfBar, p.wait_ns);
   float* red = (float*)(sm + kDfRed);
   put_small<NT>(sm + kDfWs, p.W + (int64_t)b * p.swb + (int64_t)h * p.swh);
   if constexpr (kNwDf == 32)
@@ -1043,7 +1070,7 @@ __global__ void __launch_bounds__(128 * kTDesliceFwd, kCtasDesliceFwd)
   const uint64_t dWs = desc_smallK(sm + kDfWs);
   const uint64_t dTs = kNwDf == 32 ? desc_smallM(sm + kDfTs) : desc_stacked(sm + kDfTs);
   int tile = blockIdx.x;
-  if (threadIdx.x == 0 && tile < sp.ntiles) tma_tile<PT>(p, sm + kDfStageX, nullptr, h, sp, tile, c.bar);
+  if (c.issuer() && tile < sp.ntiles) tma_tile<PT>(p, sm + kDfStageX, nullptr, h, sp, tile, c.bar);
   for (; tile < sp.ntiles; tile += p.P) {
     const int n0 = tile * kTile;
     wait_bar(c, kBarTma, p.status);
@@ -1054,7 +1081,7 @@ __global__ void __launch_bounds__(128 * kTDesliceFwd, kCtasDesliceFwd)
       tst_wait();
     }
     to_async_barrier();
-    if (threadIdx.x == 0) {
+    if (c.issuer()) {
       prefetch<PT>(p, sm + kDfStageX, nullptr, h, sp, tile, c.bar);
       wide_ts<kNwDf, false>(tL, tA, dWs);  // logits = x W^T
       commit(c, kG1);
@@ -1068,7 +1095,7 @@ __global__ void __launch_bounds__(128 * kTDesliceFwd, kCtasDesliceFwd)
       tst_wait();
     }
     to_async_barrier();
-    if (threadIdx.x == 0) {
+    if (c.issuer()) {
       wide_ts<kNwDf, true>(tL, tA, dTs);  // out = w tokens, over the consumed logits
       commit(c, kG2);
     }
@@ -1103,7 +1130,7 @@ __global__ void __launch_bounds__(128 * kTSliceBwd, kCtasSliceBwd)
   const Th<T> th;
   const int bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
   const Span sp = span_of(p, b);
-  Ctl c = prologue_begin<256>(sm, kSbBar);
+  Ctl c = prologue_begin<256>(sm, kSbBar, p.wait_ns);
   float* ds_s = (float*)(sm + kSbDs);
   float* red = (float*)(sm + kSbRed);
   put_small<NT>(sm + kSbWs, p.W + (int64_t)b * p.swb + (int64_t)h * p.swh);
@@ -1123,7 +1150,7 @@ __global__ void __launch_bounds__(128 * kTSliceBwd, kCtasSliceBwd)
 #pragma unroll
   for (int i = 0; i < C; ++i) accw[i] = accb[i] = 0.f;
   int tile = blockIdx.x;
-  if (threadIdx.x == 0 && tile < sp.ntiles)
+  if (c.issuer() && tile < sp.ntiles)
     tma_tile<PT>(p, sm + kSbStageX, sm + kSbStageF, h, sp, tile, c.bar);
   for (; tile < sp.ntiles; tile += p.P) {
     const int n0 = tile * kTile;
@@ -1140,7 +1167,7 @@ __global__ void __launch_bounds__(128 * kTSliceBwd, kCtasSliceBwd)
       tst_wait();
     }
     to_async_barrier();
-    if (threadIdx.x == 0) {
+    if (c.issuer()) {
       prefetch<PT>(p, sm + kSbStageX, sm + kSbStageF, h, sp, tile, c.bar);
       wide_ts<96, false>(tL, tX, dWk);  // logits = x W^T
       commit(c, kG1);
@@ -1167,7 +1194,7 @@ __global__ void __launch_bounds__(128 * kTSliceBwd, kCtasSliceBwd)
       tst_wait();
     }
     to_async_barrier();
-    if (threadIdx.x == 0) {
+    if (c.issuer()) {
       wide_ts<32, true>(tDfx, tW, dZm);  // dfx = w dz_num
       wide_ts<32, true>(tDx, tU, dWm);   // dx = (dl/tau) W
       commit(c, kG3);
@@ -1220,7 +1247,7 @@ __global__ void __launch_bounds__(128 * kTDesliceBwd, kCtasDesliceBwd)
   const Th<T> th;
   const int bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
   const Span sp = span_of(p, b);
-  Ctl c = prologue_begin<256>(sm, kDbBar);
+  Ctl c = prologue_begin<256>(sm, kDbBar, p.wait_ns);
   float* red = (float*)(sm + kDbRed);
   put_small<NT>(sm + kDbWs, p.W + (int64_t)b * p.swb + (int64_t)h * p.swh);
   put_small<NT>(sm + kDbTs, p.M + (int64_t)bh * 32 * 32);
@@ -1240,7 +1267,7 @@ __global__ void __launch_bounds__(128 * kTDesliceBwd, kCtasDesliceBwd)
 #pragma unroll
   for (int i = 0; i < C; ++i) acct[i] = accw[i] = accb[i] = 0.f;
   int tile = blockIdx.x;
-  if (threadIdx.x == 0 && tile < sp.ntiles) tma_tile<PT>(p, stX, stO, h, sp, tile, c.bar);
+  if (c.issuer() && tile < sp.ntiles) tma_tile<PT>(p, stX, stO, h, sp, tile, c.bar);
   for (; tile < sp.ntiles; tile += p.P) {
     const int n0 = tile * kTile;
     const bool valid = n0 + th.row < sp.N;
@@ -1259,7 +1286,7 @@ __global__ void __launch_bounds__(128 * kTDesliceBwd, kCtasDesliceBwd)
       tst_wait();
     }
     to_async_barrier();
-    if (threadIdx.x == 0) {
+    if (c.issuer()) {
       wide_ts<96, false>(tL, tX, dWk);  // logits = x W^T
       commit(c, kG1);
       wide_ts<64, false>(tDw, tO, dTk);  // dw = d_out tok^T
@@ -1282,7 +1309,7 @@ __global__ void __launch_bounds__(128 * kTDesliceBwd, kCtasDesliceBwd)
       tst_wait();
     }
     to_async_barrier();
-    if (threadIdx.x == 0) {
+    if (c.issuer()) {
       wide_ts<32, true>(tDx, tX, dWm);  // dx = (dl/tau) W
       commit(c, kG3);
       mma_pool(tP, dWp, dOb);  // dtokens += w^T d_out
@@ -1298,7 +1325,7 @@ __global__ void __launch_bounds__(128 * kTDesliceBwd, kCtasDesliceBwd)
     tc_fence_before();
     __syncthreads();  // the pool region is read out; WP is free
     tc_fence_after();
-    if (threadIdx.x == 0) {
+    if (c.issuer()) {
       if (more) {
         mbar_arrive_expect_tx(c.bar + kBarTma, 2 * stage_bytes<PT>());
         tma_load_4d(stX, &p.mx, 0, h, sp.row(tile + p.P), sp.bc, c.bar + kBarTma);
@@ -1307,7 +1334,7 @@ __global__ void __launch_bounds__(128 * kTDesliceBwd, kCtasDesliceBwd)
       commit(c, kG5);
     }
     wait_bar(c, kG5, p.status);
-    if (threadIdx.x == 0 && more)  // UP is free once the dW pool is done
+    if (c.issuer() && more)  // UP is free once the dW pool is done
       tma_load_4d(stO, &p.mv, 0, h, sp.row(tile + p.P), sp.bc, c.bar + kBarTma);
     if (th.q < 3) drain_pool<C>(tP + th.lane_off, th.cs, accw);
   }
@@ -1362,7 +1389,7 @@ __global__ void __launch_bounds__(128 * kTCoupledBwd, kCtasCoupledBwd)
   const Th<T> th;
   const int bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
   const Span sp = span_of(p, b);
-  Ctl c = prologue_begin<256>(sm, kCbBar);
+  Ctl c = prologue_begin<256>(sm, kCbBar, p.wait_ns);
   float* ds_s = (float*)(sm + kCbDs);
   float* red = (float*)(sm + kCbRed);
   put_small<NT>(sm + kCbWs, p.W + (int64_t)b * p.swb + (int64_t)h * p.swh);
@@ -1388,7 +1415,7 @@ __global__ void __launch_bounds__(128 * kTCoupledBwd, kCtasCoupledBwd)
 #pragma unroll
   for (int i = 0; i < C; ++i) accw[i] = accb[i] = 0.f;
   int tile = blockIdx.x;
-  if (threadIdx.x == 0 && tile < sp.ntiles) {
+  if (c.issuer() && tile < sp.ntiles) {
     mbar_arrive_expect_tx(c.bar + kBarTma, 3 * stage_bytes<PT>());
     tma_load_4d(stX, &p.mx, 0, h, sp.row(tile), sp.bc, c.bar + kBarTma);
     tma_load_4d(stF, &p.mv, 0, h, sp.row(tile), sp.bc, c.bar + kBarTma);
@@ -1410,7 +1437,7 @@ __global__ void __launch_bounds__(128 * kTCoupledBwd, kCtasCoupledBwd)
       tst_wait();
     }
     to_async_barrier();
-    if (threadIdx.x == 0) {
+    if (c.issuer()) {
       if (more) {  // x and fx of the next tile; its d_out once UP is free
         mbar_arrive_expect_tx(c.bar + kBarTma, 3 * stage_bytes<PT>());
         tma_load_4d(stX, &p.mx, 0, h, sp.row(tile + p.P), sp.bc, c.bar + kBarTma);
@@ -1441,7 +1468,7 @@ __global__ void __launch_bounds__(128 * kTCoupledBwd, kCtasCoupledBwd)
       tst_wait();
     }
     to_async_barrier();
-    if (threadIdx.x == 0) {
+    if (c.issuer()) {
       mma_pool(tP, dUp, dXb);  // dW += (dl/tau)^T x
       commit(c, kG3);
       wide_ts<32, true>(tDfx, tW, dZm);  // dfx = w dz_num
@@ -1449,7 +1476,7 @@ __global__ void __launch_bounds__(128 * kTCoupledBwd, kCtasCoupledBwd)
       commit(c, kG4);
     }
     wait_bar(c, kG3, p.status);
-    if (threadIdx.x == 0 && more)  // UP is free once the dW pool is done
+    if (c.issuer() && more)  // UP is free once the dW pool is done
       tma_load_4d(stO, &p.mo, 0, h, sp.row(tile + p.P), sp.bc, c.bar + kBarTma);
     if (th.q < 3) drain_pool<C>(tP + th.lane_off, th.cs, accw);
     wait_bar(c, kG4, p.status);
@@ -1501,7 +1528,7 @@ __global__ void __launch_bounds__(256, 2) k_tc_blk_slice_fwd_bf16(const __grid_c
   const int gb = blockIdx.y, bh = blockIdx.z, b = bh / p.H, h = bh - b * p.H;
   const int g0 = gb * kBgSlots, DV = p.dv;
   const Span sp = span_of(p, b);
-  Ctl c = prologue_begin<256>(sm, kBgBar);
+  Ctl c = prologue_begin<256>(sm, kBgBar, p.wait_ns);
   // W rows g0 .. g0 + 127, two bf16 parts (mid, hi), K-major (rows g, k = d)
   {
     const float* Wb = p.W + (int64_t)b * p.swb + (int64_t)h * p.swh + (int64_t)g0 * 32;
@@ -1541,11 +1568,11 @@ __global__ void __launch_bounds__(256, 2) k_tc_blk_slice_fwd_bf16(const __grid_c
   const uint32_t id_l = idesc_bf16(128, 128, 0, 0), id_z = idesc_bf16(128, DV == 64 ? 64 : 32, 1, 1),
                  id_s = idesc_bf16(128, 16, 1, 1);
   const int n_my = sp.ntiles > (int)blockIdx.x ? (sp.ntiles - 1 - (int)blockIdx.x) / p.P + 1 : 0;
-  if (threadIdx.x == 0 && n_my > 0) load(0, blockIdx.x);
+  if (c.issuer() && n_my > 0) load(0, blockIdx.x);
   for (int k = 0; k < n_my; ++k) {
     const int tile = blockIdx.x + k * p.P, n0 = tile * kTile;
     wait_bar(c, kBarTma, p.status);
-    if (threadIdx.x == 0) {  // logits: x times W mid, hi (small first)
+    if (c.issuer()) {  // logits: x times W mid, hi (small first)
       for (int part = 0; part < 2; ++part)
         for (int ks = 0; ks < 2; ++ks)
           mma_bf16(tL, smem_desc(smem_u32(xs(k)) + ks * 4096, 2048, 128),
@@ -1554,7 +1581,7 @@ __global__ void __launch_bounds__(256, 2) k_tc_blk_slice_fwd_bf16(const __grid_c
       commit(c, kG1);
     }
     if (k > 0) wait_bar(c, kG2, p.status);  // tile k - 1's pool: its buffers and the w tile free
-    if (threadIdx.x == 0 && k + 1 < n_my) load(k + 1, tile + p.P);
+    if (c.issuer() && k + 1 < n_my) load(k + 1, tile + p.P);
     wait_bar(c, kG1, p.status);
     {
       const int n = n0 + row;
@@ -1590,7 +1617,7 @@ __global__ void __launch_bounds__(256, 2) k_tc_blk_slice_fwd_bf16(const __grid_c
       }
     }
     to_async_barrier();
-    if (threadIdx.x == 0) {  // z_num += w^T fx, s += w^T 1, 16 points a step
+    if (c.issuer()) {  // z_num += w^T fx, s += w^T 1, 16 points a step
       for (int ks = 0; ks < 8; ++ks) {
         const uint64_t ad = smem_desc(smem_u32(sm + kBgW) + ks * 2 * (kBgSlots * 16), kBgSlots * 16, 128);
         mma_bf16(tZ, ad, smem_desc(smem_u32(fs(k)) + ks * 256, 128, 2048), id_z, (k | ks) != 0);
@@ -1654,7 +1681,7 @@ __global__ void __launch_bounds__(512, 1) k_tc_blk_bwd_g_bf16(const __grid_const
   const int gb = blockIdx.y, bh = blockIdx.z, b = bh / p.H, h = bh - b * p.H;
   const int g0 = gb * kBgSlots, DV = p.dv;
   const Span sp = span_of(p, b);
-  Ctl c = prologue_begin<512>(sm, kBbBar);
+  Ctl c = prologue_begin<512>(sm, kBbBar, p.wait_ns);
   const float inv_tau = __frcp_rn(p.tau[h]);
   {
     // W rows g0 .. g0 + 127 (K = d, 32) and M rows (K = dv) in two bf16 parts
@@ -1709,11 +1736,11 @@ __global__ void __launch_bounds__(512, 1) k_tc_blk_bwd_g_bf16(const __grid_const
   const uint32_t id_w = idesc_bf16(128, 32, 1, 1), id_s = idesc_bf16(128, 16, 1, 1),
                  id_t = idesc_bf16(128, DV == 64 ? 64 : 32, 1, 1);
   const int n_my = sp.ntiles > (int)blockIdx.x ? (sp.ntiles - 1 - (int)blockIdx.x) / p.P + 1 : 0;
-  if (threadIdx.x == 0 && n_my > 0) load(0, blockIdx.x);
+  if (c.issuer() && n_my > 0) load(0, blockIdx.x);
   for (int k = 0; k < n_my; ++k) {
     const int tile = blockIdx.x + k * p.P, n0 = tile * kTile;
     wait_bar(c, kBarTma, p.status);
-    if (threadIdx.x == 0) {
+    if (c.issuer()) {
       for (int part = 0; part < 2; ++part)  // logits = x W^T (mid, hi of W)
         for (int ks = 0; ks < 2; ++ks)
           mma_bf16(tL, smem_desc(smem_u32(xs(k)) + ks * 4096, 2048, 128),
@@ -1727,7 +1754,7 @@ __global__ void __launch_bounds__(512, 1) k_tc_blk_bwd_g_bf16(const __grid_const
       commit(c, kG1);
     }
     if (k > 0) wait_bar(c, kG2, p.status);  // tile k - 1's pools: buffers and tiles free
-    if (threadIdx.x == 0 && k + 1 < n_my) load(k + 1, tile + p.P);
+    if (c.issuer() && k + 1 < n_my) load(k + 1, tile + p.P);
     wait_bar(c, kG1, p.status);
     {
       const int n = n0 + row;
@@ -1775,7 +1802,7 @@ __global__ void __launch_bounds__(512, 1) k_tc_blk_bwd_g_bf16(const __grid_const
       }
     }
     to_async_barrier();
-    if (threadIdx.x == 0) {  // dW += dl^T x, db += dl^T 1, dtokens += w^T d_out
+    if (c.issuer()) {  // dW += dl^T x, db += dl^T 1, dtokens += w^T d_out
       for (int ks = 0; ks < 8; ++ks) {
         const uint64_t ad = smem_desc(smem_u32(sm + kBbDl) + ks * 4096, 2048, 128);
         mma_bf16(tW, ad, smem_desc(smem_u32(xs(k)) + ks * 256, 128, 2048), id_w, (k | ks) != 0);
@@ -1907,7 +1934,7 @@ __global__ void __launch_bounds__(256, 2) k_tc_blk_pown_bf16(const __grid_consta
   const int bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H, DV = p.dv, N = p.N;
   const int nblk = p.G / kPnSlots, mp = im_mpart(DV);
   const Span sp = span_of(p, b);
-  Ctl c = prologue_begin<256>(sm, kPnBar);
+  Ctl c = prologue_begin<256>(sm, kPnBar, p.wait_ns);
   prologue_end(c);
   const float inv_tau = __frcp_rn(p.tau[h]);
   const float scale = inv_tau * kLog2e;
@@ -1941,7 +1968,7 @@ __global__ void __launch_bounds__(256, 2) k_tc_blk_pown_bf16(const __grid_consta
   const uint32_t id_a = idesc_bf16(128, DV == 64 ? 64 : 32, 0, 1), id_x = idesc_bf16(128, 32, 0, 1);
   const int n_my = sp.ntiles > (int)blockIdx.x ? (sp.ntiles - 1 - (int)blockIdx.x) / p.P + 1 : 0;
   const int nq = n_my * NPASS * nblk;
-  if (threadIdx.x == 0 && nq > 0) {
+  if (c.issuer() && nq > 0) {
     load_tile(blockIdx.x);
     load_image(0, 0);
   }
@@ -1973,7 +2000,7 @@ __global__ void __launch_bounds__(256, 2) k_tc_blk_pown_bf16(const __grid_consta
           wait_bar(c, kG4, p.status);
         else
           wait_bar(c, kG3, p.status);
-        if (threadIdx.x == 0) {
+        if (c.issuer()) {
           // logits = x W^T and dw = v M^T, the small parts first
           for (int part = 0; part < 2; ++part)  // W mid, hi
             for (int ks = 0; ks < 2; ++ks)
@@ -1992,13 +2019,13 @@ __global__ void __launch_bounds__(256, 2) k_tc_blk_pown_bf16(const __grid_consta
           wait_bar(c, kG2, p.status);
           v_pending = false;
         }
-        if (threadIdx.x == 0 && q + 1 < nq) load_image(q + 1, j + 1 < nblk ? j + 1 : 0);
+        if (c.issuer() && q + 1 < nq) load_image(q + 1, j + 1 < nblk ? j + 1 : 0);
         wait_bar(c, kG1, p.status);
         // The tile's last products have read x and v: fetch the next tile's.
         // Every thread must have waited for this tile's phase of the TMA
         // barrier first (else a lagging thread would see it two phases on):
         // the barrier of the tile's first block-pass guarantees it (nblk >= 2).
-        if (threadIdx.x == 0 && j == nblk - 1 && pass == NPASS - 1 && k + 1 < n_my)
+        if (c.issuer() && j == nblk - 1 && pass == NPASS - 1 && k + 1 < n_my)
           load_tile(tile + p.P);
         const float* bias2 = (const float*)(im + kImBias);
         const float* dss = (const float*)(im + kImDs);
@@ -2072,7 +2099,7 @@ __global__ void __launch_bounds__(256, 2) k_tc_blk_pown_bf16(const __grid_consta
         }
         to_async_barrier();
         if (value_mma) {
-          if (threadIdx.x == 0) {
+          if (c.issuer()) {
             if (BWD && pass == 1) {  // dx += dl W (W hi, MN-major)
               for (int ks = 0; ks < 4; ++ks)
                 mma_bf16(tA, smem_desc(smem_u32(et) + ks * 256, 128, 1024),
@@ -2364,7 +2391,7 @@ __global__ void __launch_bounds__(256, 2) k_tc_slice_fwd64(const __grid_constant
   const Th<T> th;
   const int bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
   const Span sp = span_of(p, b);
-  Ctl c = prologue_begin<256>(sm, kS6Bar);
+  Ctl c = prologue_begin<256>(sm, kS6Bar, p.wait_ns);
   float* red = (float*)(sm + kS6Red);
   put_small64<NT>(sm + kS6Ws, p.W + (int64_t)b * p.swb + (int64_t)h * p.swh);
   const RowConst rc = row_const64<NT>((float*)(sm + kS6Bias),
@@ -2379,7 +2406,7 @@ __global__ void __launch_bounds__(256, 2) k_tc_slice_fwd64(const __grid_constant
 #pragma unroll
   for (int i = 0; i < 32; ++i) acc[i] = 0.f;
   int tile = blockIdx.x;
-  if (threadIdx.x == 0 && tile < sp.ntiles) tma_tile<PT>(p, stX, F, h, sp, tile, c.bar);
+  if (c.issuer() && tile < sp.ntiles) tma_tile<PT>(p, stX, F, h, sp, tile, c.bar);
   for (; tile < sp.ntiles; tile += p.P) {
     const int n0 = tile * kTile;
     const bool more = tile + p.P < sp.ntiles;
@@ -2396,7 +2423,7 @@ __global__ void __launch_bounds__(256, 2) k_tc_slice_fwd64(const __grid_constant
     split_to_smem4(f.split(), F, th.row, th.cs);
     tst_wait();
     to_async_barrier();
-    if (threadIdx.x == 0) {
+    if (c.issuer()) {
       if (more) {  // the next tile's x now, its fx once the pool is done with F
         mbar_arrive_expect_tx(c.bar + kBarTma, 2 * stage_bytes<PT>());
         tma_load_4d(stX, &p.mx, 0, h, sp.row(tile + p.P), sp.bc, c.bar + kBarTma);
@@ -2412,12 +2439,12 @@ __global__ void __launch_bounds__(256, 2) k_tc_slice_fwd64(const __grid_constant
       split_to_smemw(Split<32>(lg), WS, th.row, th.cs);
     }
     to_async_barrier();
-    if (threadIdx.x == 0) {
+    if (c.issuer()) {
       mma_pool64(tP, F, WS);  // [fx; 1]^T w
       commit(c, kG2);
     }
     wait_bar(c, kG2, p.status);
-    if (threadIdx.x == 0 && more)
+    if (c.issuer() && more)
       tma_load_4d(F, &p.mv, 0, h, sp.row(tile + p.P), sp.bc, c.bar + kBarTma);
     drain_pool64(tP + th.lane_off, th.cs, acc);
   }
@@ -2482,7 +2509,7 @@ __global__ void __launch_bounds__(256, 2) k_tc_deslice_fwd64(const __grid_consta
   const Th<T> th;
   const int bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
   const Span sp = span_of(p, b);
-  Ctl c = prologue_begin<256>(sm, kD6Bar);
+  Ctl c = prologue_begin<256>(sm, kD6Bar, p.wait_ns);
   float* red = (float*)(sm + kD6Red);
   put_small64<NT>(sm + kD6Ws, p.W + (int64_t)b * p.swb + (int64_t)h * p.swh);
   put_small_stacked64<NT>(sm + kD6Ts, p.M + (int64_t)bh * 64 * 32);
@@ -2495,7 +2522,7 @@ __global__ void __launch_bounds__(256, 2) k_tc_deslice_fwd64(const __grid_consta
   // stage k & 1 completes on barrier kBarTma (even) or kG3 (odd)
   auto sbar = [&](int k) { return (k & 1) ? kG3 : kBarTma; };
   const int n_my = sp.ntiles > (int)blockIdx.x ? (sp.ntiles - 1 - (int)blockIdx.x) / p.P + 1 : 0;
-  if (threadIdx.x == 0) {
+  if (c.issuer()) {
     for (int k = 0; k < 2 && k < n_my; ++k)
       tma_tile<PT>(p, stage(k), nullptr, h, sp, blockIdx.x + k * p.P, c.bar + sbar(k));
   }
@@ -2511,7 +2538,7 @@ __global__ void __launch_bounds__(256, 2) k_tc_deslice_fwd64(const __grid_consta
     x.split().to_tmem(tX + th.lane_off, th.cs);
     tst_wait();
     to_async_barrier();
-    if (threadIdx.x == 0) {
+    if (c.issuer()) {
       if (k + 2 < n_my)  // stage k & 1 is consumed: the tile after next
         tma_tile<PT>(p, stage(k), nullptr, h, sp, tile + 2 * p.P, c.bar + sbar(k));
       logits64(tL, tX, dWs);
@@ -2526,7 +2553,7 @@ __global__ void __launch_bounds__(256, 2) k_tc_deslice_fwd64(const __grid_consta
       tst_wait();
     }
     to_async_barrier();
-    if (threadIdx.x == 0) {
+    if (c.issuer()) {
       wide64_mn96(tO, tA, dTs);  // out = w tokens, over the consumed logits
       commit(c, kG2);
     }
@@ -2619,7 +2646,7 @@ __global__ void __launch_bounds__(128 * T, 1) k_tc_coupled_bwd64(const __grid_co
   const Th<T> th;
   const int bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
   const Span sp = span_of(p, b);
-  Ctl c = prologue_begin<512>(sm, c6_bar(T));
+  Ctl c = prologue_begin<512>(sm, c6_bar(T), p.wait_ns);
   float* ds_s = (float*)(sm + kC6Ds);
   float* red = (float*)(sm + kC6Red);
   const float* Wp = p.W + (int64_t)b * p.swb + (int64_t)h * p.swh;
@@ -2651,7 +2678,7 @@ __global__ void __launch_bounds__(128 * T, 1) k_tc_coupled_bwd64(const __grid_co
 #pragma unroll
   for (int i = 0; i < CG; ++i) acc[i] = 0.f;
   int tile = blockIdx.x;
-  if (threadIdx.x == 0 && tile < sp.ntiles) load3(tile);
+  if (c.issuer() && tile < sp.ntiles) load3(tile);
   for (; tile < sp.ntiles; tile += p.P) {
     const int n0 = tile * kTile;
     const bool valid = n0 + th.row < sp.N;
@@ -2669,7 +2696,7 @@ __global__ void __launch_bounds__(128 * T, 1) k_tc_coupled_bwd64(const __grid_co
       tst_wait();
     }
     to_async_barrier();
-    if (threadIdx.x == 0) {
+    if (c.issuer()) {
       if (tile + p.P < sp.ntiles) load3(tile + p.P);  // the stages are consumed
       logits64_ss(tL, XS, dWk);
       commit(c, kG1);
@@ -2694,13 +2721,13 @@ __global__ void __launch_bounds__(128 * T, 1) k_tc_coupled_bwd64(const __grid_co
       tst_wait();
     }
     to_async_barrier();
-    if (threadIdx.x == 0) {
+    if (c.issuer()) {
       wide64_mn96(tDfx, tW, dZm);  // dfx = w dz_num
       wide64_mn96(tDx, tU, dWm);   // dx = (dl/tau) W
       commit(c, kG3);
     }
     wait_bar(c, kG3, p.status);
-    if (threadIdx.x == 0) {
+    if (c.issuer()) {
       mma_pool64(tP, XS, US);  // [x; 1]^T (dl/tau): dW and db, over the consumed operands
       commit(c, kG4);
     }
@@ -2811,6 +2838,7 @@ static cudaError_t set_smem(const void* k, int bytes) {
 }
 
 std::atomic<uint64_t> g_tc_launches{0};
+std::atomic<uint64_t> g_wait_limit_ns{0};
 
 template <typename K>
 static cudaError_t launch_tc(K kernel, int T, int bytes, const TcParams& p, cudaStream_t s) {

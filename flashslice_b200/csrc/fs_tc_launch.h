@@ -60,6 +60,7 @@ struct TcParams {
   float* partDt;
   uint8_t* img;     // blocked point-owning kernels: operand images, one per (b, h, slot block)
   int* status;      // device word: set to a non-zero code when a bounded wait gives up
+  uint64_t wait_ns;  // how long one device-side wait may take (0: the kernels' default)
   // ragged samples: nsplit = B > 0 and split[0 .. B] the row offsets of the
   // samples in the point tensors' single batch entry; 0 = dense
   int nsplit;
@@ -88,6 +89,10 @@ bool make_point_map(CUtensorMap* map, const void* data, int64_t B, int64_t N, in
 
 // Address of this library's device status word on the current device.
 int* device_status();
+
+// The wait limit the next launches get (TcParams::wait_ns): 0 for the
+// kernels' default; a short one lets a test make real kernels' waits run out.
+extern std::atomic<uint64_t> g_wait_limit_ns;
 
 }  // namespace tcx
 }  // namespace fs

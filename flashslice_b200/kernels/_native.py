@@ -66,6 +66,7 @@ SIGNATURES = {
     "fs_coupled_supported": (ctypes.c_int, [_PP]),
     "fs_rank_sum": (ctypes.c_int, [_P, _P, ctypes.c_int, ctypes.c_int64, _P]),
     "fs_selftest_wait_timeout": (ctypes.c_int, [ctypes.c_uint64, _P]),
+    "fs_set_wait_limit_ns": (ctypes.c_int, [ctypes.c_uint64]),
 }
 
 ENGINE_AUTO, ENGINE_FMA = 0, 1

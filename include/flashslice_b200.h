@@ -109,9 +109,11 @@ typedef struct fs_problem {
 #define FS_MAX_SPLITS 128
 
 /* Engine selection. FS_ENGINE_AUTO runs the tensor-core kernels where they
- * serve the problem (single-tile family, fp32, D = DV = G = 32, TMA-friendly
- * strides) and the exact-fp32 FMA kernels elsewhere; FS_ENGINE_FMA forces the
- * FMA kernels (every product an fp32 FMA). Both meet the ieee contract. */
+ * serve the problem (single-tile family with fp32 or bf16 points, D = DV = 32
+ * and G = 32 or 64, TMA-friendly strides; the blocked family for bf16 points
+ * in the bf16 dot mode with D = 32, DV = 32 or 64, G a multiple of 128) and
+ * the exact-fp32 FMA kernels elsewhere; FS_ENGINE_FMA forces the FMA kernels
+ * (every product an fp32 FMA). Both meet the ieee contract. */
 #define FS_ENGINE_AUTO 0
 #define FS_ENGINE_FMA 1
 
@@ -152,6 +154,15 @@ FS_API int fs_device_status(int reset);
  * does; the kernel then returns and the context stays usable. No reference
  * counterpart. */
 FS_API int fs_selftest_wait_timeout(uint64_t limit_ns, void* stream);
+
+/* How long one device-side wait of the tensor-core kernels launched from now
+ * on may take, in ns (at most 2e9); 0 restores the default 2e9. A short
+ * limit makes real kernels' waits run out on a healthy GPU: the status word
+ * is set, every later wait of a thread whose wait gave up returns at once,
+ * the issuing thread stops issuing and lets what it issued land, and the
+ * kernel returns (its outputs not valid). For tests of that path; a
+ * diagnostic of this library, no reference counterpart. */
+FS_API int fs_set_wait_limit_ns(uint64_t limit_ns);
 
 /* Bytes of workspace `op` needs for problem `p` (0 when it needs none). */
 FS_API size_t fs_workspace_bytes(int op, const fs_problem* p);
@@ -245,8 +256,9 @@ FS_API int fs_coupled_bwd(const fs_problem* p, const fs_tensor4* x_mid,
                           float* db, float* dtau, void* workspace, size_t workspace_bytes,
                           void* stream);
 
-/* 1 when fs_coupled_bwd serves problem p: single-tile family, fp32 points,
- * D = DV = G = 32, engine auto, no statistics flags; 0 otherwise. */
+/* 1 when fs_coupled_bwd serves problem p: single-tile family, fp32 or bf16
+ * points, D = DV = 32, G = 32 or 64, engine auto, no statistics flags; 0
+ * otherwise. */
 FS_API int fs_coupled_supported(const fs_problem* p);
 
 /* Per-point softmax statistics (B,H,2,N) of the slice logits, in

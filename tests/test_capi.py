@@ -167,3 +167,9 @@ def test_noalloc_refuses_row_splits_without_gpu():
     rc = lib.fs_slice_fwd_noalloc(ctypes.byref(p), ctypes.byref(t), ctypes.byref(t), one, one,
                                   one, one, one, None)
     assert rc == nat.FS_ERR_UNSUPPORTED
+
+
+def test_wait_limit_argument_checked_without_gpu():
+    lib = nat.load()
+    assert lib.fs_set_wait_limit_ns(3_000_000_000) == nat.FS_ERR_ARGUMENT
+    assert lib.fs_set_wait_limit_ns(0) == nat.FS_OK

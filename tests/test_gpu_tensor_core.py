@@ -162,3 +162,62 @@ def test_bounded_wait_reports_and_context_survives(env):
     for a, e in zip(tc, ex):
         assert relerr(a, e) <= 1e-5
     assert lib.fs_device_status(1) == 0
+
+
+def _tied(K, leaves, r):
+    """fused_coupling forward and backward of sum(out * r)."""
+    L = [t.detach().float().requires_grad_(True) for t in leaves]
+    out = K.fused_coupling(*L, eps=1e-5)
+    out.backward(r.float())
+    torch.cuda.synchronize()
+    res = {"out": out.detach()}
+    for k, v in zip(("x", "fx", "W", "b", "tau"), L):
+        res["grad:" + k] = v.grad
+    return res
+
+
+def test_real_kernels_waits_run_out_and_context_survives(env):
+    """The failure path of the real tensor-core kernels, made on a healthy
+    GPU: their device-side waits get a 100 ns limit (the TMA loads and MMAs
+    take longer), so they give up. The status word is set, every later wait
+    of a thread that gave up returns at once, the issuing thread stops issuing
+    and lets what it issued land, and the kernels return within a bound; with
+    the default limit back, the same context computes correctly. Covers the
+    tied rounds at G = 32 and G = 64 (slice, deslice, dtokens pass, coupled
+    backward)."""
+    import time
+    K, st, lib = env
+    from flashslice_b200.kernels import _native as nat
+    from oracle import eager_torch as E
+    assert lib.fs_device_status(1) == 0
+    x, fx, W, b, tau, tok = _inputs(200_000, "hgd", H=8)
+    W64 = torch.cat([W, W.flip(1)], dim=1)
+    b64 = torch.cat([b, -b], dim=1)
+    r = torch.randn(x.shape, generator=torch.Generator().manual_seed(2),
+                    dtype=torch.float64).cuda()
+    torch.cuda.synchronize()
+    nat.check(lib.fs_set_wait_limit_ns(100))
+    try:
+        t0 = time.monotonic()
+        n0 = lib.fs_tc_launch_count()
+        _tied(K, (x, fx, W, b, tau), r)
+        _tied(K, (x, fx, W64, b64, tau), r)
+        waited = time.monotonic() - t0
+        assert lib.fs_tc_launch_count() - n0 == 8
+    finally:
+        nat.check(lib.fs_set_wait_limit_ns(0))
+    assert lib.fs_device_status(1) == 1
+    assert waited < 60, waited
+    for WW, bb in ((W, b), (W64, b64)):
+        tc = _tied(K, (x, fx, WW, bb, tau), r)
+        st.set_engine("fma")
+        try:
+            ex = _round(K, st, "fma", (x, fx, WW, bb, tau), r)
+        finally:
+            st.set_engine("auto")
+        ref = E.coupling_round(*[t.detach().clone().requires_grad_(True)
+                                 for t in (x, fx, WW, bb, tau)], r)
+        for k in tc:
+            et, ee = relerr(tc[k], ref[k]), relerr(ex[k], ref[k])
+            assert relerr(tc[k], ex[k]) <= 1e-5 or et <= 1.25 * ee + 1e-6, (k, et, ee)
+    assert lib.fs_device_status(1) == 0
