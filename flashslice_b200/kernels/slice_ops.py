@@ -480,7 +480,20 @@ def _slice_impl(x_mid, fx_mid, weight, bias, tau, dot):
     return z, s
 
 
+# The op-by-op backward ops at G = 64 run on the tensor cores through the
+# coupled backward kernel with the other op's contribution zeroed: the slice
+# backward is the coupled one with zero tokens (d_out tok^T vanishes; fx is
+# passed in d_out's place), the deslice backward is the dtokens pass (a slice
+# forward of d_out) and the coupled one with zero dz_num and ds (its dfx,
+# w dz_num = 0, is discarded). Exact zeros: the split products of 0 are 0.
+# Shapes the coupled kernel does not serve run the FMA backward kernels.
+
 def _slice_bwd_impl(x_mid, fx_mid, weight, bias, tau, dz_num, ds, dot):
+    if weight.shape[-2] == 64 and x_mid.shape[1] > 0:
+        r = native_coupled_bwd(x_mid, fx_mid, fx_mid, weight, bias, tau,
+                               torch.zeros_like(dz_num, dtype=torch.float32), dz_num, ds, dot)
+        if r is not None:
+            return r
     return native_slice_bwd(x_mid, fx_mid, weight, bias, tau, None, dz_num, ds, dot,
                             nat.FAMILY_SINGLE)
 
@@ -492,6 +505,14 @@ def _deslice_impl(x_mid, weight, bias, tau, tokens, dot):
 
 
 def _deslice_bwd_impl(x_mid, weight, bias, tau, tokens, d_out, dot):
+    if weight.shape[-2] == 64 and x_mid.shape[1] > 0 and \
+            _coupled_call(x_mid, d_out, weight, bias, tau, dot) is not None:
+        dtok, s = _slice_impl(x_mid, d_out, weight, bias, tau, dot)
+        r = native_coupled_bwd(x_mid, d_out, d_out, weight, bias, tau, tokens,
+                               torch.zeros_like(dtok), torch.zeros_like(s), dot)
+        if r is not None:
+            dxm, _, dw, db, dt = r
+            return dxm, dtok.to(tokens.dtype), dw, db, dt
     return native_deslice_bwd(x_mid, weight, bias, tau, tokens, None, d_out, dot,
                               nat.FAMILY_SINGLE)
 

@@ -209,3 +209,28 @@ def test_round_mix_strided_bf16_deterministic(env):
     for k in ("out", "grad:x", "grad:fx", "grad:W", "grad:b", "grad:tau"):
         assert relerr(tb[k], ref[k]) <= 2e-2, (k, relerr(tb[k], ref[k]))
     assert lib.fs_device_status(1) == 0
+
+
+@pytest.mark.parametrize("mode", ["gd", "bhgd"])
+def test_op_by_op_round_on_tensor_cores(env, mode):
+    """The reference's own surface at G = 64 -- fused_slice, fused_deslice and
+    autograd's backward of both -- runs on the tensor cores: the slice
+    backward as the coupled kernel with zero tokens, the deslice backward as
+    the dtokens pass plus the coupled kernel with zero dz_num and ds. Against
+    the float64 eager round and the exact FMA engine, every gradient."""
+    K, st, lib = env
+    x, fx, W, b, tau, _ = _inputs(20_011, mode, B=2 if mode == "bhgd" else 1)
+    r = torch.randn(x.shape, generator=torch.Generator().manual_seed(8),
+                    dtype=torch.float64).cuda()
+    n0 = lib.fs_tc_launch_count()
+    tc = _round(K, st, "auto", x, fx, W, b, tau, r, tied=False)
+    # slice, deslice; deslice backward (dtokens pass, coupled); slice backward (coupled)
+    assert lib.fs_tc_launch_count() - n0 == 5
+    ex = _round(K, st, "fma", x, fx, W, b, tau, r, tied=False)
+    from oracle import eager_torch as E
+    ref = E.coupling_round(*[t.detach().clone().requires_grad_(True)
+                             for t in (x, fx, W, b, tau)], r)
+    for k in ("out", "grad:x", "grad:fx", "grad:W", "grad:b", "grad:tau"):
+        et, ee = relerr(tc[k], ref[k]), relerr(ex[k], ref[k])
+        assert relerr(tc[k], ex[k]) <= 1e-5 or et <= 1.25 * ee + 1e-6, (k, et, ee)
+    assert lib.fs_device_status(1) == 0
