@@ -86,6 +86,8 @@ def parse():
                     help="config 4: let the model's torch GEMMs use TF32 (the coupling ops "
                          "stay exact fp32 either way)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the op-by-op and reverse-order figures")
     ap.add_argument("--cpu-sample", type=int, default=None,
                     help="points per CPU step (default: the workload's points per GPU, "
                          "at most 2^20)")
@@ -826,8 +828,8 @@ def main():
 
     # the reference's surface (op by op) and the reverse call order, same inputs
     extra = {}
-    if world == 1 and not K.slice_ops._use_blocked(cfg["D"], cfg["G"], cfg["DV"], dot,
-                                                    x.device):
+    if world == 1 and not args.no_extras and \
+            not K.slice_ops._use_blocked(cfg["D"], cfg["G"], cfg["DV"], dot, x.device):
         def obo():
             zero_grads(x, fx, W, b, tau)
             op_by_op_step(K, x, fx, W, b, tau, r)
