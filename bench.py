@@ -85,6 +85,8 @@ def parse():
     ap.add_argument("--tf32-gemms", action="store_true",
                     help="config 4: let the model's torch GEMMs use TF32 (the coupling ops "
                          "stay exact fp32 either way)")
+    ap.add_argument("--compile", action="store_true",
+                    help="config 4: run both models under torch.compile(fullgraph=True)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the op-by-op and reverse-order figures")
@@ -567,11 +569,12 @@ def run_model(args):
 
     def timed(model):
         opt = torch.optim.Adam(model.parameters(), lr=1e-4)
+        fwd = torch.compile(model, fullgraph=True) if args.compile else model
 
         def step():
             opt.zero_grad(set_to_none=True)
             with torch.autocast("cuda", dtype=torch.bfloat16, enabled=bool(args.bf16_autocast)):
-                loss = torch.nn.functional.mse_loss(model(xs, fs).float(), ys)
+                loss = torch.nn.functional.mse_loss(fwd(xs, fs).float(), ys)
             loss.backward()
             opt.step()
 
@@ -600,6 +603,7 @@ def run_model(args):
             "config": {"workload": "cfg4", "model": "Transolver", **MODEL4, "N": n,
                        "step": "forward + MSE backward + Adam", "l2": "activations larger "
                        "than L2, no flush", "gemms": "tf32" if args.tf32_gemms else "fp32",
+                       "compiled": bool(args.compile),
                        "eager_ms_per_step": round(ms_eager, 4),
                        "speedup_vs_eager": round(ms_eager / ms, 3)},
             "gpu_launches": launches,
