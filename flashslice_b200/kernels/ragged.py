@@ -87,11 +87,16 @@ class _Native:
         self.device = x_mid.device
 
     @staticmethod
-    def make(x_mid, dv, weight, bias, tau, dot, splits):
+    def make(x_mid, dv, weight, bias, tau, dot, splits, tied=False):
+        """``tied``: only the slice forward, deslice forward and coupled
+        backward will run (a tied round), which the engine also serves at
+        G = 64; the op-by-op backward entry points serve ragged rows at G = 32
+        only."""
         S = splits.numel() - 1
+        slots = (32, 64) if tied else (32,)
         if (x_mid.dtype not in (torch.float32, torch.bfloat16) or S > MAX_SPLITS or
-                x_mid.shape[1] == 0 or
-                x_mid.shape[3] != 32 or dv != 32 or weight.shape[-2] != 32 or not x_mid.is_cuda):
+                x_mid.shape[1] == 0 or x_mid.shape[3] != 32 or dv != 32 or
+                weight.shape[-2] not in slots or not x_mid.is_cuda):
             return None
         c = _Native(x_mid, dv, weight, bias, tau, dot, splits)
         return c if nat.load().fs_coupled_supported(ctypes.byref(c.prob)) else None
@@ -102,7 +107,7 @@ class _Native:
 
 def native_slice(x_mid, fx_mid, weight, bias, tau, splits, dot=0):
     """(z_num (S, H, G, DV), s (S, H, G)) in one launch, or None."""
-    c = _Native.make(x_mid, fx_mid.shape[3], weight, bias, tau, dot, splits)
+    c = _Native.make(x_mid, fx_mid.shape[3], weight, bias, tau, dot, splits, tied=True)
     if c is None or fx_mid.dtype != x_mid.dtype:
         return None
     x_mid, fx_mid = _tc_strides(x_mid), _tc_strides(fx_mid)
@@ -118,7 +123,7 @@ def native_slice(x_mid, fx_mid, weight, bias, tau, splits, dot=0):
 
 def native_deslice(x_mid, weight, bias, tau, tokens, splits, dot=0):
     """out (1, N_total, H, DV) in one launch, or None."""
-    c = _Native.make(x_mid, tokens.shape[3], weight, bias, tau, dot, splits)
+    c = _Native.make(x_mid, tokens.shape[3], weight, bias, tau, dot, splits, tied=True)
     if c is None:
         return None
     x_mid = _tc_strides(x_mid)
@@ -172,7 +177,7 @@ def native_deslice_bwd(x_mid, weight, bias, tau, tokens, d_out, splits, dot=0):
 
 def native_coupled_bwd(x_mid, fx_mid, d_out, weight, bias, tau, tokens, dz_num, ds, splits,
                        dot=0):
-    c = _Native.make(x_mid, fx_mid.shape[3], weight, bias, tau, dot, splits)
+    c = _Native.make(x_mid, fx_mid.shape[3], weight, bias, tau, dot, splits, tied=True)
     x_mid, fx_mid = _tc_strides(x_mid), _tc_strides(fx_mid)
     d_out = _tc_strides(d_out.to(x_mid.dtype))
     dx, dfx = torch.empty_like(x_mid), torch.empty_like(fx_mid)
@@ -285,8 +290,8 @@ def ragged_coupling(x_mid, fx_mid, weight, bias, tau, row_splits, mix=None, mix_
     if mix_params is None:
         mix_params = [q for q in mix.parameters()] if isinstance(mix, torch.nn.Module) else []
     params = tuple(q for q in mix_params if q.requires_grad)
-    if _Native.make(x_mid, fx_mid.shape[3], weight, bias, tau, 0, splits) is not None and \
-            fx_mid.dtype == x_mid.dtype:
+    if _Native.make(x_mid, fx_mid.shape[3], weight, bias, tau, 0, splits,
+                    tied=True) is not None and fx_mid.dtype == x_mid.dtype:
         return _CouplingRound.apply(x_mid, fx_mid, weight, bias, tau, eps, 0, mix, None,
                                     _RaggedOps(splits), *params)
     S = splits.numel() - 1

@@ -234,3 +234,46 @@ def test_op_by_op_round_on_tensor_cores(env, mode):
         et, ee = relerr(tc[k], ref[k]), relerr(ex[k], ref[k])
         assert relerr(tc[k], ex[k]) <= 1e-5 or et <= 1.25 * ee + 1e-6, (k, et, ee)
     assert lib.fs_device_status(1) == 0
+
+
+@pytest.mark.parametrize("mode", ["gd", "bhgd"])
+def test_ragged_round(env, mode):
+    """Ragged samples (different N packed along the point axis) through the
+    tied round at G = 64: one launch per op for all samples, every result
+    against the float64 eager round of each sample."""
+    K, st, lib = env
+    from flashslice_b200.kernels import ragged as R
+    from oracle import eager_torch as E
+    lens = [77, 4097, 0, 128, 1, 20_000]
+    S, N = len(lens), sum(lens)
+    g = torch.Generator().manual_seed(6)
+    r = lambda *s: torch.randn(*s, generator=g, dtype=torch.float64)  # noqa: E731
+    x, fx, up = r(1, N, 4, 32), r(1, N, 4, 32), r(1, N, 4, 32)
+    W = {"gd": r(G, 32), "bhgd": r(S, 4, G, 32)}[mode] / 32 ** 0.5
+    b = {"gd": r(G), "bhgd": r(S, 4, G)}[mode] * 0.1
+    tau = 0.3 + 0.7 * torch.rand(4, generator=g, dtype=torch.float64)
+    splits = [0]
+    for n in lens:
+        splits.append(splits[-1] + n)
+    x, fx, up, W, b, tau = (t.cuda() for t in (x, fx, up, W, b, tau))
+    leaves = [t.float().clone().requires_grad_(True) for t in (x, fx, W, b, tau)]
+    n0 = lib.fs_tc_launch_count()
+    out = R.ragged_coupling(*leaves, splits)
+    (out * up.float()).sum().backward()
+    torch.cuda.synchronize()
+    assert lib.fs_tc_launch_count() - n0 == 4
+    ref_leaves = [t.clone().requires_grad_(True) for t in (x, fx, W, b, tau)]
+    outs = []
+    for i in range(S):
+        a, e = splits[i], splits[i + 1]
+        Wi = ref_leaves[2][i:i + 1] if W.dim() == 4 else ref_leaves[2]
+        bi = ref_leaves[3][i:i + 1] if b.dim() == 3 else ref_leaves[3]
+        z, s = E.slice_fwd(ref_leaves[0][:, a:e], ref_leaves[1][:, a:e], Wi, bi, ref_leaves[4])
+        outs.append(E.deslice_fwd(ref_leaves[0][:, a:e], Wi, bi, ref_leaves[4],
+                                  z / (s + 1e-5)[..., None]))
+    ref = torch.cat(outs, dim=1)
+    (ref * up).sum().backward()
+    assert relerr(out, ref) <= 1e-5
+    for a, e, name in zip(leaves, ref_leaves, ("x", "fx", "W", "b", "tau")):
+        assert relerr(a.grad, e.grad) <= 2e-5, (name, relerr(a.grad, e.grad))
+    assert lib.fs_device_status(1) == 0
