@@ -160,12 +160,25 @@ bool blk_tc_params(const fs_problem& p, const fs_tensor4* x, const fs_tensor4* v
   q.G = (int)p.G;
   q.dv = (int)p.DV;
   q.ntiles = (int)((p.N + 127) / 128);
-  // ctas_per_sm CTAs per SM over (slot blocks x b x h), one wave, within the partial
-  // buffers (sized for max_p programs per slot block of the FMA kernels)
-  int64_t P = ctas_per_sm * kSmCount / (p.B * p.H * (p.G / 128));
-  if (P > max_p) P = max_p;
-  if (P > q.ntiles) P = q.ntiles;
-  q.P = (int)(P < 1 ? 1 : P);
+  // Programs per (slot block, b, h): the fewest that fill whole waves of
+  // ctas_per_sm CTAs per SM to 97% (one program per unit would leave SMs
+  // idle: config 3's 128 slot blocks on 148 SMs), within the partial
+  // buffers (max_p programs) and the tiles; a function of the shape only.
+  const int64_t units = p.B * p.H * (p.G / 128), slots = (int64_t)ctas_per_sm * kSmCount;
+  int64_t lim = max_p < q.ntiles ? max_p : q.ntiles;
+  if (lim < 1) lim = 1;
+  int64_t P = 1;
+  double best = 0.0;
+  for (int64_t c = 1; c <= lim; ++c) {
+    const int64_t waves = (units * c + slots - 1) / slots;
+    const double eff = (double)(units * c) / (double)(waves * slots);
+    if (eff > best + 1e-9) {
+      best = eff;
+      P = c;
+    }
+    if (eff >= 0.97) break;
+  }
+  q.P = (int)P;
   q.W = W;
   q.bias = bias;
   q.tau = tau;
@@ -234,9 +247,11 @@ bool tc_params(const fs_problem& p, tcx::TcKind k, const fs_tensor4* x, const fs
   return true;
 }
 
+constexpr int kBlkTcMaxP = 16;
+
 struct Setup {
   bool fused;
-  int nt, ntiles, ngb, Pn, Pg, BH;
+  int nt, ntiles, ngb, Pn, Pg, Pgb, BH;
   bool internal_stats;
   size_t stats, delta, partA, partB, partS, partDt, total;
   bool has_img;  // operand images of the blocked point-owning tensor-core kernels
@@ -264,6 +279,9 @@ Setup setup(int op, const fs_problem& p) {
   };
   s.Pn = clampP((kTargetCtas + s.BH - 1) / s.BH);
   s.Pg = clampP((kTargetCtas + (int64_t)s.BH * s.ngb - 1) / ((int64_t)s.BH * s.ngb));
+  // the blocked tensor-core slot-owning kernels pick up to kBlkTcMaxP programs
+  // per slot block (to fill whole waves); their partials need room for them
+  const int Pgb = s.Pgb = blk_tc_shape(p) && s.Pg < kBlkTcMaxP ? clampP(kBlkTcMaxP) : s.Pg;
   const bool has_in = p.flags & FS_FLAG_STATS_IN;
   const bool has_out = p.flags & FS_FLAG_STATS_OUT;
   size_t off = 0;
@@ -280,8 +298,8 @@ Setup setup(int op, const fs_problem& p) {
         s.partS = take(BH * s.Pn * G);
       } else {
         s.internal_stats = !has_in && !(p.family == FS_FAMILY_BLOCKED && has_out);
-        s.partA = take(BH * s.Pg * G * DV);
-        s.partS = take(BH * s.Pg * G);
+        s.partA = take(BH * Pgb * G * DV);
+        s.partS = take(BH * Pgb * G);
       }
       break;
     case FS_OP_DESLICE_FWD:
@@ -299,9 +317,9 @@ Setup setup(int op, const fs_problem& p) {
         s.internal_stats = !has_in;
         s.delta = take(BH * 2 * p.N);
         s.partDt = take(BH * s.Pn);
-        s.partA = take(BH * s.Pg * G * D);
-        if (!sl) s.partB = take(BH * s.Pg * G * DV);
-        s.partS = take(BH * s.Pg * G);
+        s.partA = take(BH * Pgb * G * D);
+        if (!sl) s.partB = take(BH * Pgb * G * DV);
+        s.partS = take(BH * Pgb * G);
       }
       break;
     }
@@ -602,7 +620,7 @@ int fs_slice_fwd(const fs_problem* p, const fs_tensor4* x_mid, const fs_tensor4*
     q.stats_in = stats;
     tcx::TcParams tb;
     if (blk_tc_shape(*p) && tc_tensor_ok(x_mid) && tc_tensor_ok(fx_mid) &&
-        blk_tc_params(*p, x_mid, fx_mid, weight, bias, tau, stats, s.Pg, tb)) {
+        blk_tc_params(*p, x_mid, fx_mid, weight, bias, tau, stats, s.Pgb, tb)) {
       // the partial buffers sized for the FMA kernels hold the (fewer) CTAs'
       tb.partA = q.partA;
       tb.partS = q.partS;
@@ -787,7 +805,7 @@ static int bwd_common(bool slice, const fs_problem* p, const fs_tensor4* x_mid,
     q.delta = at(workspace, s.delta);
     tcx::TcParams tb;
     const bool blk_tc = blk_tc_shape(*p) && tc_tensor_ok(x_mid) && tc_tensor_ok(vals) &&
-                        blk_tc_params(*p, x_mid, vals, weight, bias, tau, stats, s.Pg, tb, 1);
+                        blk_tc_params(*p, x_mid, vals, weight, bias, tau, stats, s.Pgb, tb, 1);
     if (blk_tc && s.has_img && tc_tensor_ok(dx) && (!slice || tc_tensor_ok(dfx))) {
       tcx::TcParams tn = tb;
       tn.M = mat;
