@@ -912,9 +912,15 @@ int fs_coupled_bwd(const fs_problem* p, const fs_tensor4* x_mid, const fs_tensor
   if (!tc_params(*p, kind, x_mid, fx_mid, weight, bias, tau, tq) ||
       !point_map(&tq.mo, *p, d_out))
     return fail(FS_ERR_UNSUPPORTED, "no TMA tensor map for the point tensors");
-  if (g64) {  // partials of the slot-blocked layout
-    if (tq.P > s.Pg) tq.P = s.Pg;
-    if (tq.P > s.Pn) tq.P = s.Pn;
+  if (g64) {
+    // one CTA per SM: two whole waves (B H P = 2 x 148 when B H divides it)
+    // leave no SM idle where one wave of 148 / (B H) programs would; within
+    // the tiles and the partials of the slot-blocked layout
+    int64_t P = 2 * kSmCount / ((int64_t)p->B * p->H);
+    if (P > tq.ntiles) P = tq.ntiles;
+    if (P > s.Pg) P = s.Pg;
+    if (P > s.Pn) P = s.Pn;
+    tq.P = (int)(P < 1 ? 1 : P);
   }
   cudaStream_t st = (cudaStream_t)stream;
   tq.M = tokens;
