@@ -61,6 +61,7 @@
 #include <cudaTypedefs.h>
 
 #include <atomic>
+#include <type_traits>
 #include <cstring>
 
 #include "fs_launch.h"
@@ -356,6 +357,11 @@ __host__ __device__ constexpr int stage_bytes() {
   return kTile * 32 * (int)sizeof(PT);
 }
 
+// point tensors of type PT have only a hi part (bf16: each value is its own
+// hi part, mid and lo are zero), so the MMAs of their other parts are skipped
+template <typename PT>
+constexpr bool kHi = std::is_same<PT, __nv_bfloat16>::value;
+
 // two result values of a row stored in the point tensor's type
 __device__ __forceinline__ void store2(float* p, float2 v) { *(float2*)p = v; }
 __device__ __forceinline__ void store2(__nv_bfloat16* p, float2 v) {
@@ -474,7 +480,11 @@ __device__ __forceinline__ void mma_ts(uint32_t d, uint32_t a, uint64_t b, uint3
 // The NW = 64 schedule (below) of D = A1 B1^T, or with S = 2 of
 // D = A1 B1^T + A2 B2^T into one accumulator, the two products' partial
 // products interleaved so that the small ones still go first.
-template <bool MN, int S>
+//
+// AHI: the point operands have only a hi part (bf16 points: their lo and mid
+// parts are zero), so only their hi-part MMAs run: hi x [B_mid | B_hi] first
+// (it sets all 64 columns), then hi x B_lo into the B_mid group.
+template <bool MN, int S, bool AHI = false>
 __device__ __forceinline__ void wide_ts64_pair(uint32_t d, uint32_t a1, uint64_t b1, uint32_t a2,
                                                uint64_t b2) {
   constexpr uint32_t id64 = idesc_bf16(128, 64, 0, MN ? 1 : 0);
@@ -483,24 +493,37 @@ __device__ __forceinline__ void wide_ts64_pair(uint32_t d, uint32_t a1, uint64_t
   constexpr int mid = MN ? 512 : 2048;       // offset of B_mid
   const uint32_t a[2] = {a1, a2};
   const uint64_t b[2] = {b1, b2};
-#pragma unroll
-  for (int pa = 0; pa < 2; ++pa)
+  if constexpr (AHI) {
 #pragma unroll
     for (int s = 0; s < S; ++s)
 #pragma unroll
       for (int ks = 0; ks < 2; ++ks)
-        mma_ts(d, a[s] + pa * 16 + ks * 8, b[s] + ((mid + ks * kstep) >> 4), id64,
-               (pa | s | ks) != 0);
+        mma_ts(d, a[s] + 32 + ks * 8, b[s] + ((mid + ks * kstep) >> 4), id64, (s | ks) != 0);
 #pragma unroll
-  for (int s = 0; s < S; ++s)
+    for (int s = 0; s < S; ++s)
 #pragma unroll
-    for (int ks = 0; ks < 2; ++ks)
-      mma_ts(d, a[s] + 32 + ks * 8, b[s] + ((ks * kstep) >> 4), id32, true);
+      for (int ks = 0; ks < 2; ++ks)
+        mma_ts(d, a[s] + 32 + ks * 8, b[s] + ((ks * kstep) >> 4), id32, true);
+  } else {
 #pragma unroll
-  for (int s = 0; s < S; ++s)
+    for (int pa = 0; pa < 2; ++pa)
 #pragma unroll
-    for (int ks = 0; ks < 2; ++ks)
-      mma_ts(d, a[s] + 32 + ks * 8, b[s] + ((mid + ks * kstep) >> 4), id64, true);
+      for (int s = 0; s < S; ++s)
+#pragma unroll
+        for (int ks = 0; ks < 2; ++ks)
+          mma_ts(d, a[s] + pa * 16 + ks * 8, b[s] + ((mid + ks * kstep) >> 4), id64,
+                 (pa | s | ks) != 0);
+#pragma unroll
+    for (int s = 0; s < S; ++s)
+#pragma unroll
+      for (int ks = 0; ks < 2; ++ks)
+        mma_ts(d, a[s] + 32 + ks * 8, b[s] + ((ks * kstep) >> 4), id32, true);
+#pragma unroll
+    for (int s = 0; s < S; ++s)
+#pragma unroll
+      for (int ks = 0; ks < 2; ++ks)
+        mma_ts(d, a[s] + 32 + ks * 8, b[s] + ((mid + ks * kstep) >> 4), id64, true);
+  }
 }
 
 // Wide product D = A B^T, A = point rows in TMEM at `a` (K = 32), B = small
@@ -519,26 +542,34 @@ __device__ __forceinline__ void wide_ts64_pair(uint32_t d, uint32_t a1, uint64_t
 //    stacked copy of M (B[n][k] = M[k][n]).
 // An MMA with N <= 96 takes about as long as one with N = 32, so NW = 96
 // and NW = 64 cost half and two thirds of NW = 32.
-template <int NW, bool MN>
+// AHI: the point operand has only a hi part (bf16 points), so only its
+// hi-part MMAs run.
+template <int NW, bool MN, bool AHI = false>
 __device__ __forceinline__ void wide_ts(uint32_t d, uint32_t a, uint64_t bd) {
   if constexpr (NW == 64) {
-    wide_ts64_pair<MN, 1>(d, a, bd, a, bd);
+    wide_ts64_pair<MN, 1, AHI>(d, a, bd, a, bd);
   } else if constexpr (NW == 32) {
     constexpr uint32_t id = idesc_bf16(128, 32, 0, MN ? 1 : 0);
+    bool first = true;
 #pragma unroll
-    for (int i = 0; i < 6; ++i)
+    for (int i = 0; i < 6; ++i) {
+      if (AHI && part_a(i) != 2) continue;
 #pragma unroll
-      for (int ks = 0; ks < 2; ++ks)
+      for (int ks = 0; ks < 2; ++ks) {
         mma_ts(d, a + part_a(i) * 16 + ks * 8,
-               bd + ((part_b(i) * 2048 + ks * (MN ? 1024 : 256)) >> 4), id, (i | ks) != 0);
+               bd + ((part_b(i) * 2048 + ks * (MN ? 1024 : 256)) >> 4), id, !first);
+        first = false;
+      }
+    }
   } else {
     constexpr uint32_t id = idesc_bf16(128, 96, 0, MN ? 1 : 0);
+    constexpr int pa0 = AHI ? 2 : 0;
 #pragma unroll
-    for (int pa = 0; pa < 3; ++pa)
+    for (int pa = pa0; pa < 3; ++pa)
 #pragma unroll
       for (int ks = 0; ks < 2; ++ks)
         mma_ts(d, a + pa * 16 + ks * 8, bd + ((ks * (MN ? 2 * kRS : 256)) >> 4), id,
-               (pa | ks) != 0);
+               (pa != pa0) || ks != 0);
   }
 }
 
@@ -546,13 +577,17 @@ __device__ __forceinline__ void wide_ts(uint32_t d, uint32_t a, uint64_t bd) {
 // rows of a stacked buffer read K-major (part p at +512 p), B = the small
 // operand's three parts stacked along N (K-major); six MMAs, A parts lo, mid,
 // hi accumulated one after the other.
+// (AHI: the point rows have only a hi part, bf16 points: only its MMAs run)
+template <bool AHI = false>
 __device__ __forceinline__ void wide_ss96(uint32_t d, uint64_t ad, uint64_t bd) {
   constexpr uint32_t id = idesc_bf16(128, 96, 0, 0);
+  constexpr int pa0 = AHI ? 2 : 0;
 #pragma unroll
-  for (int pa = 0; pa < 3; ++pa)
+  for (int pa = pa0; pa < 3; ++pa)
 #pragma unroll
     for (int ks = 0; ks < 2; ++ks)
-      mma_bf16(d, ad + ((pa * 512 + ks * 256) >> 4), bd + ((ks * 256) >> 4), id, (pa | ks) != 0);
+      mma_bf16(d, ad + ((pa * 512 + ks * 256) >> 4), bd + ((ks * 256) >> 4), id,
+               (pa != pa0) || ks != 0);
 }
 
 __device__ __forceinline__ uint64_t desc_rowsA(const void* p) {
@@ -991,7 +1026,7 @@ __global__ void __launch_bounds__(128 * kTSliceFwd, kCtasSliceFwd)
     to_async_barrier();
     if (c.issuer()) {
       prefetch<PT>(p, stX, fbuf(1), h, sp, tile, c.bar);  // F[1] is unused yet
-      wide_ts<96, false>(tL, tX, dWs);  // logits = x W^T
+      wide_ts<96, false, kHi<PT>>(tL, tX, dWs);  // logits = x W^T
       commit(c, kG1);
     }
   }
@@ -1021,7 +1056,7 @@ __global__ void __launch_bounds__(128 * kTSliceFwd, kCtasSliceFwd)
           mbar_arrive_expect_tx(c.bar + kBarTma, 2 * stage_bytes<PT>());
           tma_load_4d(stX, &p.mx, 0, h, sp.row(tile + 2 * p.P), sp.bc, c.bar + kBarTma);
         }
-        wide_ts<96, false>(tL, tX, dWs);
+        wide_ts<96, false, kHi<PT>>(tL, tX, dWs);
         commit(c, kG1);
       }
     }
@@ -1083,7 +1118,7 @@ __global__ void __launch_bounds__(128 * kTDesliceFwd, kCtasDesliceFwd)
     to_async_barrier();
     if (c.issuer()) {
       prefetch<PT>(p, sm + kDfStageX, nullptr, h, sp, tile, c.bar);
-      wide_ts<kNwDf, false>(tL, tA, dWs);  // logits = x W^T
+      wide_ts<kNwDf, false, kHi<PT>>(tL, tA, dWs);  // logits = x W^T
       commit(c, kG1);
     }
     wait_bar(c, kG1, p.status);
@@ -1169,9 +1204,9 @@ __global__ void __launch_bounds__(128 * kTSliceBwd, kCtasSliceBwd)
     to_async_barrier();
     if (c.issuer()) {
       prefetch<PT>(p, sm + kSbStageX, sm + kSbStageF, h, sp, tile, c.bar);
-      wide_ts<96, false>(tL, tX, dWk);  // logits = x W^T
+      wide_ts<96, false, kHi<PT>>(tL, tX, dWk);  // logits = x W^T
       commit(c, kG1);
-      wide_ts<64, false>(tDw, tF, dZk);  // dw = fx dz_num^T
+      wide_ts<64, false, kHi<PT>>(tDw, tF, dZk);  // dw = fx dz_num^T
       commit(c, kG2);
     }
     {
@@ -1287,9 +1322,9 @@ __global__ void __launch_bounds__(128 * kTDesliceBwd, kCtasDesliceBwd)
     }
     to_async_barrier();
     if (c.issuer()) {
-      wide_ts<96, false>(tL, tX, dWk);  // logits = x W^T
+      wide_ts<96, false, kHi<PT>>(tL, tX, dWk);  // logits = x W^T
       commit(c, kG1);
-      wide_ts<64, false>(tDw, tO, dTk);  // dw = d_out tok^T
+      wide_ts<64, false, kHi<PT>>(tDw, tO, dTk);  // dw = d_out tok^T
       commit(c, kG2);
     }
     {
@@ -1443,9 +1478,9 @@ __global__ void __launch_bounds__(128 * kTCoupledBwd, kCtasCoupledBwd)
         tma_load_4d(stX, &p.mx, 0, h, sp.row(tile + p.P), sp.bc, c.bar + kBarTma);
         tma_load_4d(stF, &p.mv, 0, h, sp.row(tile + p.P), sp.bc, c.bar + kBarTma);
       }
-      wide_ss96(tL, dXa, dWk);  // logits = x W^T
+      wide_ss96<kHi<PT>>(tL, dXa, dWk);  // logits = x W^T
       commit(c, kG1);
-      wide_ts64_pair<false, 2>(tD, tO, dTk, tF, dZk);  // d_out tok^T + fx dz_num^T
+      wide_ts64_pair<false, 2, kHi<PT>>(tD, tO, dTk, tF, dZk);  // d_out tok^T + fx dz_num^T
       commit(c, kG2);
     }
     {
@@ -2251,18 +2286,29 @@ __device__ __forceinline__ RowConst row_const64(float* bias_s, const float* bias
 // small operand: A lo and mid times [W_mid | W_hi], A hi times W_lo into
 // the W_mid group, A hi times [W_mid | W_hi] -- seven of the nine partial
 // products (the two left out are below 2^-26 of the result), small first.
+// (AHI: the point operand has only a hi part, bf16 points: hi x [W_mid |
+// W_hi] first, which sets all 128 columns, then hi x W_lo.)
+template <bool AHI = false>
 __device__ __forceinline__ void logits64(uint32_t d, uint32_t a, uint64_t bd) {
   constexpr uint32_t id128 = idesc_bf16(128, 128, 0, 0), id64 = idesc_bf16(128, 64, 0, 0);
-#pragma unroll
-  for (int pa = 0; pa < 2; ++pa)
+  if constexpr (AHI) {
 #pragma unroll
     for (int ks = 0; ks < 2; ++ks)
-      mma_ts(d, a + pa * 16 + ks * 8, bd + ((4096 + ks * 256) >> 4), id128, (pa | ks) != 0);
+      mma_ts(d, a + 32 + ks * 8, bd + ((4096 + ks * 256) >> 4), id128, ks != 0);
 #pragma unroll
-  for (int ks = 0; ks < 2; ++ks) mma_ts(d, a + 32 + ks * 8, bd + ((ks * 256) >> 4), id64, true);
+    for (int ks = 0; ks < 2; ++ks) mma_ts(d, a + 32 + ks * 8, bd + ((ks * 256) >> 4), id64, true);
+  } else {
 #pragma unroll
-  for (int ks = 0; ks < 2; ++ks)
-    mma_ts(d, a + 32 + ks * 8, bd + ((4096 + ks * 256) >> 4), id128, true);
+    for (int pa = 0; pa < 2; ++pa)
+#pragma unroll
+      for (int ks = 0; ks < 2; ++ks)
+        mma_ts(d, a + pa * 16 + ks * 8, bd + ((4096 + ks * 256) >> 4), id128, (pa | ks) != 0);
+#pragma unroll
+    for (int ks = 0; ks < 2; ++ks) mma_ts(d, a + 32 + ks * 8, bd + ((ks * 256) >> 4), id64, true);
+#pragma unroll
+    for (int ks = 0; ks < 2; ++ks)
+      mma_ts(d, a + 32 + ks * 8, bd + ((4096 + ks * 256) >> 4), id128, true);
+  }
 }
 
 // This thread's CG logits (slots CG cs ..) from the [W_mid | W_hi] groups.
@@ -2428,7 +2474,7 @@ __global__ void __launch_bounds__(256, 2) k_tc_slice_fwd64(const __grid_constant
         mbar_arrive_expect_tx(c.bar + kBarTma, 2 * stage_bytes<PT>());
         tma_load_4d(stX, &p.mx, 0, h, sp.row(tile + p.P), sp.bc, c.bar + kBarTma);
       }
-      logits64(tL, tX, dWs);
+      logits64<kHi<PT>>(tL, tX, dWs);
       commit(c, kG1);
     }
     wait_bar(c, kG1, p.status);
@@ -2541,7 +2587,7 @@ __global__ void __launch_bounds__(256, 2) k_tc_deslice_fwd64(const __grid_consta
     if (c.issuer()) {
       if (k + 2 < n_my)  // stage k & 1 is consumed: the tile after next
         tma_tile<PT>(p, stage(k), nullptr, h, sp, tile + 2 * p.P, c.bar + sbar(k));
-      logits64(tL, tX, dWs);
+      logits64<kHi<PT>>(tL, tX, dWs);
       commit(c, kG1);
     }
     wait_bar(c, kG1, p.status);
@@ -2596,46 +2642,69 @@ static_assert(kC6XS % 1024 == 0, "stage tiles need 1 KB alignment");
 
 // logits64 with the point operand x in shared memory (the stacked buffer
 // with a ones part, read K-major: part p at +512 p)
+template <bool AHI = false>
 __device__ __forceinline__ void logits64_ss(uint32_t d, const uint8_t* xs, uint64_t bd) {
   constexpr uint32_t id128 = idesc_bf16(128, 128, 0, 0), id64 = idesc_bf16(128, 64, 0, 0);
   auto ad = [&](int part, int ks) { return smem_desc(smem_u32(xs + 512 * part + 256 * ks), 128, kRS4); };
-#pragma unroll
-  for (int pa = 0; pa < 2; ++pa)
+  if constexpr (AHI) {  // bf16 points: hi part only (as logits64)
 #pragma unroll
     for (int ks = 0; ks < 2; ++ks)
-      mma_bf16(d, ad(pa, ks), bd + ((4096 + ks * 256) >> 4), id128, (pa | ks) != 0);
+      mma_bf16(d, ad(2, ks), bd + ((4096 + ks * 256) >> 4), id128, ks != 0);
 #pragma unroll
-  for (int ks = 0; ks < 2; ++ks) mma_bf16(d, ad(2, ks), bd + ((ks * 256) >> 4), id64, true);
+    for (int ks = 0; ks < 2; ++ks) mma_bf16(d, ad(2, ks), bd + ((ks * 256) >> 4), id64, true);
+  } else {
 #pragma unroll
-  for (int ks = 0; ks < 2; ++ks)
-    mma_bf16(d, ad(2, ks), bd + ((4096 + ks * 256) >> 4), id128, true);
+    for (int pa = 0; pa < 2; ++pa)
+#pragma unroll
+      for (int ks = 0; ks < 2; ++ks)
+        mma_bf16(d, ad(pa, ks), bd + ((4096 + ks * 256) >> 4), id128, (pa | ks) != 0);
+#pragma unroll
+    for (int ks = 0; ks < 2; ++ks) mma_bf16(d, ad(2, ks), bd + ((ks * 256) >> 4), id64, true);
+#pragma unroll
+    for (int ks = 0; ks < 2; ++ks)
+      mma_bf16(d, ad(2, ks), bd + ((4096 + ks * 256) >> 4), id128, true);
+  }
 }
 
 // D = A1 B1^T + A2 B2^T into one 128-column accumulator [. B_mid | . B_hi]
 // (64-row small operands, point operands in TMEM, K = 32): the logits64
 // schedule of both products, their partial products interleaved.
+template <bool AHI = false>
 __device__ __forceinline__ void wide64_pair(uint32_t d, uint32_t a1, uint64_t b1, uint32_t a2,
                                             uint64_t b2) {
   constexpr uint32_t id128 = idesc_bf16(128, 128, 0, 0), id64 = idesc_bf16(128, 64, 0, 0);
   const uint32_t a[2] = {a1, a2};
   const uint64_t b[2] = {b1, b2};
-#pragma unroll
-  for (int pa = 0; pa < 2; ++pa)
+  if constexpr (AHI) {  // bf16 points: hi parts only (as logits64)
 #pragma unroll
     for (int s = 0; s < 2; ++s)
 #pragma unroll
       for (int ks = 0; ks < 2; ++ks)
-        mma_ts(d, a[s] + pa * 16 + ks * 8, b[s] + ((4096 + ks * 256) >> 4), id128,
-               (pa | s | ks) != 0);
+        mma_ts(d, a[s] + 32 + ks * 8, b[s] + ((4096 + ks * 256) >> 4), id128, (s | ks) != 0);
 #pragma unroll
-  for (int s = 0; s < 2; ++s)
+    for (int s = 0; s < 2; ++s)
 #pragma unroll
-    for (int ks = 0; ks < 2; ++ks) mma_ts(d, a[s] + 32 + ks * 8, b[s] + ((ks * 256) >> 4), id64, true);
+      for (int ks = 0; ks < 2; ++ks)
+        mma_ts(d, a[s] + 32 + ks * 8, b[s] + ((ks * 256) >> 4), id64, true);
+  } else {
 #pragma unroll
-  for (int s = 0; s < 2; ++s)
+    for (int pa = 0; pa < 2; ++pa)
 #pragma unroll
-    for (int ks = 0; ks < 2; ++ks)
-      mma_ts(d, a[s] + 32 + ks * 8, b[s] + ((4096 + ks * 256) >> 4), id128, true);
+      for (int s = 0; s < 2; ++s)
+#pragma unroll
+        for (int ks = 0; ks < 2; ++ks)
+          mma_ts(d, a[s] + pa * 16 + ks * 8, b[s] + ((4096 + ks * 256) >> 4), id128,
+                 (pa | s | ks) != 0);
+#pragma unroll
+    for (int s = 0; s < 2; ++s)
+#pragma unroll
+      for (int ks = 0; ks < 2; ++ks) mma_ts(d, a[s] + 32 + ks * 8, b[s] + ((ks * 256) >> 4), id64, true);
+#pragma unroll
+    for (int s = 0; s < 2; ++s)
+#pragma unroll
+      for (int ks = 0; ks < 2; ++ks)
+        mma_ts(d, a[s] + 32 + ks * 8, b[s] + ((4096 + ks * 256) >> 4), id128, true);
+  }
 }
 
 template <typename PT, int T>
@@ -2698,9 +2767,9 @@ __global__ void __launch_bounds__(128 * T, 1) k_tc_coupled_bwd64(const __grid_co
     to_async_barrier();
     if (c.issuer()) {
       if (tile + p.P < sp.ntiles) load3(tile + p.P);  // the stages are consumed
-      logits64_ss(tL, XS, dWk);
+      logits64_ss<kHi<PT>>(tL, XS, dWk);
       commit(c, kG1);
-      wide64_pair(tD, tO, dTk, tF, dZk);  // d_out tok^T + fx dz_num^T
+      wide64_pair<kHi<PT>>(tD, tO, dTk, tF, dZk);  // d_out tok^T + fx dz_num^T
       commit(c, kG2);
     }
     {
