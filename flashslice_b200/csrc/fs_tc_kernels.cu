@@ -2418,12 +2418,16 @@ __device__ __forceinline__ void pool64_write(float* xch, const float (&acc)[64 /
 }
 
 // ------------------------------------------------------------ slice forward, G = 64
-// One CTA of 256 threads (two per point row), two CTAs per SM; the phases
-// of a tile run in turn (the co-resident CTA fills the gaps).
+// One CTA of 256 threads (two per point row), two CTAs per SM.
 // smem: [stage x][F: fx staged, then its split with a ones part][WS: w, 64
 //       slots][W][bias][red][bars]
 // TMEM (256 columns): logits at 0 (128), the z pool at 0 (192, once the
 // logits are read), the x point operand at 192.
+// x and fx arrive on barriers of their own (kBarTma, kG3). A tile's x is
+// split and its logits issued at the end of the previous tile (once that
+// tile's pool is drained out of the columns the logits take), so the fx
+// split runs under the logits MMAs, and the next fx -- which can load only
+// once the pool is done with F -- has the drain and the x split to land.
 constexpr int kS6StageX = 0, kS6F = kStage, kS6WS = kS6F + kSplit4, kS6Ws = kS6WS + kSplitW,
               kS6Bias = kS6Ws + kSmall64, kS6Red = kS6Bias + 256,
               kS6Bar = kS6Red + red_bytes(2, 2), kS6Bytes = kS6Bar + kBarBytes;
@@ -2451,31 +2455,47 @@ __global__ void __launch_bounds__(256, 2) k_tc_slice_fwd64(const __grid_constant
   float acc[32];
 #pragma unroll
   for (int i = 0; i < 32; ++i) acc[i] = 0.f;
+  auto load_x = [&](int t) {  // one thread
+    mbar_arrive_expect_tx(c.bar + kBarTma, stage_bytes<PT>());
+    tma_load_4d(stX, &p.mx, 0, h, sp.row(t), sp.bc, c.bar + kBarTma);
+  };
+  auto load_f = [&](int t) {  // one thread
+    mbar_arrive_expect_tx(c.bar + kG3, stage_bytes<PT>());
+    tma_load_4d(F, &p.mv, 0, h, sp.row(t), sp.bc, c.bar + kG3);
+  };
+  // tile t's x into the TMEM operand and its logits issued; the barrier
+  // also orders the last drain of the pool before the logits overwrite it,
+  // and every read of the x stage before the next x loads into it
+  auto x_phase = [&](int t) {
+    wait_bar(c, kBarTma, p.status);
+    {
+      RowVals<16, PT> x;
+      x.load(stX, th.row, th.cs);
+      x.split().to_tmem(tX + th.lane_off, th.cs);
+      tst_wait();
+    }
+    to_async_barrier();
+    if (c.issuer()) {
+      if (t + p.P < sp.ntiles) load_x(t + p.P);
+      logits64<kHi<PT>>(tL, tX, dWs);
+      commit(c, kG1);
+    }
+  };
   int tile = blockIdx.x;
-  if (c.issuer() && tile < sp.ntiles) tma_tile<PT>(p, stX, F, h, sp, tile, c.bar);
+  if (c.issuer() && tile < sp.ntiles) {
+    load_x(tile);
+    load_f(tile);
+  }
+  if (tile < sp.ntiles) x_phase(tile);
   for (; tile < sp.ntiles; tile += p.P) {
     const int n0 = tile * kTile;
     const bool more = tile + p.P < sp.ntiles;
-    wait_bar(c, kBarTma, p.status);
-    RowVals<16, PT> x, f;
-    x.load(stX, th.row, th.cs);
-    f.load(F, th.row, th.cs);
-    // every staged fx row is in registers before F is overwritten, and the
-    // last tile's pool is read out of TMEM before the logits overwrite it
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    x.split().to_tmem(tX + th.lane_off, th.cs);
-    split_to_smem4(f.split(), F, th.row, th.cs);
-    tst_wait();
-    to_async_barrier();
-    if (c.issuer()) {
-      if (more) {  // the next tile's x now, its fx once the pool is done with F
-        mbar_arrive_expect_tx(c.bar + kBarTma, 2 * stage_bytes<PT>());
-        tma_load_4d(stX, &p.mx, 0, h, sp.row(tile + p.P), sp.bc, c.bar + kBarTma);
-      }
-      logits64<kHi<PT>>(tL, tX, dWs);
-      commit(c, kG1);
+    wait_bar(c, kG3, p.status);
+    {
+      RowVals<16, PT> f;
+      f.load(F, th.row, th.cs);
+      __syncthreads();  // every staged fx row is in registers before F is overwritten
+      split_to_smem4(f.split(), F, th.row, th.cs);
     }
     wait_bar(c, kG1, p.status);
     {
@@ -2484,15 +2504,15 @@ __global__ void __launch_bounds__(256, 2) k_tc_slice_fwd64(const __grid_constant
       softmax_fwd<T, 32>(lg, rc, n0 + th.row < sp.N, red, th);
       split_to_smemw(Split<32>(lg), WS, th.row, th.cs);
     }
-    to_async_barrier();
+    to_async_barrier();  // the F and WS splits, and the logits read out
     if (c.issuer()) {
       mma_pool64(tP, F, WS);  // [fx; 1]^T w
       commit(c, kG2);
     }
     wait_bar(c, kG2, p.status);
-    if (c.issuer() && more)
-      tma_load_4d(F, &p.mv, 0, h, sp.row(tile + p.P), sp.bc, c.bar + kBarTma);
+    if (c.issuer() && more) load_f(tile + p.P);  // F is free once the pool is done
     drain_pool64(tP + th.lane_off, th.cs, acc);
+    if (more) x_phase(tile + p.P);
   }
   const int64_t slot = (int64_t)bh * p.P + blockIdx.x;
   tc_fence_before();
