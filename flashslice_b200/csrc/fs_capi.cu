@@ -77,14 +77,16 @@ int check_problem(const fs_problem* p) {
 // The calls below serve row splits on the tensor-core engine only.
 int ragged_unsupported(const char* op) {
   return fail(FS_ERR_UNSUPPORTED,
-              "%s with row_splits needs the tensor-core engine: fp32 single-tile problems "
-              "with D = DV = G = 32, TMA-addressable point tensors, at most %d samples", op,
-              FS_MAX_SPLITS);
+              "%s with row_splits needs the tensor-core engine: single-tile problems with "
+              "fp32 or bf16 point tensors, D = DV = 32 and G = 32 (every op) or G = 64 (slice "
+              "forward, deslice forward, coupled backward), TMA-addressable point tensors, at "
+              "most %d samples", op, FS_MAX_SPLITS);
 }
 
 // ---------------------------------------------------------------- tensor-core path
-// The tcgen05 kernels serve the single-tile family for fp32 point tensors
-// with D = DV = G = 32 whose rows TMA can address. Their CTA count per
+// The tcgen05 kernels serve the single-tile family for fp32 or bf16 point
+// tensors with D = DV = 32 and G = 32 or 64 whose rows TMA can address, and
+// the blocked family's bf16 shapes (blk_tc_shape). Their CTA count per
 // (b, h) is a function of the shape only (148 SMs of a B200 as a constant),
 // so results stay bitwise reproducible.
 constexpr int kSmCount = 148;

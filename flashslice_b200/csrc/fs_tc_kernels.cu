@@ -1,6 +1,8 @@
 // flashslice_b200 -- tensor-core (tcgen05) kernels of the single-tile family
-// for the hot shape: D = DV = G = 32, fp32 or bf16 point tensors (the kernels
-// are templated on the point type; a bf16 value is its own exact hi part).
+// for the hot shape: D = DV = 32, G = 32 (and the G = 64 round further down),
+// fp32 or bf16 point tensors (the kernels are templated on the point type; a
+// bf16 value is its own exact hi part), and of the blocked family's bf16
+// shapes.
 //
 // Every product is formed on the tensor cores from an exact three-way bf16
 // split of each fp32 operand, x = hi + mid + lo (8 + 8 + 8 significant bits);

@@ -14,9 +14,10 @@ contract per sample:
 * every result equals the dense op applied to each sample alone.
 
 The tensor-core engine serves them in one launch per op (fp32 or bf16 point
-tensors, D = DV = G = 32, at most ``FS_MAX_SPLITS`` samples): each (sample, head) gets its CTAs and
-masks the rows past its sample. Other problems run the dense ops sample by
-sample (still native, one launch per sample)."""
+tensors, D = DV = 32, at most ``FS_MAX_SPLITS`` samples; G = 32, and G = 64
+for the tied round of ``ragged_coupling``): each (sample, head) gets its
+CTAs and masks the rows past its sample. Other problems run the dense ops
+sample by sample (still native, one launch per sample)."""
 
 import ctypes
 
