@@ -203,6 +203,14 @@ def profile_traffic(op, rows):
     return None
 
 
+# Each per-op timing rep starts on an idle GPU (a synchronize ends the last
+# one); a device-side sleep of about 2 ms enqueued before the first event
+# keeps the GPU busy while the host dispatches the first op, so that its
+# time, like the others', is device time and not the host's dispatch
+# latency.
+_HIDE_DISPATCH_CYCLES = 4_000_000
+
+
 def op_timings(K, x, fx, W, b, tau, r, dot, reps=3):
     """Per-op device time (ms) of one tied round, each op launched directly
     on the current stream between CUDA events; median over reps. The ops are
@@ -215,6 +223,7 @@ def op_timings(K, x, fx, W, b, tau, r, dot, reps=3):
     times = {k: [] for k in UNITS}
     for _ in range(reps):
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(7)]
+        torch.cuda._sleep(_HIDE_DISPATCH_CYCLES)
         ev[0].record()
         z, s = ops.flash_slice(xd, fd, Wd, bd, td, dot)
         ev[1].record()
@@ -250,6 +259,7 @@ def op_timings_blocked(x, fx, W, b, tau, r, dot, reps=3):
     times = {k: [] for k in BLK_FLOPS}
     for _ in range(reps):
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(8)]
+        torch.cuda._sleep(_HIDE_DISPATCH_CYCLES)
         ev[0].record()
         z, s, st = ops.slice_blk(xd, fd, Wd, bd, td, None, dot)
         ev[1].record()
